@@ -1,0 +1,1017 @@
+// bank.cpp — host logic of the lifelong KV cache (see bank.h).
+//
+// Reference map (nomas-core):
+//   Bank::Bank          HistoryCache::new        cache/history.rs:104-156
+//   Bank::validate      validate_segment         cache/history.rs:168-238
+//   Bank::commit        commit_segment           cache/history.rs:458-463
+//                       archive_segment          cache/history.rs:241-305
+//   Bank::plan_rebuild  rebuild                  cache/history.rs:341-446
+//   Bank::rollback      rollback_last_segment    cache/history.rs:507-528
+//   Bank::park/unpark   PhaseSwappedCache        cache/phase_swap.rs:42-81
+//   Bank::bank_metrics  KvBank::metrics          cache/mod.rs:305-319
+#include "bank.h"
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <thread>
+
+#include "nkv_qvg_fit.h"
+
+namespace nkv {
+
+void fail(int code, std::string msg) { throw Error{code, std::move(msg)}; }
+
+void check_cuda(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) fail(NKV_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+#define NKV_CUDA(expr) check_cuda((expr), #expr)
+
+static inline size_t align_up(size_t x, size_t a = 256) { return (x + a - 1) / a * a; }
+static inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// ------------------------------------------------------------ DeviceScope --
+DeviceScope::DeviceScope(int device) {
+  if (cudaGetDevice(&prev_) != cudaSuccess) prev_ = -1;
+  if (prev_ != device) {
+    NKV_CUDA(cudaSetDevice(device));
+    switched_ = true;
+  }
+}
+DeviceScope::~DeviceScope() {
+  if (switched_ && prev_ >= 0) cudaSetDevice(prev_);
+}
+
+// ----------------------------------------------------------- ArchiveArena --
+ArchiveArena::~ArchiveArena() { release(); }
+
+void ArchiveArena::release() {
+  for (auto& c : chunks_) cudaFree(c.base);
+  chunks_.clear();
+  stack_.clear();
+}
+
+size_t ArchiveArena::free_from_top() const {
+  size_t ci = stack_.empty() ? 0 : stack_.back().chunk;
+  size_t off = stack_.empty() ? 0 : stack_.back().off + stack_.back().size;
+  size_t free = 0;
+  for (size_t i = ci; i < chunks_.size(); ++i) free += chunks_[i].cap - (i == ci ? off : 0);
+  return free;
+}
+
+unsigned char* ArchiveArena::push(size_t bytes) {
+  bytes = align_up(std::max<size_t>(bytes, 1));
+  size_t ci = stack_.empty() ? 0 : stack_.back().chunk;
+  size_t off = stack_.empty() ? 0 : stack_.back().off + stack_.back().size;
+  while (ci < chunks_.size() && off + bytes > chunks_[ci].cap) {
+    ++ci;
+    off = 0;
+  }
+  if (ci == chunks_.size()) {
+    unsigned char* p = nullptr;
+    NKV_CUDA(cudaMalloc(&p, bytes));
+    chunks_.push_back({p, bytes});
+  }
+  stack_.push_back({ci, off, bytes});
+  return chunks_[ci].base + off;
+}
+
+void ArchiveArena::pop() {
+  if (!stack_.empty()) stack_.pop_back();
+}
+
+void ArchiveArena::reserve(size_t bytes) {
+  if (free_from_top() >= bytes) return;
+  unsigned char* p = nullptr;
+  NKV_CUDA(cudaMalloc(&p, align_up(bytes)));
+  chunks_.push_back({p, align_up(bytes)});
+}
+
+// ---------------------------------------------------------------- Staging --
+Staging::~Staging() { release(); }
+
+void Staging::release() {
+  if (done_) {
+    cudaEventSynchronize(done_);
+    cudaEventDestroy(done_);
+  }
+  if (host_) cudaFreeHost(host_);
+  if (dev_) cudaFree(dev_);
+  host_ = dev_ = nullptr;
+  done_ = nullptr;
+  cap_ = used_ = 0;
+}
+
+void Staging::begin() {
+  if (!done_) NKV_CUDA(cudaEventCreateWithFlags(&done_, cudaEventDisableTiming));
+  if (pending_) {
+    NKV_CUDA(cudaEventSynchronize(done_));
+    pending_ = false;
+  }
+  used_ = 0;
+}
+
+size_t Staging::add(const void* p, size_t bytes) {
+  size_t off = align_up(used_, 16);
+  if (off + bytes > cap_) {
+    size_t cap = std::max<size_t>(align_up(off + bytes, 4096) * 2, 64 * 1024);
+    unsigned char *h = nullptr, *d = nullptr;
+    NKV_CUDA(cudaHostAlloc(&h, cap, cudaHostAllocDefault));
+    if (cudaMalloc(&d, cap) != cudaSuccess) {
+      cudaFreeHost(h);
+      fail(NKV_ERR_CUDA, "staging: cudaMalloc failed");
+    }
+    if (used_) std::memcpy(h, host_, used_);
+    // the old device buffer may still be read by kernels in flight
+    if (dev_) cudaDeviceSynchronize();
+    if (host_) cudaFreeHost(host_);
+    if (dev_) cudaFree(dev_);
+    host_ = h, dev_ = d, cap_ = cap;
+  }
+  if (bytes) std::memcpy(host_ + off, p, bytes);
+  used_ = off + bytes;
+  return off;
+}
+
+void Staging::upload(cudaStream_t s) {
+  if (used_ == 0) return;
+  NKV_CUDA(cudaMemcpyAsync(dev_, host_, used_, cudaMemcpyHostToDevice, s));
+  NKV_CUDA(cudaEventRecord(done_, s));
+  pending_ = true;
+}
+
+// ------------------------------------------------------------------- Bank --
+static void validate_config(const nkv_cache_config& c, int n_layers, int64_t batch, int64_t heads, int64_t head_dim,
+                            int dtype) {
+  // history.rs:112-134, in the reference's order
+  if (c.storage < NKV_STORAGE_FLOAT || c.storage > NKV_STORAGE_QVG)
+    fail(NKV_ERR_INVALID_CONFIG, "unknown cache storage " + std::to_string(c.storage));
+  if (c.sampling < NKV_SAMPLING_RECENT || c.sampling > NKV_SAMPLING_TEMPORAL)
+    fail(NKV_ERR_INVALID_CONFIG, "unknown history sampling " + std::to_string(c.sampling));
+  if (c.storage == NKV_STORAGE_QVG) {
+    if (batch != 1)
+      fail(NKV_ERR_INVALID_CONFIG, "QVG storage requires batch=1 (interactive world-model sessions)");
+    if (c.qvg.bits_per_stage <= 0 || c.qvg.bits_per_stage > 8 || c.qvg.stages <= 0)
+      fail(NKV_ERR_INVALID_CONFIG, "invalid QVG stages/bits");
+  }
+  if (c.sampling == NKV_SAMPLING_TEMPORAL && (!std::isfinite(c.gamma) || c.gamma <= 0.0))
+    fail(NKV_ERR_INVALID_CONFIG, "invalid temporal_context gamma " + rust_f64(c.gamma));
+  if (c.has_capacity && c.capacity == 0) fail(NKV_ERR_INVALID_CONFIG, "cache capacity must be > 0");
+  if (c.past_frames == 0) fail(NKV_ERR_INVALID_CONFIG, "past_frames must be > 0");
+  // Checks with no reference counterpart (the reference would panic or build
+  // degenerate tensors): positive geometry, a known dtype, and QVG shapes the
+  // device encoder can hold.
+  if (n_layers < 1) fail(NKV_ERR_INVALID_CONFIG, "n_layers must be >= 1");
+  if (batch < 1 || heads < 1 || head_dim < 1) fail(NKV_ERR_INVALID_CONFIG, "batch, heads and head_dim must be >= 1");
+  if (dtype < NKV_F32 || dtype > NKV_F16) fail(NKV_ERR_INVALID_CONFIG, "unknown model dtype");
+  if (c.storage == NKV_STORAGE_QVG) {
+    if (c.qvg.block_size <= 0) fail(NKV_ERR_INVALID_CONFIG, "QVG block_size must be > 0");
+    if (int64_t(c.qvg.stages) * c.qvg.bits_per_stage > 64)
+      fail(NKV_ERR_INVALID_CONFIG, "QVG stages * bits_per_stage must be <= 64");
+    if (qvg_encode_smem_bytes(int(head_dim), c.qvg.block_size, c.qvg.bits_per_stage) > 200 * 1024)
+      fail(NKV_ERR_INVALID_CONFIG, "QVG block_size x head_dim too large for the device encoder");
+  }
+}
+
+Bank::Bank(const nkv_cache_config& cfg, int n_layers, int layer_begin, int64_t batch, int64_t heads, int64_t head_dim,
+           int dtype, int device, cudaStream_t stream)
+    : cfg_(cfg),
+      n_layers_(n_layers),
+      layer_begin_(layer_begin),
+      B_(batch),
+      H_(heads),
+      D_(head_dim),
+      dtype_(dtype),
+      device_(device),
+      stream_(stream) {
+  validate_config(cfg, n_layers, batch, heads, head_dim, dtype);
+  if (cfg.storage == NKV_STORAGE_QVG) {
+    q_stages_ = cfg.qvg.stages, q_bits_ = cfg.qvg.bits_per_stage, q_block_ = cfg.qvg.block_size;
+    q_E_ = 1 << q_bits_;
+    q_bpt_ = (q_stages_ * q_bits_ + 7) / 8;
+  }
+  int n_dev = 0;
+  if (cudaGetDeviceCount(&n_dev) != cudaSuccess || n_dev == 0)
+    fail(NKV_ERR_CUDA, "no CUDA device: the cache has no CPU fallback");
+  if (device < 0 || device >= n_dev) fail(NKV_ERR_ARGUMENT, "device " + std::to_string(device) + " out of range");
+  DeviceScope ds(device_);
+  NKV_CUDA(cudaStreamCreateWithFlags(&side_, cudaStreamNonBlocking));
+  NKV_CUDA(cudaMalloc(&d_flag_, sizeof(uint32_t)));
+  NKV_CUDA(cudaHostAlloc(&h_flag_, sizeof(uint32_t), cudaHostAllocDefault));
+  *h_flag_ = 0;
+  if (cfg.storage == NKV_STORAGE_QVG) {
+    cb_layer_ = size_t(2) * H_ * q_stages_ * q_E_ * D_;
+    NKV_CUDA(cudaMalloc(&cb_dev_, cb_layer_ * n_layers_ * sizeof(float)));
+    cb_host_.assign(cb_layer_ * n_layers_, 0.0f);
+    fitted_.assign(n_layers_, 0);
+  }
+  p_host_.assign(n_layers_, nullptr);
+  p_host_cap_.assign(n_layers_, 0);
+}
+
+Bank::~Bank() {
+  cudaSetDevice(device_);
+  if (stream_) cudaStreamSynchronize(stream_);
+  if (side_) {
+    cudaStreamSynchronize(side_);
+    cudaStreamDestroy(side_);
+  }
+  for (auto& p : pending_) {
+    cudaEventDestroy(p.a);
+    cudaEventDestroy(p.b);
+  }
+  for (auto e : ev_pool_) cudaEventDestroy(e);
+  if (cur_a_) cudaEventDestroy(cur_a_);
+  if (ws_) cudaFree(ws_);
+  if (cb_dev_) cudaFree(cb_dev_);
+  if (d_flag_) cudaFree(d_flag_);
+  if (h_flag_) cudaFreeHost(h_flag_);
+  for (auto p : p_host_)
+    if (p) cudaFreeHost(p);
+  stg_.release();
+  arena_.release();
+}
+
+// Archive slab geometry of one segment (ArchivedPayload, history.rs:25-37).
+Rec Bank::make_rec(const nkv_segment_desc& s) const {
+  Rec r;
+  r.desc = s;
+  const size_t L = s.image_tokens + s.text_tokens, HD = size_t(H_) * D_, B = size_t(B_);
+  size_t o = 0;
+  auto put = [&](size_t bytes) {
+    size_t at = o;
+    o += align_up(bytes);
+    return at;
+  };
+  if (cfg_.storage == NKV_STORAGE_FLOAT) {
+    const size_t n = B * L * HD * dtype_size(dtype_);
+    r.off[0] = put(n), r.off[1] = put(n);
+    r.nbytes = 2 * n;
+  } else if (cfg_.storage == NKV_STORAGE_INT8) {
+    r.off[0] = put(B * L * HD), r.off[1] = put(B * L * HD);
+    r.off[2] = put(B * L * H_ * 4), r.off[3] = put(B * L * H_ * 4);
+    r.nbytes = 2 * B * L * HD + 2 * B * L * H_ * 4;  // Int8KvBlock::nbytes (int8.rs:56-61)
+  } else {
+    const size_t Lv = s.image_tokens, Lt = s.text_tokens;
+    r.n_blocks = (Lv + q_block_ - 1) / q_block_;
+    r.off[0] = put(Lv * H_ * q_bpt_), r.off[1] = put(Lv * H_ * q_bpt_);
+    r.off[2] = put(size_t(H_) * r.n_blocks * q_stages_ * 4), r.off[3] = put(size_t(H_) * r.n_blocks * q_stages_ * 4);
+    // QvgPayload::nbytes (qvg.rs:81-83) for k and v
+    r.nbytes = 2 * (Lv * H_ * q_bpt_ + size_t(H_) * r.n_blocks * q_stages_ * 4);
+    if (Lt > 0) {
+      r.off[4] = put(Lt * HD), r.off[5] = put(Lt * HD);
+      r.off[6] = put(Lt * H_ * 4), r.off[7] = put(Lt * H_ * 4);
+      r.nbytes += 2 * Lt * HD + 2 * Lt * H_ * 4;
+    }
+  }
+  r.layer_stride = std::max<size_t>(align_up(o), 256);
+  return r;
+}
+
+uint64_t Bank::segment_bytes(const nkv_segment_desc& s) const { return make_rec(s).layer_stride; }
+
+// validate_segment (history.rs:168-238).  Like the reference it records
+// tokens_per_frame from the first segment before the later checks run.
+void Bank::validate(const nkv_segment_desc& s, int kv_dtype, const void* const* k, const void* const* v) {
+  if (s.frame_count == 0 || s.image_tokens == 0) fail(NKV_ERR_GEOMETRY, "segment must contain at least one frame");
+  const uint64_t tpf = s.image_tokens / s.frame_count;
+  if (s.image_tokens % s.frame_count != 0 || tpf == 0)
+    fail(NKV_ERR_GEOMETRY, "image_tokens " + std::to_string(s.image_tokens) + " not divisible by frame_count " +
+                               std::to_string(s.frame_count));
+  if (tpf_ == 0)
+    tpf_ = tpf;
+  else if (tpf_ != tpf)
+    fail(NKV_ERR_GEOMETRY,
+         "tokens_per_frame changed mid-session: " + std::to_string(tpf_) + " -> " + std::to_string(tpf));
+  if (!archive_.empty()) {
+    if (s.segment_index <= archive_.back().desc.segment_index)
+      fail(NKV_ERR_CACHE_STATE, "history requires one chronological write per segment");
+    if (s.frame_start != total_frames_)
+      fail(NKV_ERR_GEOMETRY, "segment frame_start " + std::to_string(s.frame_start) +
+                                 " does not continue the timeline at " + std::to_string(total_frames_));
+  } else if (s.frame_start != 0 && total_frames_ == 0) {
+    fail(NKV_ERR_GEOMETRY, "first segment must start at frame 0, got " + std::to_string(s.frame_start));
+  }
+  if (s.action_start < -1 || s.action_start > int64_t(s.text_tokens))
+    fail(NKV_ERR_GEOMETRY, "action_start " + std::to_string(s.action_start) + " outside text block of " +
+                               std::to_string(s.text_tokens));
+  if (kv_dtype < NKV_F32 || kv_dtype > NKV_F16) fail(NKV_ERR_GEOMETRY, "segment k must be float");
+  // "segment KV must live on the cache device" (history.rs:232-236)
+  for (int i = 0; i < n_layers_; ++i)
+    for (int side = 0; side < 2; ++side) {
+      const void* p = side ? v[i] : k[i];
+      cudaPointerAttributes at{};
+      if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+        cudaGetLastError();
+        fail(NKV_ERR_GEOMETRY, "segment KV must live on the cache device");
+      }
+      const bool on_dev = (at.type == cudaMemoryTypeDevice && at.device == device_) || at.type == cudaMemoryTypeManaged;
+      if (!on_dev) fail(NKV_ERR_GEOMETRY, "segment KV must live on the cache device");
+    }
+}
+
+// rebuild (history.rs:341-446), host half: which frames of which archived
+// segments the working set holds, as contiguous token runs, plus the layout.
+// Recent mode adds its evicted tokens to the counters before the capacity
+// check, exactly like the reference.
+Plan Bank::plan_rebuild() {
+  const uint64_t tpf = std::max<uint64_t>(tpf_, 1);
+  std::vector<std::pair<size_t, std::vector<uint64_t>>> selection;
+  if (cfg_.sampling == NKV_SAMPLING_RECENT) {
+    std::vector<DenseRecord> recs;
+    recs.reserve(archive_.size());
+    for (const auto& a : archive_)
+      recs.push_back({a.desc.segment_index, a.desc.frame_start, a.desc.frame_count, a.desc.image_tokens,
+                      a.desc.text_tokens});
+    TrimPlan plan = plan_recent_trim(recs, capacity_or_max(), tpf);
+    m_.evicted_tokens += plan.evicted_tokens;
+    for (const auto& r : apply_trim(recs, plan, tpf)) {
+      size_t idx = 0;
+      for (size_t i = 0; i < archive_.size(); ++i)
+        if (archive_[i].desc.segment_index == r.segment_index) {
+          idx = i;
+          break;
+        }
+      // The reference keeps frames 0..kept of the segment (its oldest
+      // frames) after a partial trim (history.rs:350-358).
+      std::vector<uint64_t> frames(r.frame_count);
+      for (uint64_t f = 0; f < r.frame_count; ++f) frames[f] = f;
+      selection.push_back({idx, std::move(frames)});
+    }
+  } else {
+    std::vector<uint64_t> ids;
+    try {
+      ids = history_frame_indices(total_frames_, cfg_.past_frames, cfg_.sampling, cfg_.gamma);
+    } catch (const PolicyError& e) {
+      fail(e.code, e.msg);
+    }
+    size_t j = 0;  // ids are strictly increasing and archives are chronological
+    for (size_t idx = 0; idx < archive_.size(); ++idx) {
+      const auto& a = archive_[idx].desc;
+      std::vector<uint64_t> sel;
+      while (j < ids.size() && ids[j] < a.frame_start) ++j;
+      for (size_t t = j; t < ids.size() && ids[t] < a.frame_start + a.frame_count; ++t)
+        sel.push_back(ids[t] - a.frame_start);
+      if (!sel.empty()) selection.push_back({idx, std::move(sel)});
+    }
+  }
+  Plan p;
+  uint64_t cursor = 0;
+  for (const auto& [idx, sel] : selection) {
+    const auto& a = archive_[idx].desc;
+    const uint64_t video_end = cursor + sel.size() * tpf;
+    const uint64_t text_end = video_end + a.text_tokens;
+    p.layout.push_back({a.segment_index, cursor, video_end, video_end, text_end, a.action_start});
+    // consecutive frames merge into one run
+    uint64_t dst = cursor;
+    for (size_t i = 0; i < sel.size();) {
+      size_t j2 = i + 1;
+      while (j2 < sel.size() && sel[j2] == sel[j2 - 1] + 1) ++j2;
+      const int64_t n = int64_t((j2 - i) * tpf);
+      p.runs.push_back({idx, false, int64_t(sel[i] * tpf), int64_t(dst), n});
+      dst += uint64_t(n);
+      i = j2;
+    }
+    if (a.text_tokens > 0)
+      p.runs.push_back({idx, cfg_.storage == NKV_STORAGE_QVG, int64_t(a.image_tokens), int64_t(video_end),
+                        int64_t(a.text_tokens)});
+    cursor = text_end;
+  }
+  if (cursor > capacity_or_max())
+    fail(NKV_ERR_GEOMETRY,
+         "history needs " + std::to_string(cursor) + " tokens; capacity is " + std::to_string(capacity_or_max()));
+  p.valid = cursor;
+  return p;
+}
+
+// Device run/tile tables for a plan, appended to the staging area.
+void Bank::add_runs(const Plan& plan, size_t& runs_off, size_t& tiles_off, int& n_tiles, bool& aligned) {
+  constexpr int64_t kTile = 32;
+  std::vector<GatherRun> runs;
+  std::vector<GatherTile> tiles;
+  runs.reserve(plan.runs.size());
+  for (const auto& rs : plan.runs) {
+    const Rec& r = archive_[rs.rec];
+    GatherRun g{};
+    g.src = r.slab;
+    g.layer_stride = int64_t(r.layer_stride);
+    g.src_tok = rs.src_tok;
+    g.dst_tok = rs.dst_tok;
+    g.ntok = rs.ntok;
+    g.n_blocks = int32_t(r.n_blocks);
+    const int64_t L = int64_t(r.desc.image_tokens + r.desc.text_tokens);
+    if (cfg_.storage == NKV_STORAGE_FLOAT) {
+      g.kind = RUN_FLOAT, g.src_L = L;
+      g.off[0] = int64_t(r.off[0]), g.off[1] = int64_t(r.off[1]);
+    } else if (cfg_.storage == NKV_STORAGE_INT8) {
+      g.kind = RUN_INT8, g.src_L = L;
+      for (int i = 0; i < 4; ++i) g.off[i] = int64_t(r.off[i]);
+    } else if (!rs.text) {
+      g.kind = RUN_QVG_VIDEO, g.src_L = int64_t(r.desc.image_tokens);
+      for (int i = 0; i < 4; ++i) g.off[i] = int64_t(r.off[i]);
+    } else {
+      g.kind = RUN_INT8, g.src_L = int64_t(r.desc.text_tokens);
+      g.src_tok = rs.src_tok - int64_t(r.desc.image_tokens);
+      for (int i = 0; i < 4; ++i) g.off[i] = int64_t(r.off[4 + i]);
+    }
+    const int32_t run_id = int32_t(runs.size());
+    runs.push_back(g);
+    for (int64_t b = 0; b < B_; ++b)
+      for (int64_t t0 = 0; t0 < rs.ntok; t0 += kTile)
+        tiles.push_back({run_id, int32_t(b), int32_t(t0), int32_t(std::min<int64_t>(kTile, rs.ntok - t0))});
+  }
+  aligned = true;  // slabs, components and working-set planes are 256-byte aligned
+  runs_off = stg_.add(runs.data(), runs.size() * sizeof(GatherRun));
+  tiles_off = stg_.add(tiles.data(), tiles.size() * sizeof(GatherTile));
+  n_tiles = int(tiles.size());
+}
+
+void Bank::launch_gather_into(size_t runs_off, size_t tiles_off, int n_tiles, size_t outk_off, size_t outv_off,
+                              uint64_t out_L, bool vector_ok, const uint32_t* abort_flag) {
+  if (n_tiles == 0) return;
+  GatherArgs a{};
+  a.runs = static_cast<const GatherRun*>(stg_.dev(runs_off));
+  a.tiles = static_cast<const GatherTile*>(stg_.dev(tiles_off));
+  a.n_tiles = n_tiles;
+  a.n_layers = n_layers_;
+  a.out_k = static_cast<void* const*>(stg_.dev(outk_off));
+  a.out_v = static_cast<void* const*>(stg_.dev(outv_off));
+  a.out_L = int64_t(out_L);
+  a.H = int32_t(H_), a.D = int32_t(D_);
+  a.out_dtype = dtype_;
+  a.cb = cb_dev_;
+  a.cb_layer_stride = int64_t(cb_layer_);
+  a.stages = q_stages_, a.bits = q_bits_, a.block = q_block_;
+  a.abort_flag = abort_flag;
+  const bool hd_ok = ((H_ * D_) % 16) == 0;
+  tbegin(NKV_KERNEL_GATHER);
+  NKV_CUDA(launch_gather(a, vector_ok && hd_ok, stream_));
+  tend(NKV_KERNEL_GATHER);
+}
+
+size_t Bank::ws_plane_bytes(uint64_t cap) const { return align_up(size_t(B_) * cap * H_ * D_ * dtype_size(dtype_)); }
+
+unsigned char* Bank::ws_plane(unsigned char* base, uint64_t cap, int layer, int side) const {
+  return base + (size_t(2) * layer + side) * ws_plane_bytes(cap);
+}
+
+// Working-set storage for `tokens` tokens per layer: *fresh is a new buffer
+// (installed by the caller once the commit is known good) or null when the
+// current one is big enough.
+void Bank::ensure_ws(uint64_t tokens, unsigned char** fresh, uint64_t* fresh_cap) {
+  *fresh = nullptr;
+  *fresh_cap = 0;
+  if (ws_ && tokens <= ws_cap_) return;
+  if (tokens == 0) return;
+  uint64_t cap = std::max<uint64_t>(tokens, ws_cap_ + ws_cap_ / 4);
+  unsigned char* p = nullptr;
+  NKV_CUDA(cudaMalloc(&p, size_t(2) * n_layers_ * ws_plane_bytes(cap)));
+  *fresh = p;
+  *fresh_cap = cap;
+}
+
+void Bank::fit_qvg(const nkv_segment_desc& s, int kv_dtype, const void* const* k, const void* const* v) {
+  const size_t L = s.image_tokens + s.text_tokens, n = L * H_ * D_;
+  const size_t esz = dtype_size(kv_dtype);
+  std::vector<unsigned char> raw(n * esz);
+  std::vector<float> kf(n), vf(n);
+  auto to_f32 = [&](std::vector<float>& dst) {
+    if (kv_dtype == NKV_F32) {
+      std::memcpy(dst.data(), raw.data(), n * 4);
+      return;
+    }
+    const uint16_t* h = reinterpret_cast<const uint16_t*>(raw.data());
+    for (size_t i = 0; i < n; ++i) {
+      uint32_t b = h[i];
+      uint32_t u;
+      if (kv_dtype == NKV_BF16) {
+        if ((b & 0x7FFFu) > 0x7F80u) b |= 0x40u;
+        u = b << 16;
+      } else {  // IEEE binary16, exact
+        const uint32_t sign = (b & 0x8000u) << 16, e = (b >> 10) & 0x1Fu, m = b & 0x3FFu;
+        if (e == 0x1F) u = sign | 0x7F800000u | (m ? (0x00400000u | (m << 13)) : 0u);
+        else if (e == 0) {
+          float f = float(m) * 5.9604644775390625e-8f;  // m * 2^-24, exact
+          std::memcpy(&u, &f, 4);
+          u |= sign;
+        } else u = sign | ((e + 112u) << 23) | (m << 13);
+      }
+      std::memcpy(&dst[i], &u, 4);
+    }
+  };
+  const int threads = std::max(1u, std::thread::hardware_concurrency());
+  for (int i = 0; i < n_layers_; ++i) {
+    if (fitted_[i]) continue;
+    NKV_CUDA(cudaMemcpyAsync(raw.data(), k[i], n * esz, cudaMemcpyDeviceToHost, stream_));
+    NKV_CUDA(cudaStreamSynchronize(stream_));
+    to_f32(kf);
+    NKV_CUDA(cudaMemcpyAsync(raw.data(), v[i], n * esz, cudaMemcpyDeviceToHost, stream_));
+    NKV_CUDA(cudaStreamSynchronize(stream_));
+    to_f32(vf);
+    float* out = cb_host_.data() + cb_layer_ * i;
+    qvg_fit_layer(kf.data(), vf.data(), L, H_, D_, q_stages_, q_E_, cfg_.qvg.codebook_seed, out, threads);
+    NKV_CUDA(cudaMemcpyAsync(cb_dev_ + cb_layer_ * i, out, cb_layer_ * 4, cudaMemcpyHostToDevice, stream_));
+    NKV_CUDA(cudaStreamSynchronize(stream_));
+    fitted_[i] = 1;
+  }
+}
+
+// commit_segment (history.rs:458-463).
+void Bank::commit(const nkv_segment_desc& s, int kv_dtype, const void* const* k, const void* const* v) {
+  if (!k || !v) fail(NKV_ERR_ARGUMENT, "null K/V pointer array");
+  for (int i = 0; i < n_layers_; ++i)
+    if (!k[i] || !v[i]) fail(NKV_ERR_ARGUMENT, "null K/V pointer for layer " + std::to_string(i));
+  DeviceScope ds(device_);
+  validate(s, kv_dtype, k, v);
+
+  // ---- archive_segment: slab + device encode into it
+  Rec r = make_rec(s);
+  r.slab = arena_.push(r.layer_stride * n_layers_);
+  const nkv_metrics saved = m_;
+  const uint64_t L = s.image_tokens + s.text_tokens;
+  bool pushed = false;
+  unsigned char* fresh = nullptr;
+  uint64_t fresh_cap = 0;
+  try {
+    if (cfg_.storage == NKV_STORAGE_QVG) fit_qvg(s, kv_dtype, k, v);  // first commit only (history.rs:256-262)
+
+    archive_.push_back(r);
+    pushed = true;
+    total_frames_ += s.frame_count;
+    m_.encode_calls += cfg_.storage == NKV_STORAGE_FLOAT ? 0 : 1;
+    m_.archived_segments += 1;
+    m_.archived_bytes += r.nbytes;
+    m_.d2h_bytes += r.nbytes;
+
+    // ---- rebuild plan on the new archive
+    Plan plan;
+    bool plan_ok = true;
+    Error plan_err{0, ""};
+    try {
+      plan = plan_rebuild();
+    } catch (const Error& e) {
+      plan_ok = false;
+      plan_err = e;
+    }
+
+    stg_.begin();
+    bool in_aligned = true;
+    for (int i = 0; i < n_layers_; ++i) in_aligned &= aligned16(k[i]) && aligned16(v[i]);
+    size_t jobs_off = 0, text_jobs_off = 0;
+    if (cfg_.storage == NKV_STORAGE_FLOAT) {
+      std::vector<ConvertJob> jobs;
+      for (int i = 0; i < n_layers_; ++i) {
+        unsigned char* lb = r.slab + size_t(i) * r.layer_stride;
+        jobs.push_back({k[i], lb + r.off[0]});
+        jobs.push_back({v[i], lb + r.off[1]});
+      }
+      jobs_off = stg_.add(jobs.data(), jobs.size() * sizeof(ConvertJob));
+    } else if (cfg_.storage == NKV_STORAGE_INT8) {
+      std::vector<QuantJob> jobs;
+      for (int i = 0; i < n_layers_; ++i) {
+        unsigned char* lb = r.slab + size_t(i) * r.layer_stride;
+        jobs.push_back({k[i], v[i], lb + r.off[0], lb + r.off[1], reinterpret_cast<float*>(lb + r.off[2]),
+                        reinterpret_cast<float*>(lb + r.off[3])});
+      }
+      jobs_off = stg_.add(jobs.data(), jobs.size() * sizeof(QuantJob));
+    } else {
+      std::vector<QvgEncodeJob> jobs;
+      std::vector<QuantJob> tj;
+      for (int i = 0; i < n_layers_; ++i) {
+        unsigned char* lb = r.slab + size_t(i) * r.layer_stride;
+        const float* cb = cb_dev_ + cb_layer_ * i;
+        jobs.push_back({k[i], lb + r.off[0], reinterpret_cast<float*>(lb + r.off[2]), cb});
+        jobs.push_back({v[i], lb + r.off[1], reinterpret_cast<float*>(lb + r.off[3]), cb + cb_layer_ / 2});
+        tj.push_back({k[i], v[i], lb + r.off[4], lb + r.off[5], reinterpret_cast<float*>(lb + r.off[6]),
+                      reinterpret_cast<float*>(lb + r.off[7])});
+      }
+      jobs_off = stg_.add(jobs.data(), jobs.size() * sizeof(QvgEncodeJob));
+      text_jobs_off = stg_.add(tj.data(), tj.size() * sizeof(QuantJob));
+    }
+
+    size_t runs_off = 0, tiles_off = 0, outk_off = 0, outv_off = 0;
+    int n_tiles = 0;
+    bool runs_aligned = true;
+    if (plan_ok && plan.valid > 0) {
+      ensure_ws(plan.valid, &fresh, &fresh_cap);
+      unsigned char* base = fresh ? fresh : ws_;
+      const uint64_t cap = fresh ? fresh_cap : ws_cap_;
+      add_runs(plan, runs_off, tiles_off, n_tiles, runs_aligned);
+      std::vector<void*> ok(n_layers_), ov(n_layers_);
+      for (int i = 0; i < n_layers_; ++i) ok[i] = ws_plane(base, cap, i, 0), ov[i] = ws_plane(base, cap, i, 1);
+      outk_off = stg_.add(ok.data(), ok.size() * sizeof(void*));
+      outv_off = stg_.add(ov.data(), ov.size() * sizeof(void*));
+    }
+    stg_.upload(stream_);
+
+    NKV_CUDA(cudaMemsetAsync(d_flag_, 0, sizeof(uint32_t), stream_));
+    if (cfg_.storage == NKV_STORAGE_FLOAT) {
+      tbegin(NKV_KERNEL_FLOAT_ARCHIVE);
+      NKV_CUDA(launch_convert(static_cast<const ConvertJob*>(stg_.dev(jobs_off)), 2 * n_layers_,
+                              uint64_t(B_) * L * H_ * D_, kv_dtype, dtype_, stream_));
+      tend(NKV_KERNEL_FLOAT_ARCHIVE);
+    } else if (cfg_.storage == NKV_STORAGE_INT8) {
+      tbegin(NKV_KERNEL_QUANTIZE);
+      NKV_CUDA(launch_int8_quantize(static_cast<const QuantJob*>(stg_.dev(jobs_off)), n_layers_,
+                                    uint64_t(B_) * L * H_, 0, D_, kv_dtype, in_aligned, d_flag_, stream_));
+      tend(NKV_KERNEL_QUANTIZE);
+    } else {
+      tbegin(NKV_KERNEL_QVG_ENCODE);
+      NKV_CUDA(launch_qvg_encode(static_cast<const QvgEncodeJob*>(stg_.dev(jobs_off)), 2 * n_layers_, kv_dtype, L,
+                                 int(H_), int(D_), s.image_tokens, q_stages_, q_bits_, q_block_, stream_));
+      tend(NKV_KERNEL_QVG_ENCODE);
+      if (s.text_tokens > 0) {
+        tbegin(NKV_KERNEL_QUANTIZE);
+        NKV_CUDA(launch_int8_quantize(static_cast<const QuantJob*>(stg_.dev(text_jobs_off)), n_layers_,
+                                      s.text_tokens * H_, s.image_tokens * H_, D_, kv_dtype, in_aligned, d_flag_,
+                                      stream_));
+        tend(NKV_KERNEL_QUANTIZE);
+      }
+    }
+    if (n_tiles > 0) launch_gather_into(runs_off, tiles_off, n_tiles, outk_off, outv_off, plan.valid, runs_aligned, d_flag_);
+    NKV_CUDA(cudaMemcpyAsync(h_flag_, d_flag_, sizeof(uint32_t), cudaMemcpyDeviceToHost, stream_));
+    NKV_CUDA(cudaStreamSynchronize(stream_));
+    collect_timing(false);
+
+    if (*h_flag_ != 0) {
+      // quantize_kv_pair rejected the segment (int8.rs:99-117): nothing was
+      // archived and the working set was left untouched by the gather.
+      const bool k_bad = (*h_flag_ & 1u) != 0;
+      archive_.pop_back();
+      pushed = false;
+      total_frames_ -= s.frame_count;
+      m_ = saved;
+      arena_.pop();
+      if (fresh) cudaFree(fresh);
+      fresh = nullptr;
+      fail(NKV_ERR_MSG, std::string("cannot quantize non-finite ") + (k_bad ? "k" : "v") + " values");
+    }
+    if (!plan_ok) {
+      // like the reference, the segment stays archived when rebuild fails
+      if (fresh) cudaFree(fresh);
+      fresh = nullptr;
+      throw plan_err;
+    }
+    if (fresh) {
+      if (ws_) cudaFree(ws_);
+      ws_ = fresh, ws_cap_ = fresh_cap;
+      fresh = nullptr;
+    }
+    layout_ = std::move(plan.layout);
+    valid_ = plan.valid;
+    m_.h2d_bytes += valid_ * B_ * H_ * D_ * dtype_size(dtype_) * 2;  // history.rs:438-439
+    m_.rebuilds += 1;
+  } catch (const Error& e) {
+    if (fresh) cudaFree(fresh);
+    if (pushed && (e.code == NKV_ERR_CUDA || e.code == NKV_ERR_ARGUMENT)) {
+      archive_.pop_back();
+      total_frames_ -= s.frame_count;
+      m_ = saved;
+      arena_.pop();
+    } else if (!pushed && e.code != NKV_ERR_MSG) {
+      arena_.pop();
+    }
+    throw;
+  }
+}
+
+// rebuild() for rollback: plan, gather into the working set, counters.
+void Bank::rebuild_now() {
+  Plan plan = plan_rebuild();
+  unsigned char* fresh = nullptr;
+  uint64_t fresh_cap = 0;
+  if (plan.valid > 0) {
+    ensure_ws(plan.valid, &fresh, &fresh_cap);
+    stg_.begin();
+    size_t runs_off, tiles_off;
+    int n_tiles;
+    bool aligned;
+    add_runs(plan, runs_off, tiles_off, n_tiles, aligned);
+    unsigned char* base = fresh ? fresh : ws_;
+    const uint64_t cap = fresh ? fresh_cap : ws_cap_;
+    std::vector<void*> ok(n_layers_), ov(n_layers_);
+    for (int i = 0; i < n_layers_; ++i) ok[i] = ws_plane(base, cap, i, 0), ov[i] = ws_plane(base, cap, i, 1);
+    const size_t outk_off = stg_.add(ok.data(), ok.size() * sizeof(void*));
+    const size_t outv_off = stg_.add(ov.data(), ov.size() * sizeof(void*));
+    stg_.upload(stream_);
+    try {
+      launch_gather_into(runs_off, tiles_off, n_tiles, outk_off, outv_off, plan.valid, aligned, nullptr);
+    } catch (...) {
+      if (fresh) cudaFree(fresh);
+      throw;
+    }
+    if (fresh) {
+      if (ws_) {
+        NKV_CUDA(cudaStreamSynchronize(stream_));
+        cudaFree(ws_);
+      }
+      ws_ = fresh, ws_cap_ = fresh_cap;
+    }
+  }
+  layout_ = std::move(plan.layout);
+  valid_ = plan.valid;
+  m_.h2d_bytes += valid_ * B_ * H_ * D_ * dtype_size(dtype_) * 2;
+  m_.rebuilds += 1;
+}
+
+// rollback_last_segment (history.rs:507-528).
+void Bank::rollback() {
+  if (cfg_.sampling == NKV_SAMPLING_RECENT)
+    fail(NKV_ERR_CACHE_STATE, "recent-mode SWA does not support streaming rollback (use an archived sampling)");
+  if (archive_.empty()) fail(NKV_ERR_CACHE_STATE, "nothing to roll back");
+  DeviceScope ds(device_);
+  const Rec last = archive_.back();
+  archive_.pop_back();
+  arena_.pop();  // stream order keeps earlier readers of the slab ahead of its reuse
+  if (last.desc.frame_start + last.desc.frame_count != total_frames_)
+    fail(NKV_ERR_CACHE_STATE, "archive does not match the frame timeline");
+  total_frames_ -= last.desc.frame_count;
+  m_.archived_segments = m_.archived_segments > 0 ? m_.archived_segments - 1 : 0;
+  rebuild_now();
+  m_.rollbacks += 1;
+}
+
+// PhaseSwappedCache::park (phase_swap.rs:42-66): the working set goes to
+// pinned host memory and its device memory is released.
+void Bank::park() {
+  if (!cfg_.phase_swap || parked_) return;
+  DeviceScope ds(device_);
+  const size_t plane = size_t(B_) * valid_ * H_ * D_ * dtype_size(dtype_);
+  cudaEvent_t ready;
+  NKV_CUDA(cudaEventCreateWithFlags(&ready, cudaEventDisableTiming));
+  NKV_CUDA(cudaEventRecord(ready, stream_));
+  NKV_CUDA(cudaStreamWaitEvent(side_, ready, 0));
+  cudaEventDestroy(ready);
+  for (int i = 0; i < n_layers_; ++i) {
+    if (p_host_cap_[i] < 2 * plane) {
+      if (p_host_[i]) cudaFreeHost(p_host_[i]);
+      p_host_[i] = nullptr;
+      p_host_cap_[i] = 0;
+      NKV_CUDA(cudaHostAlloc(&p_host_[i], std::max<size_t>(2 * plane, 1), cudaHostAllocDefault));
+      p_host_cap_[i] = std::max<size_t>(2 * plane, 1);
+    }
+    if (plane) {
+      NKV_CUDA(cudaMemcpyAsync(p_host_[i], ws_plane(ws_, ws_cap_, i, 0), plane, cudaMemcpyDeviceToHost, side_));
+      NKV_CUDA(cudaMemcpyAsync(p_host_[i] + plane, ws_plane(ws_, ws_cap_, i, 1), plane, cudaMemcpyDeviceToHost, side_));
+    }
+  }
+  NKV_CUDA(cudaStreamSynchronize(side_));
+  if (ws_) cudaFree(ws_);
+  ws_ = nullptr, ws_cap_ = 0;
+  p_layout_ = layout_;
+  p_valid_ = valid_;
+  p_bytes_ = 2 * plane;
+  layout_.clear();  // release_working_set (history.rs:539-544)
+  valid_ = 0;
+  m_.d2h_bytes += p_bytes_;
+  parked_ = true;
+}
+
+// PhaseSwappedCache::unpark (phase_swap.rs:69-81).  Like the reference, a
+// working set rebuilt while parked is replaced by the parked one.
+void Bank::unpark() {
+  if (!cfg_.phase_swap || !parked_) return;
+  DeviceScope ds(device_);
+  const size_t plane = size_t(B_) * p_valid_ * H_ * D_ * dtype_size(dtype_);
+  if (p_valid_ > 0) {
+    unsigned char* fresh = nullptr;
+    uint64_t fresh_cap = 0;
+    ensure_ws(p_valid_, &fresh, &fresh_cap);
+    if (fresh) {
+      if (ws_) {
+        NKV_CUDA(cudaStreamSynchronize(stream_));
+        cudaFree(ws_);
+      }
+      ws_ = fresh, ws_cap_ = fresh_cap;
+    }
+    // order after any work still using the old contents of the buffer
+    cudaEvent_t ready, done;
+    NKV_CUDA(cudaEventCreateWithFlags(&ready, cudaEventDisableTiming));
+    NKV_CUDA(cudaEventCreateWithFlags(&done, cudaEventDisableTiming));
+    NKV_CUDA(cudaEventRecord(ready, stream_));
+    NKV_CUDA(cudaStreamWaitEvent(side_, ready, 0));
+    for (int i = 0; i < n_layers_; ++i) {
+      NKV_CUDA(cudaMemcpyAsync(ws_plane(ws_, ws_cap_, i, 0), p_host_[i], plane, cudaMemcpyHostToDevice, side_));
+      NKV_CUDA(cudaMemcpyAsync(ws_plane(ws_, ws_cap_, i, 1), p_host_[i] + plane, plane, cudaMemcpyHostToDevice, side_));
+    }
+    NKV_CUDA(cudaEventRecord(done, side_));
+    NKV_CUDA(cudaStreamWaitEvent(stream_, done, 0));
+    NKV_CUDA(cudaStreamSynchronize(side_));
+    cudaEventDestroy(ready);
+    cudaEventDestroy(done);
+  }
+  layout_ = p_layout_;
+  valid_ = p_valid_;
+  m_.h2d_bytes += p_bytes_;
+  parked_ = false;
+}
+
+// decode_segment (history.rs:308-338) of every local layer into caller buffers.
+void Bank::decode_segment(uint64_t pos, void* const* k_out, void* const* v_out) {
+  if (pos >= archive_.size()) fail(NKV_ERR_ARGUMENT, "archive position out of range");
+  if (!k_out || !v_out) fail(NKV_ERR_ARGUMENT, "null output pointer array");
+  for (int i = 0; i < n_layers_; ++i)
+    if (!k_out[i] || !v_out[i]) fail(NKV_ERR_ARGUMENT, "null output pointer for layer " + std::to_string(i));
+  DeviceScope ds(device_);
+  const Rec& r = archive_[pos];
+  Plan p;
+  const int64_t Lv = int64_t(r.desc.image_tokens), Lt = int64_t(r.desc.text_tokens);
+  if (cfg_.storage == NKV_STORAGE_QVG) {
+    p.runs.push_back({pos, false, 0, 0, Lv});
+    if (Lt > 0) p.runs.push_back({pos, true, Lv, Lv, Lt});
+  } else {
+    p.runs.push_back({pos, false, 0, 0, Lv + Lt});
+  }
+  p.valid = uint64_t(Lv + Lt);
+  stg_.begin();
+  size_t runs_off, tiles_off;
+  int n_tiles;
+  bool aligned;
+  add_runs(p, runs_off, tiles_off, n_tiles, aligned);
+  for (int i = 0; i < n_layers_; ++i) aligned &= aligned16(k_out[i]) && aligned16(v_out[i]);
+  const size_t outk_off = stg_.add(k_out, n_layers_ * sizeof(void*));
+  const size_t outv_off = stg_.add(v_out, n_layers_ * sizeof(void*));
+  stg_.upload(stream_);
+  launch_gather_into(runs_off, tiles_off, n_tiles, outk_off, outv_off, p.valid, aligned, nullptr);
+}
+
+void Bank::synchronize() {
+  DeviceScope ds(device_);
+  NKV_CUDA(cudaStreamSynchronize(stream_));
+  collect_timing(false);
+}
+
+void Bank::reserve(uint64_t archive_bytes, uint64_t working_tokens) {
+  DeviceScope ds(device_);
+  if (archive_bytes) arena_.reserve(archive_bytes);
+  if (working_tokens && !parked_) {
+    unsigned char* fresh = nullptr;
+    uint64_t cap = 0;
+    ensure_ws(working_tokens, &fresh, &cap);
+    if (fresh) {
+      // keep the current contents: the working set may be in use
+      if (ws_ && valid_ > 0) {
+        for (int i = 0; i < n_layers_; ++i)
+          for (int side = 0; side < 2; ++side)
+            NKV_CUDA(cudaMemcpyAsync(ws_plane(fresh, cap, i, side), ws_plane(ws_, ws_cap_, i, side),
+                                     size_t(B_) * valid_ * H_ * D_ * dtype_size(dtype_), cudaMemcpyDeviceToDevice,
+                                     stream_));
+      }
+      NKV_CUDA(cudaStreamSynchronize(stream_));
+      if (ws_) cudaFree(ws_);
+      ws_ = fresh, ws_cap_ = cap;
+    }
+  }
+}
+
+void Bank::working_set(int layer, const void** k, const void** v, uint64_t* valid) const {
+  if (layer < 0 || layer >= n_layers_) fail(NKV_ERR_ARGUMENT, "layer out of range");
+  if (parked_) fail(NKV_ERR_CACHE_STATE, "working set is parked; call unpark() before attention");
+  if (valid_ == 0 || !ws_) {
+    *k = *v = nullptr;
+    *valid = 0;
+    return;
+  }
+  *k = ws_plane(ws_, ws_cap_, layer, 0);
+  *v = ws_plane(ws_, ws_cap_, layer, 1);
+  *valid = valid_;
+}
+
+void Bank::info(int layer, nkv_cache_info_t* o) const {
+  if (layer < 0 || layer >= n_layers_) fail(NKV_ERR_ARGUMENT, "layer out of range");
+  o->valid_len = parked_ ? p_valid_ : valid_;
+  o->capacity = capacity_or_max();
+  o->n_segments = archive_.size();
+  o->total_frames = total_frames_;
+  o->tokens_per_frame = tpf_;
+  o->parked = parked_ ? 1 : 0;
+  o->storage = cfg_.storage;
+  o->sampling = cfg_.sampling;
+  o->qvg_fitted = cfg_.storage == NKV_STORAGE_QVG ? fitted_[layer] : 0;
+}
+
+// KvBank::metrics (cache/mod.rs:305-319).  Every layer holds the same
+// counters, so max-aggregates equal one layer's and sums are n_layers times.
+nkv_metrics Bank::bank_metrics() const {
+  nkv_metrics o = m_;
+  const uint64_t n = uint64_t(n_layers_);
+  o.archived_bytes *= n;
+  o.encode_calls *= n;
+  o.d2h_bytes *= n;
+  o.h2d_bytes *= n;
+  return o;
+}
+
+void Bank::set_codebooks(int layer, const float* host) {
+  if (cfg_.storage != NKV_STORAGE_QVG) fail(NKV_ERR_CACHE_STATE, "cache does not use QVG storage");
+  if (layer < 0 || layer >= n_layers_) fail(NKV_ERR_ARGUMENT, "layer out of range");
+  if (!host) fail(NKV_ERR_ARGUMENT, "null codebook pointer");
+  DeviceScope ds(device_);
+  float* dst = cb_host_.data() + cb_layer_ * layer;
+  std::memcpy(dst, host, cb_layer_ * sizeof(float));
+  NKV_CUDA(cudaMemcpyAsync(cb_dev_ + cb_layer_ * layer, dst, cb_layer_ * sizeof(float), cudaMemcpyHostToDevice,
+                           stream_));
+  NKV_CUDA(cudaStreamSynchronize(stream_));
+  fitted_[layer] = 1;
+}
+
+void Bank::get_codebooks(int layer, float* host, int32_t* fitted) const {
+  if (cfg_.storage != NKV_STORAGE_QVG) fail(NKV_ERR_CACHE_STATE, "cache does not use QVG storage");
+  if (layer < 0 || layer >= n_layers_) fail(NKV_ERR_ARGUMENT, "layer out of range");
+  *fitted = fitted_[layer];
+  if (fitted_[layer] && host) std::memcpy(host, cb_host_.data() + cb_layer_ * layer, cb_layer_ * sizeof(float));
+}
+
+uint64_t Bank::export_segment(int layer, uint64_t pos, void* host, uint64_t cap) {
+  if (layer < 0 || layer >= n_layers_) fail(NKV_ERR_ARGUMENT, "layer out of range");
+  if (pos >= archive_.size()) fail(NKV_ERR_ARGUMENT, "archive position out of range");
+  const Rec& r = archive_[pos];
+  const size_t L = r.desc.image_tokens + r.desc.text_tokens, HD = size_t(H_) * D_, B = size_t(B_);
+  std::vector<std::pair<size_t, size_t>> parts;  // (offset, bytes)
+  if (cfg_.storage == NKV_STORAGE_FLOAT) {
+    const size_t n = B * L * HD * dtype_size(dtype_);
+    parts = {{r.off[0], n}, {r.off[1], n}};
+  } else if (cfg_.storage == NKV_STORAGE_INT8) {
+    parts = {{r.off[0], B * L * HD}, {r.off[1], B * L * HD}, {r.off[2], B * L * H_ * 4}, {r.off[3], B * L * H_ * 4}};
+  } else {
+    const size_t Lv = r.desc.image_tokens, Lt = r.desc.text_tokens;
+    const size_t cb = Lv * H_ * q_bpt_, sb = size_t(H_) * r.n_blocks * q_stages_ * 4;
+    parts = {{r.off[0], cb}, {r.off[1], cb}, {r.off[2], sb}, {r.off[3], sb}};
+    if (Lt > 0) {
+      parts.push_back({r.off[4], Lt * HD});
+      parts.push_back({r.off[5], Lt * HD});
+      parts.push_back({r.off[6], Lt * H_ * 4});
+      parts.push_back({r.off[7], Lt * H_ * 4});
+    }
+  }
+  uint64_t total = 0;
+  for (auto& p : parts) total += p.second;
+  if (!host || cap < total) return total;
+  DeviceScope ds(device_);
+  NKV_CUDA(cudaStreamSynchronize(stream_));
+  unsigned char* out = static_cast<unsigned char*>(host);
+  const unsigned char* lb = r.slab + size_t(layer) * r.layer_stride;
+  for (auto& p : parts) {
+    NKV_CUDA(cudaMemcpy(out, lb + p.first, p.second, cudaMemcpyDeviceToHost));
+    out += p.second;
+  }
+  return total;
+}
+
+// ------------------------------------------------------------------ timing --
+void Bank::set_timing(bool on) { timing_ = on; }
+
+void Bank::tbegin(int) {
+  if (!timing_) return;
+  if (ev_pool_.empty()) {
+    cudaEvent_t e;
+    NKV_CUDA(cudaEventCreate(&e));
+    ev_pool_.push_back(e);
+  }
+  cur_a_ = ev_pool_.back();
+  ev_pool_.pop_back();
+  NKV_CUDA(cudaEventRecord(cur_a_, stream_));
+}
+
+void Bank::tend(int kind) {
+  if (!timing_ || !cur_a_) return;
+  cudaEvent_t b;
+  if (ev_pool_.empty()) {
+    NKV_CUDA(cudaEventCreate(&b));
+  } else {
+    b = ev_pool_.back();
+    ev_pool_.pop_back();
+  }
+  NKV_CUDA(cudaEventRecord(b, stream_));
+  pending_.push_back({kind, cur_a_, b});
+  cur_a_ = nullptr;
+}
+
+void Bank::collect_timing(bool wait) {
+  std::vector<Pending> keep;
+  for (auto& p : pending_) {
+    if (!wait && cudaEventQuery(p.b) != cudaSuccess) {
+      keep.push_back(p);
+      continue;
+    }
+    cudaEventSynchronize(p.b);
+    float ms = 0.0f;
+    if (cudaEventElapsedTime(&ms, p.a, p.b) == cudaSuccess) {
+      stats_[p.kind].launches += 1;
+      stats_[p.kind].total_ms += ms;
+    }
+    ev_pool_.push_back(p.a);
+    ev_pool_.push_back(p.b);
+  }
+  pending_.swap(keep);
+}
+
+void Bank::kernel_stats(nkv_kernel_stat* out, bool reset) {
+  DeviceScope ds(device_);
+  collect_timing(true);
+  for (int i = 0; i < NKV_KERNEL_COUNT; ++i) out[i] = stats_[i];
+  if (reset)
+    for (auto& s : stats_) s = nkv_kernel_stat{0, 0.0};
+}
+
+}  // namespace nkv

@@ -1,0 +1,200 @@
+// bank.h — host-side lifelong KV cache for a block of DiT layers on one GPU.
+//
+// `Bank` is the B200 counterpart of the reference's KvBank of HistoryCaches
+// (cache/mod.rs:225-320, cache/history.rs:84-569) with the PhaseSwappedCache
+// wrapper folded in (cache/phase_swap.rs:27-161).  In a KvBank every layer
+// receives the same segment descriptors, so every layer's archive geometry,
+// frame timeline, working-set layout and counters are identical; the bank
+// keeps that shared state once and one device payload per layer.  Each
+// archived segment is one device slab holding every local layer's payload
+// at a fixed stride, so one kernel launch commits (or gathers) all layers.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <string>
+#include <vector>
+
+#include "nkv_kernels.h"
+#include "nkv_policy.h"
+#include "nomas_kv.h"
+
+namespace nkv {
+
+struct Error {
+  int code;
+  std::string msg;
+};
+[[noreturn]] void fail(int code, std::string msg);
+void check_cuda(cudaError_t e, const char* what);
+
+// Makes `device` current for the lifetime of the scope.
+class DeviceScope {
+ public:
+  explicit DeviceScope(int device);
+  ~DeviceScope();
+
+ private:
+  int prev_ = -1;
+  bool switched_ = false;
+};
+
+// LIFO allocator for archive slabs.  The archive only grows at the end
+// (commit) and shrinks at the end (rollback), so slabs are carved out of a
+// few large cudaMalloc'd chunks in stack order and never fragment.
+class ArchiveArena {
+ public:
+  ~ArchiveArena();
+  unsigned char* push(size_t bytes);
+  void pop();
+  void reserve(size_t bytes);
+  void release();
+
+ private:
+  struct Chunk {
+    unsigned char* base;
+    size_t cap;
+  };
+  struct Slot {
+    size_t chunk, off, size;
+  };
+  std::vector<Chunk> chunks_;
+  std::vector<Slot> stack_;
+  size_t free_from_top() const;
+};
+
+// Pinned host -> device upload area for per-call metadata (job lists, run
+// and tile tables, pointer arrays).  One H2D copy per call.
+class Staging {
+ public:
+  ~Staging();
+  void begin();  // waits until the previous upload has left the host buffer
+  size_t add(const void* p, size_t bytes);
+  void upload(cudaStream_t s);
+  const void* dev(size_t off) const { return dev_ + off; }
+  void release();
+
+ private:
+  unsigned char* host_ = nullptr;
+  unsigned char* dev_ = nullptr;
+  size_t cap_ = 0, used_ = 0;
+  cudaEvent_t done_ = nullptr;
+  bool pending_ = false;
+};
+
+struct Rec {  // one archived segment (history.rs:40-55), all local layers
+  nkv_segment_desc desc;
+  unsigned char* slab = nullptr;
+  size_t layer_stride = 0;
+  // component byte offsets inside a layer block:
+  //   FLOAT: 0 k, 1 v | INT8: 0 kq, 1 vq, 2 ks, 3 vs |
+  //   QVG  : 0 kcodes, 1 vcodes, 2 kscales, 3 vscales, 4..7 the text INT8 block
+  size_t off[8] = {0};
+  uint64_t n_blocks = 0;
+  uint64_t nbytes = 0;  // payload_bytes (history.rs:70-81) of one layer
+};
+
+struct RunSpec {  // a contiguous token range of one archived segment
+  size_t rec;
+  bool text;  // QVG: the INT8 text block
+  int64_t src_tok, dst_tok, ntok;
+};
+
+struct Plan {
+  std::vector<nkv_segment_layout> layout;
+  std::vector<RunSpec> runs;
+  uint64_t valid = 0;
+};
+
+class Bank {
+ public:
+  Bank(const nkv_cache_config& cfg, int n_layers, int layer_begin, int64_t batch, int64_t heads, int64_t head_dim,
+       int dtype, int device, cudaStream_t stream);
+  ~Bank();
+
+  void commit(const nkv_segment_desc& s, int kv_dtype, const void* const* k, const void* const* v);
+  void rollback();
+  void park();
+  void unpark();
+  void decode_segment(uint64_t pos, void* const* k_out, void* const* v_out);
+  void synchronize();
+  void reserve(uint64_t archive_bytes, uint64_t working_tokens);
+  uint64_t segment_bytes(const nkv_segment_desc& s) const;
+
+  void working_set(int layer, const void** k, const void** v, uint64_t* valid) const;
+  const std::vector<nkv_segment_layout>& layout() const { return parked_ ? p_layout_ : layout_; }
+  void info(int layer, nkv_cache_info_t* out) const;
+  nkv_metrics layer_metrics() const { return m_; }
+  nkv_metrics bank_metrics() const;
+  void set_codebooks(int layer, const float* host);
+  void get_codebooks(int layer, float* host, int32_t* fitted) const;
+  uint64_t export_segment(int layer, uint64_t pos, void* host, uint64_t cap);
+
+  void set_timing(bool on);
+  void kernel_stats(nkv_kernel_stat* out, bool reset);
+
+  int n_layers() const { return n_layers_; }
+
+ private:
+  Rec make_rec(const nkv_segment_desc& s) const;
+  void validate(const nkv_segment_desc& s, int kv_dtype, const void* const* k, const void* const* v);
+  Plan plan_rebuild();
+  void add_runs(const Plan& plan, size_t& runs_off, size_t& tiles_off, int& n_tiles, bool& aligned);
+  void fit_qvg(const nkv_segment_desc& s, int kv_dtype, const void* const* k, const void* const* v);
+  void launch_gather_into(size_t runs_off, size_t tiles_off, int n_tiles, size_t outk_off, size_t outv_off,
+                          uint64_t out_L, bool vector_ok, const uint32_t* abort_flag);
+  void ensure_ws(uint64_t tokens, unsigned char** fresh, uint64_t* fresh_cap);
+  unsigned char* ws_plane(unsigned char* base, uint64_t cap, int layer, int side) const;
+  size_t ws_plane_bytes(uint64_t cap) const;
+  void rebuild_now();  // plan + gather + install (rollback path)
+  uint64_t capacity_or_max() const { return cfg_.has_capacity ? cfg_.capacity : UINT64_MAX; }
+
+  void tbegin(int kind);
+  void tend(int kind);
+  void collect_timing(bool wait);
+
+  nkv_cache_config cfg_;
+  int n_layers_, layer_begin_;
+  int64_t B_, H_, D_;
+  int dtype_, device_;
+  cudaStream_t stream_ = nullptr, side_ = nullptr;
+  int q_stages_ = 0, q_bits_ = 0, q_block_ = 0, q_E_ = 0, q_bpt_ = 0;
+
+  std::vector<Rec> archive_;
+  uint64_t total_frames_ = 0, tpf_ = 0;
+  nkv_metrics m_{};
+  std::vector<nkv_segment_layout> layout_;
+  uint64_t valid_ = 0;
+
+  bool parked_ = false;
+  std::vector<nkv_segment_layout> p_layout_;
+  uint64_t p_valid_ = 0, p_bytes_ = 0;
+  std::vector<unsigned char*> p_host_;
+  std::vector<size_t> p_host_cap_;
+
+  ArchiveArena arena_;
+  unsigned char* ws_ = nullptr;
+  uint64_t ws_cap_ = 0;
+
+  float* cb_dev_ = nullptr;
+  std::vector<float> cb_host_;
+  std::vector<char> fitted_;
+  size_t cb_layer_ = 0;
+
+  uint32_t* d_flag_ = nullptr;
+  uint32_t* h_flag_ = nullptr;
+  Staging stg_;
+
+  bool timing_ = false;
+  struct Pending {
+    int kind;
+    cudaEvent_t a, b;
+  };
+  std::vector<Pending> pending_;
+  std::vector<cudaEvent_t> ev_pool_;
+  cudaEvent_t cur_a_ = nullptr;
+  nkv_kernel_stat stats_[NKV_KERNEL_COUNT] = {};
+};
+
+}  // namespace nkv

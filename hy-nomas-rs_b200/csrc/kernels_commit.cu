@@ -1,0 +1,382 @@
+// kernels_commit.cu — the commit side of the lifelong KV cache on sm_100a:
+// INT8 quantize (cache/int8.rs:65-134), the FLOAT archive copy
+// (cache/history.rs:243-247), QVG residual-VQ encode (cache/qvg.rs:173-256)
+// and the synthetic K/V generator used by tests and benchmarks.
+//
+// Exactness: every f32 / f64 operation the reference rounds separately is
+// written with an explicit round-to-nearest intrinsic, and the library is
+// compiled with -fmad=false, so no multiply-add is contracted behind our
+// back.  Explicit fma() is used only where the product is exact (f32 x f32
+// in f64), where fused and unfused results are identical.
+#include <cfloat>
+#include <cstdint>
+
+#include "nkv_device.cuh"
+#include "nkv_kernels.h"
+
+namespace nkv {
+
+// ---------------------------------------------------------------------------
+// INT8 quantize.  G threads per (token, head) row, 8 consecutive values per
+// thread (16-byte loads for BF16/F16, 2 x 16 bytes for F32), shuffle absmax
+// across the G lanes, coalesced 8-byte code stores and one f32 scale store
+// per row.
+//
+// Per value the reference computes round_half_away(x / s) with an IEEE
+// division.  The kernel multiplies by the correctly rounded reciprocal
+// instead (|error| <= 2^-23 relative, i.e. < 1.6e-5 absolute for |x/s| <=
+// 127.01) and rounds to nearest; only when that quotient lies within 1e-4 of
+// a half-integer, where the two could disagree, does it redo the value with
+// __fdiv_rn + roundf.  Outside that band both quotients round to the same
+// integer, so the codes are identical to the division-based reference.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t quant_exact(float x, float s) {
+  float t = roundf(__fdiv_rn(x, s));
+  t = dev::cmin(dev::cmax(t, -127.0f), 127.0f);
+  t = __fadd_rn(__fmul_rn(t, 1.0f), 128.0f);
+  t = dev::cmin(dev::cmax(t, 0.0f), 255.0f);
+  return dev::as_u8(t);
+}
+
+template <int IN_DT, int G>
+__global__ void __launch_bounds__(256) k_int8_quantize(const QuantJob* __restrict__ jobs, uint64_t rows,
+                                                       uint64_t in_row_offset, uint32_t* __restrict__ flag) {
+  constexpr int D = 8 * G;
+  const QuantJob J = jobs[blockIdx.y >> 1];
+  const int side = blockIdx.y & 1;
+  const void* in = side ? J.v : J.k;
+  uint8_t* q = side ? J.vq : J.kq;
+  float* sc = side ? J.vs : J.ks;
+  const int sub = threadIdx.x % G;
+  const uint64_t rows_per_cta = blockDim.x / G;
+  const float inv127 = (float)(1.0 / 127.0);
+  bool bad = false;
+  for (uint64_t base = (uint64_t)blockIdx.x * rows_per_cta; base < rows; base += (uint64_t)gridDim.x * rows_per_cta) {
+    const uint64_t row = base + threadIdx.x / G;
+    const bool active = row < rows;
+    float x[8];
+    if (active) {
+      dev::load8<IN_DT>(in, (in_row_offset + row) * D + sub * 8, x);
+      if constexpr (IN_DT != BF16) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) x[j] = dev::round_to<BF16>(x[j]);  // to_dtype(BF16), history.rs:249
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) x[j] = 0.0f;
+    }
+    float peak = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float a = fabsf(x[j]);
+      bad |= !(a < FLT_MAX);  // x != x || |x| >= f32::MAX (int8.rs:99-117)
+      peak = fmaxf(peak, a);
+    }
+#pragma unroll
+    for (int o = G / 2; o > 0; o >>= 1) peak = fmaxf(peak, __shfl_xor_sync(0xFFFFFFFFu, peak, o));
+    if (!active) continue;
+    // scale = where(peak > 0, peak * (f32)(1/127) + 0, 1)   (int8.rs:72)
+    const float s = peak > 0.0f ? __fadd_rn(__fmul_rn(peak, inv127), 0.0f) : 1.0f;
+    uint32_t b[8];
+    if (s >= FLT_MIN) {
+      const float r = __frcp_rn(s);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float y = __fmul_rn(x[j], r);
+        // round to nearest integer (|y| < 2^22), then check the tie band
+        const float t = __fadd_rn(__fadd_rn(y, 12582912.0f), -12582912.0f);
+        if (fabsf(__fadd_rn(y, -t)) >= 0.4999f) {
+          b[j] = quant_exact(x[j], s);
+        } else {
+          const float c = fminf(fmaxf(t, -127.0f), 127.0f);
+          b[j] = __float_as_uint(__fadd_rn(c, 8388736.0f)) & 0xFFu;  // 2^23 + 128 + c -> low byte
+        }
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) b[j] = quant_exact(x[j], s);
+    }
+    uint2 packed;
+    packed.x = b[0] | (b[1] << 8) | (b[2] << 16) | (b[3] << 24);
+    packed.y = b[4] | (b[5] << 8) | (b[6] << 16) | (b[7] << 24);
+    *reinterpret_cast<uint2*>(q + row * D + sub * 8) = packed;
+    if (sub == 0) sc[row] = s;
+  }
+  if (__any_sync(0xFFFFFFFFu, bad) && (threadIdx.x & 31) == 0) atomicOr(flag, 1u << side);
+}
+
+// Generic shape: one warp per row, any D, any alignment, exact division.
+template <int IN_DT>
+__global__ void __launch_bounds__(256) k_int8_quantize_generic(const QuantJob* __restrict__ jobs, uint64_t rows,
+                                                               uint64_t in_row_offset, int64_t D,
+                                                               uint32_t* __restrict__ flag) {
+  const QuantJob J = jobs[blockIdx.y >> 1];
+  const int side = blockIdx.y & 1;
+  const void* in = side ? J.v : J.k;
+  uint8_t* q = side ? J.vq : J.kq;
+  float* sc = side ? J.vs : J.ks;
+  const int lane = threadIdx.x & 31;
+  const uint64_t warps = blockDim.x / 32;
+  const float inv127 = (float)(1.0 / 127.0);
+  bool bad = false;
+  for (uint64_t row = (uint64_t)blockIdx.x * warps + threadIdx.x / 32; row < rows; row += (uint64_t)gridDim.x * warps) {
+    const uint64_t ib = (in_row_offset + row) * (uint64_t)D;
+    float peak = 0.0f;
+    for (int64_t d = lane; d < D; d += 32) {
+      const float a = fabsf(dev::round_to<BF16>(dev::load_elem<IN_DT>(in, ib + d)));
+      bad |= !(a < FLT_MAX);
+      peak = fmaxf(peak, a);
+    }
+    for (int o = 16; o > 0; o >>= 1) peak = fmaxf(peak, __shfl_xor_sync(0xFFFFFFFFu, peak, o));
+    const float s = peak > 0.0f ? __fadd_rn(__fmul_rn(peak, inv127), 0.0f) : 1.0f;
+    for (int64_t d = lane; d < D; d += 32)
+      q[row * D + d] = (uint8_t)quant_exact(dev::round_to<BF16>(dev::load_elem<IN_DT>(in, ib + d)), s);
+    if (lane == 0) sc[row] = s;
+  }
+  if (__any_sync(0xFFFFFFFFu, bad) && lane == 0) atomicOr(flag, 1u << side);
+}
+
+template <int IN_DT>
+static cudaError_t quantize_dispatch(const QuantJob* jobs, int n_jobs, uint64_t rows, uint64_t off, int64_t D,
+                                     bool vec_ok, uint32_t* flag, cudaStream_t s) {
+  if (rows == 0 || n_jobs == 0) return cudaSuccess;
+  const int threads = 256;
+  auto grid_for = [&](uint64_t rows_per_cta) {
+    uint64_t need = (rows + rows_per_cta - 1) / rows_per_cta;
+    uint64_t cap = 148ull * 16;  // enough CTAs to fill every SM several times
+    return dim3((unsigned)(need < cap ? need : cap), (unsigned)(2 * n_jobs));
+  };
+  if (vec_ok) {
+    switch (D) {
+      case 16: k_int8_quantize<IN_DT, 2><<<grid_for(threads / 2), threads, 0, s>>>(jobs, rows, off, flag); return cudaGetLastError();
+      case 32: k_int8_quantize<IN_DT, 4><<<grid_for(threads / 4), threads, 0, s>>>(jobs, rows, off, flag); return cudaGetLastError();
+      case 64: k_int8_quantize<IN_DT, 8><<<grid_for(threads / 8), threads, 0, s>>>(jobs, rows, off, flag); return cudaGetLastError();
+      case 128: k_int8_quantize<IN_DT, 16><<<grid_for(threads / 16), threads, 0, s>>>(jobs, rows, off, flag); return cudaGetLastError();
+      case 256: k_int8_quantize<IN_DT, 32><<<grid_for(threads / 32), threads, 0, s>>>(jobs, rows, off, flag); return cudaGetLastError();
+      default: break;
+    }
+  }
+  k_int8_quantize_generic<IN_DT><<<grid_for(threads / 32), threads, 0, s>>>(jobs, rows, off, D, flag);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_int8_quantize(const QuantJob* jobs_dev, int n_jobs, uint64_t rows, uint64_t in_row_offset,
+                                 int64_t D, int in_dtype, bool aligned16, uint32_t* flag, cudaStream_t s) {
+  // The vector path loads 16-byte chunks: every buffer must be 16-byte
+  // aligned (checked by the caller) and D a multiple of 8 keeps rows aligned.
+  const bool vec_ok = aligned16 && (D % 8) == 0;
+  switch (in_dtype) {
+    case F32: return quantize_dispatch<F32>(jobs_dev, n_jobs, rows, in_row_offset, D, vec_ok, flag, s);
+    case BF16: return quantize_dispatch<BF16>(jobs_dev, n_jobs, rows, in_row_offset, D, vec_ok, flag, s);
+    default: return quantize_dispatch<F16>(jobs_dev, n_jobs, rows, in_row_offset, D, vec_ok, flag, s);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// FLOAT archive: `to_dtype(model)` copy of each layer's K / V.
+// ---------------------------------------------------------------------------
+template <int IN_DT, int OUT_DT>
+__global__ void __launch_bounds__(256) k_convert(const ConvertJob* __restrict__ jobs, uint64_t n) {
+  const ConvertJob J = jobs[blockIdx.y];
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
+    const float v = dev::load_elem<IN_DT>(J.src, i);
+    if constexpr (IN_DT == OUT_DT) {
+      if constexpr (OUT_DT == F32) static_cast<float*>(J.dst)[i] = v;
+      else static_cast<unsigned short*>(J.dst)[i] = static_cast<const unsigned short*>(J.src)[i];
+    } else {
+      dev::store_elem<OUT_DT>(J.dst, i, v);
+    }
+  }
+}
+
+template <int IN_DT>
+static cudaError_t convert_out(const ConvertJob* jobs, int n_jobs, uint64_t n, int out_dt, cudaStream_t s) {
+  uint64_t need = (n + 255) / 256;
+  dim3 grid((unsigned)(need < 148ull * 32 ? need : 148ull * 32), (unsigned)n_jobs);
+  switch (out_dt) {
+    case F32: k_convert<IN_DT, F32><<<grid, 256, 0, s>>>(jobs, n); break;
+    case BF16: k_convert<IN_DT, BF16><<<grid, 256, 0, s>>>(jobs, n); break;
+    default: k_convert<IN_DT, F16><<<grid, 256, 0, s>>>(jobs, n); break;
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_convert(const ConvertJob* jobs_dev, int n_jobs, uint64_t n, int in_dtype, int out_dtype,
+                           cudaStream_t s) {
+  if (n == 0 || n_jobs == 0) return cudaSuccess;
+  switch (in_dtype) {
+    case F32: return convert_out<F32>(jobs_dev, n_jobs, n, out_dtype, s);
+    case BF16: return convert_out<BF16>(jobs_dev, n_jobs, n, out_dtype, s);
+    default: return convert_out<F16>(jobs_dev, n_jobs, n, out_dtype, s);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// QVG encode (cache/qvg.rs:173-256).  One CTA per (head, 64-token block,
+// layer x side), one thread per token of the block.  The block's residual
+// rows live in shared memory; per stage every thread finds its nearest
+// codeword with the reference's sequential f64 distance (ties to the lower
+// index), then one thread forms alpha = num / den from the per-token f64
+// inner sums in token order, and every thread subtracts alpha * e in f32.
+// ---------------------------------------------------------------------------
+template <int IN_DT>
+__global__ void __launch_bounds__(256) k_qvg_encode(const QvgEncodeJob* __restrict__ jobs, uint64_t L, int H, int D,
+                                                    uint64_t tokens, int stages, int bits, int block) {
+  extern __shared__ unsigned char smem_raw[];
+  const QvgEncodeJob J = jobs[blockIdx.z];
+  const int h = blockIdx.x;
+  const uint64_t blk = blockIdx.y;
+  const uint64_t start = blk * (uint64_t)block;
+  const int n = (int)((tokens - start) < (uint64_t)block ? (tokens - start) : (uint64_t)block);
+  const int E = 1 << bits;
+  const int ld = D + 1;
+  const uint64_t n_blocks = (tokens + block - 1) / block;
+  const int bpt = (stages * bits + 7) / 8;
+
+  float* res = reinterpret_cast<float*>(smem_raw);  // [block][D + 1]
+  size_t res_words = (size_t)block * ld;
+  res_words += res_words & 1;
+  double* inner = reinterpret_cast<double*>(res + res_words);              // [block]
+  double* ee = inner + block;                                              // [E]
+  uint64_t* packed = reinterpret_cast<uint64_t*>(ee + E);                  // [block]
+  int* code_s = reinterpret_cast<int*>(packed + block);                    // [block]
+  float* alpha_s = reinterpret_cast<float*>(code_s + block);               // [1]
+
+  for (int e = threadIdx.x; e < n * D; e += blockDim.x) {
+    const int t = e / D, d = e % D;
+    res[t * ld + d] = dev::load_elem<IN_DT>(J.x, ((start + t) * (uint64_t)H + h) * (uint64_t)D + d);
+  }
+  for (int t = threadIdx.x; t < n; t += blockDim.x) packed[t] = 0;
+  __syncthreads();
+
+  for (int s = 0; s < stages; ++s) {
+    const float* cbs = J.cb + ((size_t)h * stages + s) * E * D;
+    // sum_d e_d^2 per entry, sequential in d (the den inner sum, qvg.rs:228)
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+      double acc = 0.0;
+      for (int d = 0; d < D; ++d) {
+        const double v = (double)__ldg(cbs + (size_t)e * D + d);
+        acc = fma(v, v, acc);  // exact product: fused == unfused
+      }
+      ee[e] = acc;
+    }
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      const float* r = res + (size_t)i * ld;
+      // nearest (qvg.rs:303-321)
+      int best = 0;
+      double best_d = __longlong_as_double(0x7FF0000000000000ll);
+      for (int e = 0; e < E; ++e) {
+        const float* ce = cbs + (size_t)e * D;
+        double dist = 0.0;
+        for (int d = 0; d < D; ++d) {
+          const double diff = __dsub_rn((double)r[d], (double)__ldg(ce + d));
+          dist = __dadd_rn(dist, __dmul_rn(diff, diff));
+          if (dist >= best_d) break;
+        }
+        if (dist < best_d) {
+          best_d = dist;
+          best = e;
+        }
+      }
+      const float* ce = cbs + (size_t)best * D;
+      double acc = 0.0;
+      for (int d = 0; d < D; ++d) acc = fma((double)r[d], (double)__ldg(ce + d), acc);  // qvg.rs:223-227
+      inner[i] = acc;
+      code_s[i] = best;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      double num = 0.0, den = 0.0;
+      for (int t = 0; t < n; ++t) {
+        num = __dadd_rn(num, inner[t]);
+        den = __dadd_rn(den, ee[code_s[t]]);
+      }
+      const float alpha = den > 1e-12 ? __double2float_rn(__ddiv_rn(num, den)) : 1.0f;  // qvg.rs:230
+      *alpha_s = alpha;
+      J.scales[((size_t)h * n_blocks + blk) * stages + s] = alpha;
+    }
+    __syncthreads();
+    const float alpha = *alpha_s;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      float* r = res + (size_t)i * ld;
+      const int best = code_s[i];
+      const float* ce = cbs + (size_t)best * D;
+      for (int d = 0; d < D; ++d) r[d] = __fsub_rn(r[d], __fmul_rn(alpha, __ldg(ce + d)));  // qvg.rs:232-237
+      packed[i] |= (uint64_t)best << (s * bits);  // pack_bits, LSB first (qvg.rs:238-244)
+    }
+    __syncthreads();
+  }
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    uint8_t* out = J.codes + ((start + i) * (uint64_t)H + h) * bpt;
+    for (int b = 0; b < bpt; ++b) out[b] = (uint8_t)(packed[i] >> (8 * b));
+  }
+}
+
+static size_t qvg_encode_smem(int D, int block, int E) {
+  size_t res = (size_t)block * (D + 1);
+  res += res & 1;
+  return res * 4 + (size_t)block * 8 + (size_t)E * 8 + (size_t)block * 8 + (size_t)block * 4 + 16;
+}
+
+cudaError_t launch_qvg_encode(const QvgEncodeJob* jobs_dev, int n_jobs, int in_dtype, uint64_t L, int H, int D,
+                              uint64_t tokens, int stages, int bits, int block, cudaStream_t s) {
+  if (tokens == 0 || n_jobs == 0 || H == 0) return cudaSuccess;
+  const int E = 1 << bits;
+  const size_t smem = qvg_encode_smem(D, block, E);
+  const uint64_t n_blocks = (tokens + block - 1) / block;
+  dim3 grid((unsigned)H, (unsigned)n_blocks, (unsigned)n_jobs);
+  const int threads = block >= 256 ? 256 : ((block + 31) / 32) * 32;
+  cudaError_t err;
+  switch (in_dtype) {
+    case F32:
+      err = cudaFuncSetAttribute(k_qvg_encode<F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (err != cudaSuccess) return err;
+      k_qvg_encode<F32><<<grid, threads, smem, s>>>(jobs_dev, L, H, D, tokens, stages, bits, block);
+      break;
+    case BF16:
+      err = cudaFuncSetAttribute(k_qvg_encode<BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (err != cudaSuccess) return err;
+      k_qvg_encode<BF16><<<grid, threads, smem, s>>>(jobs_dev, L, H, D, tokens, stages, bits, block);
+      break;
+    default:
+      err = cudaFuncSetAttribute(k_qvg_encode<F16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (err != cudaSuccess) return err;
+      k_qvg_encode<F16><<<grid, threads, smem, s>>>(jobs_dev, L, H, D, tokens, stages, bits, block);
+      break;
+  }
+  return cudaGetLastError();
+}
+
+size_t qvg_encode_smem_bytes(int D, int block, int bits) { return qvg_encode_smem(D, block, 1 << bits); }
+
+// ---------------------------------------------------------------------------
+// Synthetic K/V: counter-based, so any element can be regenerated on the CPU
+// (tests/ reproduce it with numpy).
+// ---------------------------------------------------------------------------
+template <int DT>
+__global__ void __launch_bounds__(256) k_synth_fill(void* dst, uint64_t n, int HD, uint64_t key, uint64_t offset,
+                                                    const float* __restrict__ table,
+                                                    const float* __restrict__ chan_scale) {
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
+    const uint64_t u = dev::mix64(key + (i + offset + 1) * 0x9E3779B97F4A7C15ull);
+    float v = __ldg(table + (u >> 48));
+    if (chan_scale) v = __fmul_rn(v, __ldg(chan_scale + (i % (uint64_t)HD)));
+    dev::store_elem<DT>(dst, i, v);
+  }
+}
+
+cudaError_t launch_synth_fill(void* dst, int dtype, uint64_t rows, int H, int D, uint64_t key,
+                              uint64_t index_offset, const float* table, const float* chan_scale, cudaStream_t s) {
+  const uint64_t n = rows * (uint64_t)H * (uint64_t)D;
+  if (n == 0) return cudaSuccess;
+  uint64_t need = (n + 255) / 256;
+  unsigned grid = (unsigned)(need < 148ull * 64 ? need : 148ull * 64);
+  switch (dtype) {
+    case F32: k_synth_fill<F32><<<grid, 256, 0, s>>>(dst, n, H * D, key, index_offset, table, chan_scale); break;
+    case BF16: k_synth_fill<BF16><<<grid, 256, 0, s>>>(dst, n, H * D, key, index_offset, table, chan_scale); break;
+    default: k_synth_fill<F16><<<grid, 256, 0, s>>>(dst, n, H * D, key, index_offset, table, chan_scale); break;
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace nkv

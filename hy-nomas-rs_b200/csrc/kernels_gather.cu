@@ -1,0 +1,308 @@
+// kernels_gather.cu — the rebuild side of the lifelong KV cache on sm_100a.
+//
+// HistoryCache::rebuild (cache/history.rs:341-446) decodes every represented
+// archived segment in full and index_selects the sampled frames' token runs
+// plus the text block.  Here the host turns the selection into a list of
+// contiguous token runs and one kernel gathers exactly those tokens from the
+// archive, decoding on the fly:
+//   RUN_FLOAT     : copy (archive already holds the model dtype),
+//   RUN_INT8      : (u8 - 128) * scale, then to_dtype(model)  (int8.rs:139-155),
+//   RUN_QVG_VIDEO : sum_s alpha_s * cb_s[code_s] in f32 from +0, then
+//                   to_dtype(model)                           (qvg.rs:259-300).
+// Only selected tokens are read; every output byte is written once.
+//
+// Work decomposition: one CTA per (tile, layer, side).  A tile is <= 32
+// tokens of one run; each thread handles 16-value chunks (one 16-byte code
+// load, 32 or 64 bytes of stores), 4 chunks in flight.
+#include <cstdint>
+
+#include "nkv_device.cuh"
+#include "nkv_kernels.h"
+
+namespace nkv {
+
+namespace {
+
+// 16 dequantized values (u8 code - 128) * s as f32.  (f32(q) + (-128)) is
+// exact; the product rounds once, like candle's broadcast_mul.
+__device__ __forceinline__ void dequant16(const uint4 w, float s, float (&o)[16]) {
+  const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      // 0x4B0000bb = 2^23 + byte; minus (2^23 + 128) = byte - 128 exactly
+      const float f = __uint_as_float(__byte_perm(ws[j], 0x4B00u, 0x5440u + k));
+      o[4 * j + k] = __fmul_rn(__fadd_rn(f, -8388736.0f), s);
+    }
+  }
+}
+
+// Store 16 f32 values rounded to OUT_DT at element offset `i` (16-aligned).
+template <int OUT_DT>
+__device__ __forceinline__ void store16(void* out, uint64_t i, const float (&v)[16], bool finite) {
+  if constexpr (OUT_DT == F32) {
+    float4* p = reinterpret_cast<float4*>(static_cast<float*>(out) + i);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) p[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+  } else {
+    uint32_t w[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      uint32_t lo, hi;
+      if constexpr (OUT_DT == BF16) {
+        lo = finite ? dev::bf16_bits_finite(v[2 * j]) : dev::bf16_bits(v[2 * j]);
+        hi = finite ? dev::bf16_bits_finite(v[2 * j + 1]) : dev::bf16_bits(v[2 * j + 1]);
+      } else {
+        lo = dev::f16_bits(v[2 * j]);
+        hi = dev::f16_bits(v[2 * j + 1]);
+      }
+      w[j] = (lo & 0xFFFFu) | (hi << 16);
+    }
+    uint4* p = reinterpret_cast<uint4*>(static_cast<unsigned short*>(out) + i);
+    p[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    p[1] = make_uint4(w[4], w[5], w[6], w[7]);
+  }
+}
+
+}  // namespace
+
+constexpr int kGatherThreads = 256;
+
+template <int OUT_DT>
+__global__ void __launch_bounds__(kGatherThreads) k_gather(const GatherArgs a) {
+  if (a.abort_flag && *a.abort_flag) return;
+  const GatherTile tile = a.tiles[blockIdx.x];
+  const int layer = blockIdx.y;
+  const int side = blockIdx.z;
+  const GatherRun run = a.runs[tile.run];
+  const int H = a.H, D = a.D;
+  const int64_t HD = (int64_t)H * D;
+  const unsigned char* base = run.src + (int64_t)layer * run.layer_stride;
+  void* out_base = side ? a.out_v[layer] : a.out_k[layer];
+  const int64_t out_tok = (int64_t)tile.b * a.out_L + run.dst_tok + tile.tok0;
+  const int64_t src_tok = (int64_t)tile.b * run.src_L + run.src_tok + tile.tok0;
+  // Chunk arithmetic in 32 bits: a tile holds at most 32 tokens.
+  const int chunks_per_tok = (int)(HD / 16);
+  const int chunks_per_head = D / 16;
+  const int n_chunks = tile.ntok * chunks_per_tok;
+  constexpr int U = 4;
+
+  if (run.kind == RUN_INT8) {
+    const uint8_t* codes = base + run.off[side] + src_tok * HD;
+    const float* scales = reinterpret_cast<const float*>(base + run.off[2 + side]) + src_tok * H;
+    for (int c0 = threadIdx.x; c0 < n_chunks; c0 += kGatherThreads * U) {
+      uint4 w[U];
+      float s[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int c = c0 + u * kGatherThreads;
+        if (c < n_chunks) {
+          w[u] = __ldg(reinterpret_cast<const uint4*>(codes) + c);
+          const int t = c / chunks_per_tok;
+          const int h = (c - t * chunks_per_tok) / chunks_per_head;
+          s[u] = __ldg(scales + t * H + h);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int c = c0 + u * kGatherThreads;
+        if (c < n_chunks) {
+          float v[16];
+          dequant16(w[u], s[u], v);
+          store16<OUT_DT>(out_base, (uint64_t)(out_tok * HD + (int64_t)c * 16), v, true);
+        }
+      }
+    }
+  } else if (run.kind == RUN_FLOAT) {
+    const size_t esz = OUT_DT == F32 ? 4 : 2;
+    const uint4* src = reinterpret_cast<const uint4*>(base + run.off[side] + src_tok * HD * esz);
+    uint4* dst = reinterpret_cast<uint4*>(static_cast<unsigned char*>(out_base) + out_tok * HD * esz);
+    const int64_t n16 = (int64_t)tile.ntok * HD * esz / 16;
+    for (int64_t c0 = threadIdx.x; c0 < n16; c0 += (int64_t)kGatherThreads * U) {
+      uint4 w[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int64_t c = c0 + (int64_t)u * kGatherThreads;
+        if (c < n16) w[u] = __ldg(src + c);
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int64_t c = c0 + (int64_t)u * kGatherThreads;
+        if (c < n16) dst[c] = w[u];
+      }
+    }
+  } else {  // RUN_QVG_VIDEO
+    const int stages = a.stages, bits = a.bits, E = 1 << bits;
+    const int bpt = (stages * bits + 7) / 8;
+    const uint8_t* codes = base + run.off[side];
+    const float* scales = reinterpret_cast<const float*>(base + run.off[2 + side]);
+    const float* cb = a.cb + (int64_t)layer * a.cb_layer_stride + (int64_t)side * H * stages * E * D;
+    const uint32_t mask = (1u << bits) - 1u;
+    for (int c = threadIdx.x; c < n_chunks; c += kGatherThreads) {
+      const int t = c / chunks_per_tok;
+      const int w = c - t * chunks_per_tok;
+      const int h = w / chunks_per_head;
+      const int d0 = (w - h * chunks_per_head) * 16;
+      const int64_t tok = src_tok + t;  // batch is 1 for QVG
+      const uint8_t* cp = codes + (tok * H + h) * bpt;
+      uint64_t packed = 0;
+      for (int b = 0; b < bpt; ++b) packed |= (uint64_t)__ldg(cp + b) << (8 * b);
+      const int64_t blk = tok / a.block;
+      const float* al = scales + ((int64_t)h * run.n_blocks + blk) * stages;
+      float v[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) v[j] = 0.0f;
+      for (int s = 0; s < stages; ++s) {
+        const uint32_t code = (uint32_t)(packed >> (s * bits)) & mask;
+        const float alpha = __ldg(al + s);
+        const float4* e = reinterpret_cast<const float4*>(cb + (((int64_t)h * stages + s) * E + code) * D + d0);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float4 q = __ldg(e + j);
+          v[4 * j] = __fadd_rn(v[4 * j], __fmul_rn(alpha, q.x));
+          v[4 * j + 1] = __fadd_rn(v[4 * j + 1], __fmul_rn(alpha, q.y));
+          v[4 * j + 2] = __fadd_rn(v[4 * j + 2], __fmul_rn(alpha, q.z));
+          v[4 * j + 3] = __fadd_rn(v[4 * j + 3], __fmul_rn(alpha, q.w));
+        }
+      }
+      store16<OUT_DT>(out_base, (uint64_t)(out_tok * HD + (int64_t)c * 16), v, false);
+    }
+  }
+}
+
+// Any shape (head_dim not a multiple of 16, or unaligned tensors): one
+// thread per output element, same arithmetic.
+template <int OUT_DT>
+__global__ void __launch_bounds__(kGatherThreads) k_gather_generic(const GatherArgs a) {
+  if (a.abort_flag && *a.abort_flag) return;
+  const GatherTile tile = a.tiles[blockIdx.x];
+  const int layer = blockIdx.y;
+  const int side = blockIdx.z;
+  const GatherRun run = a.runs[tile.run];
+  const int H = a.H, D = a.D;
+  const int64_t HD = (int64_t)H * D;
+  const unsigned char* base = run.src + (int64_t)layer * run.layer_stride;
+  void* out_base = side ? a.out_v[layer] : a.out_k[layer];
+  const int64_t out_tok = (int64_t)tile.b * a.out_L + run.dst_tok + tile.tok0;
+  const int64_t src_tok = (int64_t)tile.b * run.src_L + run.src_tok + tile.tok0;
+  const int64_t n = (int64_t)tile.ntok * HD;
+  for (int64_t i = threadIdx.x; i < n; i += kGatherThreads) {
+    const int64_t t = i / HD;
+    const int64_t rem = i - t * HD;
+    const int h = (int)(rem / D);
+    const int d = (int)(rem - (int64_t)h * D);
+    float v;
+    if (run.kind == RUN_INT8) {
+      const uint8_t q = base[run.off[side] + (src_tok + t) * HD + rem];
+      const float sc = reinterpret_cast<const float*>(base + run.off[2 + side])[(src_tok + t) * H + h];
+      v = __fmul_rn(__fadd_rn((float)q, -128.0f), sc);
+    } else if (run.kind == RUN_FLOAT) {
+      const int64_t j = (src_tok + t) * HD + rem;
+      if constexpr (OUT_DT == F32) v = reinterpret_cast<const float*>(base + run.off[side])[j];
+      else {
+        reinterpret_cast<unsigned short*>(out_base)[(out_tok + t) * HD + rem] =
+            reinterpret_cast<const unsigned short*>(base + run.off[side])[j];
+        continue;
+      }
+    } else {
+      const int stages = a.stages, bits = a.bits, E = 1 << bits, bpt = (stages * bits + 7) / 8;
+      const int64_t tok = src_tok + t;
+      const uint8_t* cp = base + run.off[side] + (tok * H + h) * bpt;
+      uint64_t packed = 0;
+      for (int b = 0; b < bpt; ++b) packed |= (uint64_t)cp[b] << (8 * b);
+      const float* al = reinterpret_cast<const float*>(base + run.off[2 + side]) +
+                        ((int64_t)h * run.n_blocks + tok / a.block) * stages;
+      const float* cb = a.cb + (int64_t)layer * a.cb_layer_stride + (int64_t)side * H * stages * E * D;
+      v = 0.0f;
+      for (int s = 0; s < stages; ++s) {
+        const uint32_t code = (uint32_t)(packed >> (s * bits)) & ((1u << bits) - 1u);
+        v = __fadd_rn(v, __fmul_rn(al[s], cb[(((int64_t)h * stages + s) * E + code) * D + d]));
+      }
+    }
+    dev::store_elem<OUT_DT>(out_base, (uint64_t)((out_tok + t) * HD + rem), v);
+  }
+}
+
+cudaError_t launch_gather(const GatherArgs& a, bool vector_ok, cudaStream_t s) {
+  if (a.n_tiles == 0 || a.n_layers == 0) return cudaSuccess;
+  dim3 grid((unsigned)a.n_tiles, (unsigned)a.n_layers, 2);
+  const bool vec = vector_ok && (a.D % 16) == 0;
+  switch (a.out_dtype) {
+    case F32:
+      if (vec) k_gather<F32><<<grid, kGatherThreads, 0, s>>>(a);
+      else k_gather_generic<F32><<<grid, kGatherThreads, 0, s>>>(a);
+      break;
+    case BF16:
+      if (vec) k_gather<BF16><<<grid, kGatherThreads, 0, s>>>(a);
+      else k_gather_generic<BF16><<<grid, kGatherThreads, 0, s>>>(a);
+      break;
+    default:
+      if (vec) k_gather<F16><<<grid, kGatherThreads, 0, s>>>(a);
+      else k_gather_generic<F16><<<grid, kGatherThreads, 0, s>>>(a);
+      break;
+  }
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Standalone dequantize (int8.rs:139-155) and QVG decode (qvg.rs:259-300),
+// element per thread: used by the C-ABI kernel entry points and tests.
+// ---------------------------------------------------------------------------
+template <int OUT_DT>
+__global__ void __launch_bounds__(256) k_dequantize(const uint8_t* __restrict__ q, const float* __restrict__ scales,
+                                                    uint64_t n, int64_t D, void* out) {
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
+    const float sg = __fadd_rn(__fmul_rn((float)q[i], 1.0f), -128.0f);
+    dev::store_elem<OUT_DT>(out, i, __fmul_rn(sg, __ldg(scales + i / (uint64_t)D)));
+  }
+}
+
+cudaError_t launch_int8_dequantize(const uint8_t* q, const float* scales, uint64_t rows, int64_t D, int out_dtype,
+                                   void* out, cudaStream_t s) {
+  const uint64_t n = rows * (uint64_t)D;
+  if (n == 0) return cudaSuccess;
+  const uint64_t need = (n + 255) / 256;
+  const unsigned grid = (unsigned)(need < 148ull * 32 ? need : 148ull * 32);
+  switch (out_dtype) {
+    case F32: k_dequantize<F32><<<grid, 256, 0, s>>>(q, scales, n, D, out); break;
+    case BF16: k_dequantize<BF16><<<grid, 256, 0, s>>>(q, scales, n, D, out); break;
+    default: k_dequantize<F16><<<grid, 256, 0, s>>>(q, scales, n, D, out); break;
+  }
+  return cudaGetLastError();
+}
+
+__global__ void __launch_bounds__(256) k_qvg_decode(const float* __restrict__ cb, const uint8_t* __restrict__ codes,
+                                                    const float* __restrict__ scales, uint64_t tokens, int H, int D,
+                                                    int stages, int bits, int block, float* __restrict__ out) {
+  const int E = 1 << bits, bpt = (stages * bits + 7) / 8;
+  const uint64_t n_blocks = (tokens + block - 1) / block;
+  const uint64_t n = tokens * (uint64_t)H * D;
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
+    const uint64_t th = i / D;
+    const int d = (int)(i - th * D);
+    const uint64_t tok = th / H;
+    const int h = (int)(th - tok * H);
+    uint64_t packed = 0;
+    for (int b = 0; b < bpt; ++b) packed |= (uint64_t)codes[th * bpt + b] << (8 * b);
+    float acc = 0.0f;
+    for (int s = 0; s < stages; ++s) {
+      const uint32_t code = (uint32_t)(packed >> (s * bits)) & ((1u << bits) - 1u);
+      const float alpha = scales[((uint64_t)h * n_blocks + tok / block) * stages + s];
+      acc = __fadd_rn(acc, __fmul_rn(alpha, cb[(((uint64_t)h * stages + s) * E + code) * D + d]));
+    }
+    out[i] = acc;
+  }
+}
+
+cudaError_t launch_qvg_decode(const float* cb_side, const uint8_t* codes, const float* scales, uint64_t tokens,
+                              int H, int D, int stages, int bits, int block, float* out, cudaStream_t s) {
+  const uint64_t n = tokens * (uint64_t)H * D;
+  if (n == 0) return cudaSuccess;
+  const uint64_t need = (n + 255) / 256;
+  const unsigned grid = (unsigned)(need < 148ull * 32 ? need : 148ull * 32);
+  k_qvg_decode<<<grid, 256, 0, s>>>(cb_side, codes, scales, tokens, H, D, stages, bits, block, out);
+  return cudaGetLastError();
+}
+
+}  // namespace nkv

@@ -1,0 +1,120 @@
+// nkv_kernels.h — launch interface between the bank (host C++) and the
+// sm_100a kernels.  Plain structs of device pointers and sizes; every launch
+// is asynchronous on the given stream.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace nkv {
+
+enum DType : int { F32 = 0, BF16 = 1, F16 = 2 };
+
+inline size_t dtype_size(int dt) { return dt == F32 ? 4 : 2; }
+
+// ---------------------------------------------------------- INT8 commit ---
+// One job per (layer): quantize `rows` rows of D values of k and v
+// (cache/int8.rs:85-134 after the BF16 cast of history.rs:249-250).
+struct QuantJob {
+  const void* k;
+  const void* v;
+  uint8_t* kq;
+  uint8_t* vq;
+  float* ks;
+  float* vs;
+};
+// in_row_offset: rows of the input skipped before the first quantized row
+// (QVG text tokens start after the video tokens).  Sets bit 0 (k) / bit 1
+// (v) of *flag when a non-finite value is seen.
+// aligned16: every k/v/kq/vq pointer of every job is 16-byte aligned.
+cudaError_t launch_int8_quantize(const QuantJob* jobs_dev, int n_jobs, uint64_t rows, uint64_t in_row_offset,
+                                 int64_t D, int in_dtype, bool aligned16, uint32_t* flag, cudaStream_t s);
+
+// -------------------------------------------------------- FLOAT commit ---
+// Archive copy `to_dtype(model)` (history.rs:243-247): n elements per job.
+struct ConvertJob {
+  const void* src;
+  void* dst;
+};
+cudaError_t launch_convert(const ConvertJob* jobs_dev, int n_jobs, uint64_t n, int in_dtype, int out_dtype,
+                           cudaStream_t s);
+
+// ---------------------------------------------------------- QVG commit ---
+// One job per (layer, side): encode the first `tokens` tokens of a
+// (1, L, H, D) tensor with that side's codebooks [H][stages][E][D].
+struct QvgEncodeJob {
+  const void* x;
+  uint8_t* codes;   // [tokens][H][bpt]
+  float* scales;    // [H][n_blocks][stages]
+  const float* cb;  // [H][stages][E][D]
+};
+cudaError_t launch_qvg_encode(const QvgEncodeJob* jobs_dev, int n_jobs, int in_dtype, uint64_t L, int H, int D,
+                              uint64_t tokens, int stages, int bits, int block, cudaStream_t s);
+// Dynamic shared memory the encode kernel needs (the bank rejects configs
+// above the per-CTA limit at creation).
+size_t qvg_encode_smem_bytes(int D, int block, int bits);
+
+// -------------------------------------------------------------- gather ---
+enum RunKind : int32_t { RUN_FLOAT = 0, RUN_INT8 = 1, RUN_QVG_VIDEO = 2 };
+
+// A contiguous token range of one archived segment copied (and decoded) to
+// a contiguous range of the output.  Component byte offsets are relative to
+// the layer block `src + layer * layer_stride`:
+//   RUN_FLOAT     : off[0] k values, off[1] v values (model dtype)
+//   RUN_INT8      : off[0] k codes, off[1] v codes, off[2] k scales, off[3] v scales
+//   RUN_QVG_VIDEO : off[0] k codes, off[1] v codes, off[2] k scales, off[3] v scales
+struct GatherRun {
+  const unsigned char* src;
+  int64_t layer_stride;
+  int64_t off[4];
+  int64_t src_L;    // tokens per batch row of the source component
+  int64_t src_tok;  // first source token
+  int64_t dst_tok;  // first output token
+  int64_t ntok;
+  int32_t kind;
+  int32_t n_blocks;  // QVG: blocks in the payload
+};
+
+// Work unit of one CTA: `ntok` tokens of run `run` for batch row `b`,
+// starting `tok0` tokens into the run.
+struct GatherTile {
+  int32_t run;
+  int32_t b;
+  int32_t tok0;
+  int32_t ntok;
+};
+
+struct GatherArgs {
+  const GatherRun* runs;
+  const GatherTile* tiles;
+  int32_t n_tiles;
+  int32_t n_layers;
+  void* const* out_k;  // [n_layers] output bases (device array)
+  void* const* out_v;
+  int64_t out_L;  // tokens per batch row of the output
+  int32_t H, D;
+  int32_t out_dtype;
+  // QVG
+  const float* cb;          // layer 0 codebooks [2][H][stages][E][D]
+  int64_t cb_layer_stride;  // floats between layers
+  int32_t stages, bits, block;
+  // When non-null and nonzero at kernel start the gather writes nothing: a
+  // commit whose quantize found non-finite input leaves the working set as
+  // it was (the host then rolls the commit back).
+  const uint32_t* abort_flag;
+};
+
+// vector_ok: all run sources and outputs are 16-byte aligned (the kernel
+// additionally needs head_dim % 16 == 0 for its vector path).
+cudaError_t launch_gather(const GatherArgs& a, bool vector_ok, cudaStream_t s);
+
+// ------------------------------------------------------- standalone ops ---
+cudaError_t launch_int8_dequantize(const uint8_t* q, const float* scales, uint64_t rows, int64_t D, int out_dtype,
+                                   void* out, cudaStream_t s);
+cudaError_t launch_qvg_decode(const float* cb_side, const uint8_t* codes, const float* scales, uint64_t tokens,
+                              int H, int D, int stages, int bits, int block, float* out, cudaStream_t s);
+cudaError_t launch_synth_fill(void* dst, int dtype, uint64_t rows, int H, int D, uint64_t key,
+                              uint64_t index_offset, const float* table, const float* chan_scale, cudaStream_t s);
+
+}  // namespace nkv

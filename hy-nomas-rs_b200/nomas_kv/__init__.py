@@ -1,0 +1,546 @@
+"""nomas_kv — Python mirror of hy-nomas-rs's lifelong KV-cache API over the
+B200-native C ABI (include/nomas_kv.h).
+
+Names follow the reference crate ``nomas-core`` (``src/cache/``):
+``CacheConfig`` / ``QvgConfig`` / ``HistorySampling`` / ``CacheStorage``
+(config.rs:55-174), ``SegmentKv`` / ``SegmentLayout`` / ``CacheMetrics``
+(cache/mod.rs:61-151), ``KvBank`` (cache/mod.rs:225-320), ``build_cache``
+(cache/mod.rs:208-222) and the per-layer ``LifetimeKvCache`` methods
+(cache/mod.rs:154-204).  Errors map to the reference's ``Error`` kinds
+(error.rs:7-46).  K/V live in torch CUDA tensors; torch supplies device
+memory and the stream, every byte of cache work runs in the library's sm_100a
+kernels, and there is no CPU fallback.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import math
+from dataclasses import dataclass, field
+from typing import Optional, Sequence
+
+from . import _abi
+from ._abi import (NKV_BF16, NKV_F16, NKV_F32, NKV_SAMPLING_RECENT, NKV_SAMPLING_RECENT_MIX,
+                   NKV_SAMPLING_TEMPORAL, NKV_SAMPLING_UNIFORM, NKV_STORAGE_FLOAT, NKV_STORAGE_INT8,
+                   NKV_STORAGE_QVG)
+
+__all__ = [
+    "NomasError", "GeometryError", "CacheStateError", "InvalidConfigError", "MsgError", "CudaError", "ArgumentError",
+    "HistorySampling", "CacheStorage", "QvgConfig", "CacheConfig", "SegmentKv", "SegmentLayout", "CacheMetrics",
+    "KvBank", "LayerCache", "build_cache", "history_frame_indices", "uniform_frame_indices",
+    "recent_mix_uniform_frame_indices", "temporal_context_frame_indices", "plan_recent_trim", "partition_layers",
+    "lib",
+]
+
+
+# ------------------------------------------------------------------ errors
+class NomasError(RuntimeError):
+    """Base of the cache errors; ``code`` is the nkv_status value."""
+
+    code = -1
+
+    def __init__(self, msg: str):
+        super().__init__(msg)
+        self.msg = msg
+
+
+class GeometryError(NomasError):  # Error::Geometry
+    code = _abi.NKV_ERR_GEOMETRY
+
+
+class CacheStateError(NomasError):  # Error::CacheState
+    code = _abi.NKV_ERR_CACHE_STATE
+
+
+class InvalidConfigError(NomasError):  # Error::InvalidConfig
+    code = _abi.NKV_ERR_INVALID_CONFIG
+
+
+class MsgError(NomasError):  # Error::Msg
+    code = _abi.NKV_ERR_MSG
+
+
+class CudaError(NomasError):
+    code = _abi.NKV_ERR_CUDA
+
+
+class ArgumentError(NomasError):
+    code = _abi.NKV_ERR_ARGUMENT
+
+
+_ERRORS = {c.code: c for c in (GeometryError, CacheStateError, InvalidConfigError, MsgError, CudaError,
+                               ArgumentError)}
+
+
+def lib():
+    return _abi.load()
+
+
+def _check(rc: int):
+    if rc != _abi.NKV_OK:
+        msg = lib().nkv_last_error().decode()
+        raise _ERRORS.get(rc, NomasError)(msg)
+
+
+# ------------------------------------------------------------------ config
+@dataclass(frozen=True)
+class HistorySampling:
+    """config.rs:55-67: Recent | Uniform | RecentMixUniform | TemporalContext{gamma}."""
+
+    kind: int
+    gamma: float = 2.0
+
+    @staticmethod
+    def recent() -> "HistorySampling":
+        return HistorySampling(NKV_SAMPLING_RECENT)
+
+    @staticmethod
+    def uniform() -> "HistorySampling":
+        return HistorySampling(NKV_SAMPLING_UNIFORM)
+
+    @staticmethod
+    def recent_mix_uniform() -> "HistorySampling":
+        return HistorySampling(NKV_SAMPLING_RECENT_MIX)
+
+    @staticmethod
+    def temporal_context(gamma: float) -> "HistorySampling":
+        return HistorySampling(NKV_SAMPLING_TEMPORAL, float(gamma))
+
+    def __str__(self) -> str:  # config.rs:69-78
+        return {NKV_SAMPLING_RECENT: "recent", NKV_SAMPLING_UNIFORM: "uniform",
+                NKV_SAMPLING_RECENT_MIX: "recent_mix_uniform"}.get(self.kind, f"temporal_context(gamma={self.gamma})")
+
+
+@dataclass(frozen=True)
+class QvgConfig:
+    """config.rs:89-112 with its defaults (config.rs:101-111)."""
+
+    stages: int = 4
+    bits_per_stage: int = 2
+    block_size: int = 64
+    text_as_int8: bool = True
+    codebook_seed: int = 0x5EED0002
+
+    def entries(self) -> int:  # qvg.rs:57-59
+        return 1 << self.bits_per_stage
+
+    def bytes_per_token(self) -> int:  # qvg.rs:62-64
+        return (self.stages * self.bits_per_stage + 7) // 8
+
+    def payload_bytes(self, tokens: int, heads: int) -> int:  # qvg.rs:67-70
+        n_blocks = -(-tokens // self.block_size)
+        return tokens * heads * self.bytes_per_token() + n_blocks * heads * self.stages * 4
+
+
+@dataclass(frozen=True)
+class CacheStorage:
+    """config.rs:116-124: Floating | Int8 | Qvg(QvgConfig)."""
+
+    kind: int
+    qvg: QvgConfig = field(default_factory=QvgConfig)
+
+    @staticmethod
+    def floating() -> "CacheStorage":
+        return CacheStorage(NKV_STORAGE_FLOAT)
+
+    @staticmethod
+    def int8() -> "CacheStorage":
+        return CacheStorage(NKV_STORAGE_INT8)
+
+    @staticmethod
+    def qvg_(cfg: Optional[QvgConfig] = None) -> "CacheStorage":
+        return CacheStorage(NKV_STORAGE_QVG, cfg or QvgConfig())
+
+
+@dataclass
+class CacheConfig:
+    """config.rs:142-174 (defaults as CacheConfig::default, config.rs:162-174)."""
+
+    storage: CacheStorage = field(default_factory=CacheStorage.floating)
+    sampling: HistorySampling = field(default_factory=HistorySampling.recent)
+    capacity: Optional[int] = None
+    past_frames: int = 64
+    phase_swap: bool = False
+
+    def to_c(self) -> _abi.nkv_cache_config:
+        q = self.storage.qvg
+        return _abi.nkv_cache_config(
+            self.storage.kind,
+            _abi.nkv_qvg_config(q.stages, q.bits_per_stage, q.block_size, int(q.text_as_int8), q.codebook_seed),
+            self.sampling.kind, self.sampling.gamma, int(self.capacity is not None), self.capacity or 0,
+            self.past_frames, int(self.phase_swap))
+
+
+# -------------------------------------------------------------- records
+@dataclass
+class SegmentKv:
+    """cache/mod.rs:100-118: one completed segment's K/V (torch CUDA tensors,
+    shape (B, image_tokens + text_tokens, H, D))."""
+
+    segment_index: int
+    frame_start: int
+    frame_count: int
+    image_tokens: int
+    text_tokens: int
+    action_start: int
+    k: object
+    v: object
+
+    def __len__(self) -> int:
+        return self.image_tokens + self.text_tokens
+
+    def desc(self) -> _abi.nkv_segment_desc:
+        return _abi.nkv_segment_desc(self.segment_index, self.frame_start, self.frame_count, self.image_tokens,
+                                     self.text_tokens, self.action_start)
+
+
+@dataclass(frozen=True)
+class SegmentLayout:
+    """cache/mod.rs:61-97."""
+
+    segment_index: int
+    video_start: int
+    video_end: int
+    text_start: int
+    text_end: int
+    action_start: int
+
+    def __len__(self) -> int:
+        return (self.video_end - self.video_start) + (self.text_end - self.text_start)
+
+    def as_tuple(self):
+        return (self.segment_index, self.video_start, self.video_end, self.text_start, self.text_end,
+                self.action_start)
+
+
+@dataclass(frozen=True)
+class CacheMetrics:
+    """cache/mod.rs:133-151."""
+
+    archived_segments: int = 0
+    archived_bytes: int = 0
+    encode_calls: int = 0
+    d2h_bytes: int = 0
+    h2d_bytes: int = 0
+    rebuilds: int = 0
+    evicted_tokens: int = 0
+    rollbacks: int = 0
+
+    @staticmethod
+    def from_c(m: _abi.nkv_metrics) -> "CacheMetrics":
+        return CacheMetrics(*(int(getattr(m, n)) for n, _ in _abi.nkv_metrics._fields_))
+
+    def as_dict(self) -> dict:
+        return dict(self.__dict__)
+
+
+# ------------------------------------------------------- torch interop
+_TORCH_DTYPES = None
+
+
+def _torch():
+    import torch
+    return torch
+
+
+def dtype_code(dtype) -> int:
+    torch = _torch()
+    m = {torch.float32: NKV_F32, torch.bfloat16: NKV_BF16, torch.float16: NKV_F16}
+    if dtype not in m:
+        raise GeometryError(f"segment k must be float, got {dtype}")
+    return m[dtype]
+
+
+def torch_dtype(code: int):
+    torch = _torch()
+    return {NKV_F32: torch.float32, NKV_BF16: torch.bfloat16, NKV_F16: torch.float16}[code]
+
+
+class _DeviceView:
+    """Zero-copy __cuda_array_interface__ view of bank-owned device memory."""
+
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(int(s) for s in shape), "typestr": typestr,
+                                         "data": (int(ptr), False), "version": 2, "strides": None}
+
+
+def _wrap_device(ptr: int, shape, code: int, device):
+    torch = _torch()
+    if ptr == 0 or math.prod(shape) == 0:
+        return torch.zeros(shape, dtype=torch_dtype(code), device=device)
+    typestr = {NKV_F32: "<f4", NKV_F16: "<f2", NKV_BF16: "<i2"}[code]
+    t = torch.as_tensor(_DeviceView(ptr, shape, typestr), device=device)
+    return t.view(torch.bfloat16) if code == NKV_BF16 else t
+
+
+# ------------------------------------------------------------------ bank
+class LayerCache:
+    """One layer of a bank, with the LifetimeKvCache accessors (mod.rs:154-204)."""
+
+    def __init__(self, bank: "KvBank", layer: int):
+        self._bank, self._layer = bank, layer
+
+    def storage_format(self) -> CacheStorage:
+        return self._bank.cfg.storage
+
+    def sampling(self) -> HistorySampling:
+        return self._bank.cfg.sampling
+
+    def working_set(self):
+        """(k, v) zero-copy torch views (B, valid_len, H, D) of the model dtype;
+        valid until the bank's next commit / rollback / park."""
+        b = self._bank
+        k, v, n = C.c_void_p(), C.c_void_p(), C.c_uint64()
+        _check(lib().nkv_cache_working_set(b._h, self._layer, C.byref(k), C.byref(v), C.byref(n)))
+        shape = (b.batch, n.value, b.heads, b.head_dim)
+        return (_wrap_device(k.value or 0, shape, b.dtype_code, b.device),
+                _wrap_device(v.value or 0, shape, b.dtype_code, b.device))
+
+    def working_layout(self) -> list[SegmentLayout]:
+        b = self._bank
+        n = C.c_uint64()
+        _check(lib().nkv_cache_layout(b._h, self._layer, None, 0, C.byref(n)))
+        arr = (_abi.nkv_segment_layout * max(n.value, 1))()
+        _check(lib().nkv_cache_layout(b._h, self._layer, arr, n.value, C.byref(n)))
+        return [SegmentLayout(a.segment_index, a.video_start, a.video_end, a.text_start, a.text_end, a.action_start)
+                for a in arr[: n.value]]
+
+    def _info(self) -> _abi.nkv_cache_info_t:
+        out = _abi.nkv_cache_info_t()
+        _check(lib().nkv_cache_info(self._bank._h, self._layer, C.byref(out)))
+        return out
+
+    def valid_len(self) -> int:
+        return int(self._info().valid_len)
+
+    def capacity(self) -> int:
+        return int(self._info().capacity)
+
+    def n_segments(self) -> int:
+        return int(self._info().n_segments)
+
+    def total_frames(self) -> int:
+        return int(self._info().total_frames)
+
+    def tokens_per_frame(self) -> int:
+        return int(self._info().tokens_per_frame)
+
+    def is_parked(self) -> bool:
+        return bool(self._info().parked)
+
+    def metrics(self) -> CacheMetrics:
+        m = _abi.nkv_metrics()
+        _check(lib().nkv_cache_metrics(self._bank._h, self._layer, C.byref(m)))
+        return CacheMetrics.from_c(m)
+
+    # QvgCodec::with_codebooks (qvg.rs:101-104) / codebooks readback
+    def set_qvg_codebooks(self, cb) -> None:
+        import numpy as np
+        a = np.ascontiguousarray(cb, dtype=np.float32)
+        _check(lib().nkv_cache_set_qvg_codebooks(self._bank._h, self._layer, a.ctypes.data_as(C.c_void_p)))
+
+    def qvg_codebooks(self):
+        import numpy as np
+        b = self._bank
+        q = b.cfg.storage.qvg
+        out = np.zeros((2, b.heads, q.stages, q.entries(), b.head_dim), np.float32)
+        fitted = C.c_int32()
+        _check(lib().nkv_cache_get_qvg_codebooks(b._h, self._layer, out.ctypes.data_as(C.c_void_p),
+                                                 C.byref(fitted)))
+        return out if fitted.value else None
+
+    def export_segment(self, archive_pos: int) -> bytes:
+        """The archived payload of one segment (layout in nomas_kv.h)."""
+        import numpy as np
+        n = C.c_uint64()
+        _check(lib().nkv_cache_export_segment(self._bank._h, self._layer, archive_pos, None, 0, C.byref(n)))
+        buf = np.zeros(n.value, np.uint8)
+        _check(lib().nkv_cache_export_segment(self._bank._h, self._layer, archive_pos,
+                                              buf.ctypes.data_as(C.c_void_p), n.value, C.byref(n)))
+        return buf
+
+
+class KvBank:
+    """KvBank (cache/mod.rs:225-320) for layers [layer_begin, layer_begin+n_layers)
+    on one CUDA device, driven on torch's current stream of that device."""
+
+    def __init__(self, cfg: CacheConfig, n_layers: int, batch: int, heads: int, head_dim: int, dtype,
+                 device=None, layer_begin: int = 0, stream=None):
+        torch = _torch()
+        self.cfg = cfg
+        self.n_layers, self.layer_begin = n_layers, layer_begin
+        self.batch, self.heads, self.head_dim = batch, heads, head_dim
+        self.dtype_code = dtype if isinstance(dtype, int) else dtype_code(dtype)
+        self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        if self.device.type != "cuda":
+            raise ArgumentError("the cache runs on a CUDA device only (no CPU fallback)")
+        if stream is None:
+            stream = torch.cuda.current_stream(self.device)
+        self.stream = stream
+        h = C.c_void_p()
+        c = cfg.to_c()
+        _check(lib().nkv_bank_create(C.byref(c), n_layers, layer_begin, batch, heads, head_dim, self.dtype_code,
+                                     self.device.index or 0, C.c_void_p(stream.cuda_stream), C.byref(h)))
+        self._h = h
+
+    # -- lifecycle
+    def close(self):
+        if getattr(self, "_h", None):
+            _check(lib().nkv_bank_destroy(self._h))
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __len__(self) -> int:
+        return self.n_layers
+
+    def is_empty(self) -> bool:
+        return self.n_layers == 0
+
+    def layer(self, i: int) -> LayerCache:
+        if not 0 <= i < self.n_layers:
+            raise ArgumentError("layer out of range")
+        return LayerCache(self, i)
+
+    def as_refs(self) -> list[LayerCache]:
+        return [LayerCache(self, i) for i in range(self.n_layers)]
+
+    # -- cache/mod.rs:257-268
+    def commit(self, per_layer: Sequence[SegmentKv]) -> None:
+        if len(per_layer) != self.n_layers:
+            raise MsgError(f"KvBank::commit got {len(per_layer)} segments for {self.n_layers} layers")
+        d0 = per_layer[0]
+        key = (d0.segment_index, d0.frame_start, d0.frame_count, d0.image_tokens, d0.text_tokens, d0.action_start)
+        for s in per_layer[1:]:
+            if (s.segment_index, s.frame_start, s.frame_count, s.image_tokens, s.text_tokens, s.action_start) != key:
+                raise GeometryError("every layer of a bank commit must carry the same segment geometry")
+        ks = [s.k for s in per_layer]
+        vs = [s.v for s in per_layer]
+        self.commit_tensors(d0.desc(), ks, vs)
+
+    def commit_tensors(self, desc: _abi.nkv_segment_desc, ks, vs) -> None:
+        """Commit one segment given per-layer K/V tensors (the C-ABI shape)."""
+        expected = (self.batch, desc.image_tokens + desc.text_tokens, self.heads, self.head_dim)
+        dt = None
+        for name, ts in (("k", ks), ("v", vs)):
+            for t in ts:
+                if tuple(t.shape) != expected:
+                    raise GeometryError(f"segment {name} shape {list(t.shape)} != {list(expected)}")
+                if not t.is_contiguous():
+                    raise GeometryError(f"segment {name} must be contiguous")
+                code = dtype_code(t.dtype)
+                if dt is None:
+                    dt = code
+                elif code != dt:
+                    raise GeometryError("k and v of every layer must share one dtype")
+        kp = (C.c_void_p * self.n_layers)(*[t.data_ptr() for t in ks])
+        vp = (C.c_void_p * self.n_layers)(*[t.data_ptr() for t in vs])
+        _check(lib().nkv_bank_commit(self._h, C.byref(desc), dt, kp, vp))
+
+    def commit_ptrs(self, desc: _abi.nkv_segment_desc, kv_dtype: int, k_ptrs, v_ptrs) -> None:
+        kp = (C.c_void_p * self.n_layers)(*k_ptrs)
+        vp = (C.c_void_p * self.n_layers)(*v_ptrs)
+        _check(lib().nkv_bank_commit(self._h, C.byref(desc), kv_dtype, kp, vp))
+
+    def rollback(self) -> None:  # cache/mod.rs:276-281
+        _check(lib().nkv_bank_rollback(self._h))
+
+    def park_all(self) -> None:  # cache/mod.rs:284-289
+        _check(lib().nkv_bank_park(self._h))
+
+    def unpark_all(self) -> None:  # cache/mod.rs:292-297
+        _check(lib().nkv_bank_unpark(self._h))
+
+    def metrics(self) -> CacheMetrics:  # cache/mod.rs:305-319
+        m = _abi.nkv_metrics()
+        _check(lib().nkv_bank_metrics(self._h, C.byref(m)))
+        return CacheMetrics.from_c(m)
+
+    def synchronize(self) -> None:
+        _check(lib().nkv_bank_synchronize(self._h))
+
+    def reserve(self, archive_bytes: int, working_tokens: int = 0) -> None:
+        _check(lib().nkv_bank_reserve(self._h, archive_bytes, working_tokens))
+
+    def segment_bytes(self, desc: _abi.nkv_segment_desc) -> int:
+        n = C.c_uint64()
+        _check(lib().nkv_bank_segment_bytes(self._h, C.byref(desc), C.byref(n)))
+        return int(n.value)
+
+    def decode_segment(self, archive_pos: int, k_out, v_out) -> None:
+        """history.rs:308-338 for every local layer into caller tensors."""
+        kp = (C.c_void_p * self.n_layers)(*[t.data_ptr() for t in k_out])
+        vp = (C.c_void_p * self.n_layers)(*[t.data_ptr() for t in v_out])
+        _check(lib().nkv_bank_decode_segment(self._h, archive_pos, kp, vp))
+
+    def set_timing(self, on: bool) -> None:
+        _check(lib().nkv_bank_set_timing(self._h, int(on)))
+
+    def kernel_stats(self, reset: bool = False) -> dict:
+        arr = (_abi.nkv_kernel_stat * _abi.NKV_KERNEL_COUNT)()
+        _check(lib().nkv_bank_kernel_stats(self._h, arr, int(reset)))
+        return {n: (int(arr[i].launches), float(arr[i].total_ms)) for i, n in enumerate(_abi.KERNEL_NAMES)}
+
+
+def build_cache(cfg: CacheConfig, batch: int, heads: int, head_dim: int, dtype, device=None) -> KvBank:
+    """cache/mod.rs:208-222: a single-layer cache (phase swap per cfg)."""
+    return KvBank(cfg, 1, batch, heads, head_dim, dtype, device)
+
+
+# ------------------------------------------------------ host policy
+def _indices(kind: int, total: int, past: int, sampling: int = NKV_SAMPLING_UNIFORM, gamma: float = 2.0):
+    import numpy as np
+    n = C.c_uint64()
+    _check(lib().nkv_frame_indices(kind, total, past, sampling, gamma, None, 0, C.byref(n)))
+    out = np.zeros(max(n.value, 1), np.uint64)
+    _check(lib().nkv_frame_indices(kind, total, past, sampling, gamma, out.ctypes.data_as(C.c_void_p), n.value,
+                                   C.byref(n)))
+    return [int(x) for x in out[: n.value]]
+
+
+def uniform_frame_indices(total: int, past: int):  # uniform_history.rs:10-19
+    return _indices(0, total, past)
+
+
+def recent_mix_uniform_frame_indices(total: int, past: int):  # uniform_history.rs:23-32
+    return _indices(1, total, past)
+
+
+def temporal_context_frame_indices(total: int, past: int, gamma: float):  # uniform_history.rs:40-70
+    return _indices(2, total, past, NKV_SAMPLING_TEMPORAL, gamma)
+
+
+def history_frame_indices(total: int, past: int, sampling: HistorySampling):  # uniform_history.rs:76-125
+    return _indices(3, total, past, sampling.kind, sampling.gamma)
+
+
+def plan_recent_trim(records, capacity: int, tokens_per_frame: int):
+    """swa.rs:52-130: returns (drop_frames, drop_records, evicted_tokens, kept)."""
+    import numpy as np
+    n = len(records)
+    recs = np.ascontiguousarray(np.array(records, np.uint64).reshape(n, 5) if n else np.zeros((0, 5), np.uint64))
+    df = np.zeros(2 * n + 2, np.uint64)
+    dr = np.zeros(n + 1, np.uint64)
+    kept = np.zeros(5 * n + 5, np.uint64)
+    ndf, ndr, ev, nk = C.c_uint64(), C.c_uint64(), C.c_uint64(), C.c_uint64()
+    p = lambda a: a.ctypes.data_as(C.c_void_p)  # noqa: E731
+    _check(lib().nkv_plan_recent_trim(p(recs), n, capacity, tokens_per_frame, p(df), C.byref(ndf), p(dr),
+                                      C.byref(ndr), C.byref(ev), p(kept), C.byref(nk)))
+    return ([(int(df[2 * i]), int(df[2 * i + 1])) for i in range(ndf.value)],
+            [int(dr[i]) for i in range(ndr.value)], int(ev.value),
+            [tuple(int(x) for x in kept[5 * i: 5 * i + 5]) for i in range(nk.value)])
+
+
+def partition_layers(n_layers: int, world: int, rank: int) -> tuple[int, int]:
+    """Contiguous layer block (begin, count) of `rank` when `n_layers` caches
+    are sharded over `world` GPUs; the first n_layers % world ranks take one
+    extra layer."""
+    if world < 1 or not 0 <= rank < world:
+        raise ArgumentError("bad rank/world")
+    base, extra = divmod(n_layers, world)
+    count = base + (1 if rank < extra else 0)
+    begin = rank * base + min(rank, extra)
+    return begin, count
