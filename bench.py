@@ -1,0 +1,380 @@
+#!/usr/bin/env python
+"""Benchmark of the lifelong KV-cache hot path at 8B geometry.
+
+Workload ("Nomas-8B geometry INT8 commit+uniform
+rebuild"): 48 layers, 24 heads, head_dim 128, BF16 K/V (keys with a
+per-channel scale exp(N(0,1))), segments of 4 latent frames x 1560 tokens +
+256 text tokens, INT8 storage, uniform history sampling of 16 past frames,
+32 archived segments.  One step is one interactive turn through the public
+API: commit the new segment (quantize + archive), rebuild the working set
+(16 sampled frames + the text blocks of their segments) and gather the
+newest segment in full (the "+1 recent segment", HistoryCache::decode_segment
+semantics).  Layers are sharded contiguously across ranks (48/N each).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+Prints one JSON line (rank 0).  `value` is device-timed with inputs resident
+in HBM; `e2e` repeats the step with the K/V coming from pinned host memory
+inside the timed region.  `--impl reference` times the CPU restatement of the
+reference cache path (oracle/, the reference itself is Rust and cannot be
+built here) on the host cores with the same metric.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "hy-nomas-rs_b200"))
+
+LAYERS, HEADS, HEAD_DIM = 48, 24, 128
+TPF, FRAMES, TEXT = 1560, 4, 256
+SEG_TOKENS = FRAMES * TPF + TEXT  # 6496
+PAST = 16
+ARCHIVED = 32
+METRIC = "KV commit+rebuild GB/s (8B geometry, INT8, uniform rebuild)"
+# SURVEY 8(d) algorithmic bytes per token per layer: K+V BF16 read (12288) +
+# u8 codes and f32 scales written (6336) for a commit; the reverse for a
+# gathered output token.
+BYTES_PER_TOKEN = 2 * HEADS * HEAD_DIM * 2 + 2 * (HEADS * HEAD_DIM + HEADS * 4)  # 18624
+
+
+def rebuild_tokens() -> int:
+    """Tokens of the rebuilt working set once >= 16 segments are archived:
+    16 sampled frames in 16 distinct segments + their text blocks."""
+    return PAST * TPF + PAST * TEXT  # 29056
+
+
+def step_bytes(n_layers: int) -> dict:
+    commit = SEG_TOKENS * BYTES_PER_TOKEN * n_layers
+    rebuild = rebuild_tokens() * BYTES_PER_TOKEN * n_layers
+    recent = SEG_TOKENS * BYTES_PER_TOKEN * n_layers
+    return {"commit": commit, "rebuild": rebuild, "recent": recent, "total": commit + rebuild + recent}
+
+
+def load_peaks() -> dict:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return {"hbm_gbs": float(d["hbm_gbs"]), "src": "measured"}
+    return {"hbm_gbs": 6650.0, "src": "fallback"}
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi clock/throttle samples while the timed region runs."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits", "-lms", "100",
+                 "-i", str(self.gpu)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------- CPU side
+def cpu_sample(threads: int, warmup: int = 1, steps: int = 1) -> dict:
+    """The oracle (C++ restatement of the reference's CPU cache path, full
+    segment decode before index_select) on `threads` layers in parallel, one
+    layer per host thread, 8B geometry, archive prefilled to 31 segments."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import numpy as np
+    import oracle as orc
+    from nomas_kv import synth
+
+    orc.build()
+    n = threads
+    cfg = orc.Config(storage=orc.INT8, sampling=orc.UNIFORM, past_frames=PAST)
+    bank = orc.Bank(cfg, n, 1, HEADS, HEAD_DIM, orc.BF16)
+    ks = [synth.host_values(0, 1.0, 1, SEG_TOKENS, HEADS, HEAD_DIM, l, 0, 0, 1) for l in range(n)]
+    vs = [synth.host_values(0, 1.0, 1, SEG_TOKENS, HEADS, HEAD_DIM, l, 0, 1, 1) for l in range(n)]
+    seg = dict(segment_index=0, frame_start=0, frame_count=FRAMES, image_tokens=FRAMES * TPF, text_tokens=TEXT)
+    bank.commit(seg, orc.BF16, ks, vs, nthreads=n)
+    bank.prefill_clone(ARCHIVED - 2 - warmup)
+    idx = ARCHIVED - 1 - warmup
+    times = []
+    for i in range(warmup + steps):
+        s = dict(seg, segment_index=idx, frame_start=idx * FRAMES)
+        t0 = time.perf_counter()
+        bank.commit(s, orc.BF16, ks, vs, nthreads=n)
+        # the "+1 recent segment": full decode of the newest segment per layer
+        ths = [threading.Thread(target=bank.decode_segment, args=(l, idx, SEG_TOKENS)) for l in range(n)]
+        for t in ths:
+            t.start()
+        for t in ths:
+            t.join()
+        dt = time.perf_counter() - t0
+        if i >= warmup:
+            times.append(dt)
+        idx += 1
+    bank.close()
+    sec = sum(times) / len(times)
+    return {"value": step_bytes(n)["total"] / sec / 1e9, "unit": "GB/s", "cores": n, "kind": "port",
+            "sample": f"{n} layer(s) x 1 turn (commit + uniform rebuild + newest-segment decode) at 8B geometry, "
+                      f"archive of {ARCHIVED} segments, one host thread per layer; "
+                      f"{sec:.2f} s per turn"}
+
+
+# ------------------------------------------------------------ GPU side
+def run_gpu(args) -> None:
+    import torch
+    import torch.distributed as dist
+    import nomas_kv as nk
+    from nomas_kv import synth
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+
+    begin, n_layers = nk.partition_layers(LAYERS, world, rank)
+    stream = torch.cuda.current_stream(dev)
+    cfg = nk.CacheConfig(storage=nk.CacheStorage.int8(), sampling=nk.HistorySampling.uniform(), past_frames=PAST)
+    bank = nk.KvBank(cfg, n_layers, 1, HEADS, HEAD_DIM, torch.bfloat16, device=dev, layer_begin=begin)
+    gen = synth.DeviceGen(dev, seed=0, key_sigma=1.0)
+    desc = lambda i: nk._abi.nkv_segment_desc(i, i * FRAMES, FRAMES, FRAMES * TPF, TEXT, 0)  # noqa: E731
+
+    e2e_steps = min(args.steps, 4)
+    prefill = max(1, ARCHIVED - 1 - args.warmup)
+    total_segments = prefill + args.warmup + args.steps + args.warmup + e2e_steps
+    bank.reserve(bank.segment_bytes(desc(0)) * n_layers * total_segments, rebuild_tokens())
+
+    # two resident input sets (each > L2), alternated step to step
+    shape = (1, SEG_TOKENS, HEADS, HEAD_DIM)
+    sets = []
+    for s in range(2):
+        ks = [torch.empty(shape, dtype=torch.bfloat16, device=dev) for _ in range(n_layers)]
+        vs = [torch.empty(shape, dtype=torch.bfloat16, device=dev) for _ in range(n_layers)]
+        for i in range(n_layers):
+            gen.fill(ks[i], begin + i, s, 0, nk.NKV_BF16)
+            gen.fill(vs[i], begin + i, s, 1, nk.NKV_BF16)
+        sets.append((ks, vs))
+    recent_k = [torch.empty(shape, dtype=torch.bfloat16, device=dev) for _ in range(n_layers)]
+    recent_v = [torch.empty(shape, dtype=torch.bfloat16, device=dev) for _ in range(n_layers)]
+
+    seg = 0
+
+    def step(ks, vs):
+        nonlocal seg
+        bank.commit_tensors(desc(seg), ks, vs)  # validate + quantize + rebuild (one sync for the error flag)
+        bank.decode_segment(seg, recent_k, recent_v)  # the newest archived segment in full
+        seg += 1
+
+    for _ in range(prefill):
+        step(*sets[seg % 2])
+    for _ in range(args.warmup):
+        step(*sets[seg % 2])
+    assert bank.layer(0).valid_len() == rebuild_tokens(), bank.layer(0).valid_len()
+    torch.cuda.synchronize()
+
+    # ---------------------------------------------------- timed: resident
+    clocks = ClockSampler(local)
+    bank.kernel_stats(reset=True)
+    bank.set_timing(True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(args.steps):
+        step(*sets[seg % 2])
+    t1.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    bank.set_timing(False)
+    kst = bank.kernel_stats(reset=True)
+    ms = t0.elapsed_time(t1)
+    ms_t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms_max = float(ms_t.item())
+    bytes_all = step_bytes(LAYERS)["total"] * args.steps
+    value = bytes_all / (ms_max / 1e3) / 1e9
+
+    # ---------------------------------------------------- timed: e2e (host buffers)
+    host = []
+    for s in range(2):
+        hk = [torch.empty(shape, dtype=torch.bfloat16, pin_memory=True) for _ in range(n_layers)]
+        hv = [torch.empty(shape, dtype=torch.bfloat16, pin_memory=True) for _ in range(n_layers)]
+        for i in range(n_layers):
+            hk[i].copy_(sets[s][0][i])
+            hv[i].copy_(sets[s][1][i])
+        host.append((hk, hv))
+    stage_k = [torch.empty(shape, dtype=torch.bfloat16, device=dev) for _ in range(n_layers)]
+    stage_v = [torch.empty(shape, dtype=torch.bfloat16, device=dev) for _ in range(n_layers)]
+    flag_host = torch.empty(1, dtype=torch.int32, pin_memory=True)
+    vlen_dev = torch.empty(1, dtype=torch.int32, device=dev)
+
+    def e2e_step():
+        hk, hv = host[seg % 2]
+        for i in range(n_layers):
+            stage_k[i].copy_(hk[i], non_blocking=True)
+            stage_v[i].copy_(hv[i], non_blocking=True)
+        step(stage_k, stage_v)
+        # device -> host read of the step's result: the working-set length
+        vlen_dev.fill_(bank.layer(0).valid_len())
+        flag_host.copy_(vlen_dev, non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ems = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(ems, op=dist.ReduceOp.MAX)
+    e2e_value = step_bytes(LAYERS)["total"] * e2e_steps / (float(ems.item()) / 1e3) / 1e9
+    h2d = 2 * SEG_TOKENS * HEADS * HEAD_DIM * 2 * LAYERS
+    d2h = (4 + 4) * world  # commit's non-finite flag + the result read, per rank
+
+    # ---------------------------------------------------- roofline (gather)
+    peaks = load_peaks()
+    g_launch, g_ms = kst["gather"]
+    q_launch, q_ms = kst["quantize"]
+    sb = step_bytes(n_layers)
+    gather_bytes = (sb["rebuild"] + sb["recent"]) * args.steps
+    gather_gbs = gather_bytes / (g_ms / 1e3) / 1e9 if g_ms > 0 else None
+    quant_gbs = sb["commit"] * args.steps / (q_ms / 1e3) / 1e9 if q_ms > 0 else None
+    launches = g_launch + q_launch
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tp):
+        traffic = json.load(open(tp)).get("gather_bytes_per_launch")
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        try:
+            cpu = cpu_sample(min(os.cpu_count() or 1, 8))
+        except Exception as e:  # noqa: BLE001
+            cpu = {"value": None, "unit": "GB/s", "cores": 0, "kind": "port", "sample": f"failed: {e}"}
+
+    if rank == 0:
+        out = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "nomas-8B INT8 commit + uniform rebuild (16 past frames) + newest segment",
+                       "layers": LAYERS, "heads": HEADS, "head_dim": HEAD_DIM, "segment_tokens": SEG_TOKENS,
+                       "tokens_per_frame": TPF, "frames_per_segment": FRAMES, "text_tokens": TEXT,
+                       "past_frames": PAST, "archived_segments_at_first_timed_step": prefill + args.warmup + 1,
+                       "working_set_tokens": rebuild_tokens(), "bytes_per_step": step_bytes(LAYERS)["total"],
+                       "parallelism": f"layer-sharded x{world}", "l2": "inputs 3.8 GB per step > 126 MB L2"},
+            "roofline": {"bound": "hbm", "achieved": round(gather_gbs, 1) if gather_gbs else None,
+                         "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(gather_gbs / peaks["hbm_gbs"], 4) if gather_gbs else None,
+                         "traffic": traffic, "kernel": "k_gather (rebuild + newest segment)",
+                         "peak_src": peaks["src"], "launches": g_launch,
+                         "quantize_gbs": round(quant_gbs, 1) if quant_gbs else None,
+                         "quantize_frac": round(quant_gbs / peaks["hbm_gbs"], 4) if quant_gbs else None},
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "steps": e2e_steps},
+            "gpu_launches": launches,
+            "clocks": clk,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(out), flush=True)
+    bank.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = min(os.cpu_count() or 1, LAYERS)
+    r = cpu_sample(threads, warmup=max(0, min(args.warmup, 1)), steps=max(1, min(args.steps, 2)))
+    out = {"impl": "reference", "metric": METRIC, "value": round(r["value"], 3), "unit": "GB/s", "n_gpus": args.gpus,
+           "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "strong",
+           "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+           "config": {"workload": "nomas-8B INT8 commit + uniform rebuild (16 past frames) + newest segment",
+                      "layers_sampled": threads},
+           "cpu_baseline": r, "e2e": {"value": round(r["value"], 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                                      "d2h_bytes_per_step": 0}}
+    print(json.dumps(out), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        raise SystemExit("--warmup must be >= 3")
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_gpu(args)
+
+
+if __name__ == "__main__":
+    main()
