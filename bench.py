@@ -69,55 +69,51 @@ def load_peaks() -> dict:
 
 # ------------------------------------------------------------------ clocks
 class ClockSampler:
-    """nvidia-smi clock/throttle samples while the timed region runs."""
+    """SM clock and clock-event (throttle) reasons sampled through NVML every
+    ~5 ms while the timed region runs (nvidia-smi as a fallback)."""
 
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+            "hw_power_brake_slowdown": 0x80}
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
-        self.proc = None
-        self.lines: list[str] = []
+    def __init__(self, local_index: int):
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+        ids = [x for x in vis.split(",") if x.strip().isdigit()]
+        self.gpu = int(ids[local_index]) if local_index < len(ids) else local_index
+        self.samples: list[tuple[float, float, int]] = []
+        self._stop = threading.Event()
+        self._t = None
+        self.err = None
+
+    def _loop(self):
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.gpu)
+            smax = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+            get_reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+            while not self._stop.is_set():
+                sm = float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
+                self.samples.append((sm, smax, int(get_reasons(h))))
+                time.sleep(0.005)
+            pynvml.nvmlShutdown()
+        except Exception as e:  # noqa: BLE001
+            self.err = repr(e)
 
     def start(self):
-        try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits", "-lms", "100",
-                 "-i", str(self.gpu)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self._t = threading.Thread(target=self._read, daemon=True)
-            self._t.start()
-        except (OSError, FileNotFoundError):
-            self.proc = None
-
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+        self._t = threading.Thread(target=self._loop, daemon=True)
+        self._t.start()
+        time.sleep(0.02)
 
     def stop(self) -> dict:
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-        sm, smax, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            f = [x.strip() for x in ln.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1]))
-                smax.append(float(f[2]))
-            except ValueError:
-                continue
-            for n, v in zip(names, f[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        self._stop.set()
+        if self._t is not None:
+            self._t.join(timeout=5)
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [f"no samples: {self.err}"], "samples": 0}
+        reasons = sorted({n for _, _, r in self.samples for n, b in self.BITS.items() if r & b})
+        return {"sm_mhz": statistics.median(s for s, _, _ in self.samples),
+                "sm_max_mhz": max(m for _, m, _ in self.samples), "reasons": reasons, "samples": len(self.samples)}
 
 
 # ------------------------------------------------------------- CPU side
@@ -181,7 +177,8 @@ def run_gpu(args) -> None:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
 
-    begin, n_layers = nk.partition_layers(LAYERS, world, rank)
+    model_layers = args.layers
+    begin, n_layers = nk.partition_layers(model_layers, world, rank)
     stream = torch.cuda.current_stream(dev)
     cfg = nk.CacheConfig(storage=nk.CacheStorage.int8(), sampling=nk.HistorySampling.uniform(), past_frames=PAST)
     bank = nk.KvBank(cfg, n_layers, 1, HEADS, HEAD_DIM, torch.bfloat16, device=dev, layer_begin=begin)
@@ -246,7 +243,7 @@ def run_gpu(args) -> None:
     if world > 1:
         dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
     ms_max = float(ms_t.item())
-    bytes_all = step_bytes(LAYERS)["total"] * args.steps
+    bytes_all = step_bytes(model_layers)["total"] * args.steps
     value = bytes_all / (ms_max / 1e3) / 1e9
 
     # ---------------------------------------------------- timed: e2e (host buffers)
@@ -288,8 +285,8 @@ def run_gpu(args) -> None:
     ems = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(ems, op=dist.ReduceOp.MAX)
-    e2e_value = step_bytes(LAYERS)["total"] * e2e_steps / (float(ems.item()) / 1e3) / 1e9
-    h2d = 2 * SEG_TOKENS * HEADS * HEAD_DIM * 2 * LAYERS
+    e2e_value = step_bytes(model_layers)["total"] * e2e_steps / (float(ems.item()) / 1e3) / 1e9
+    h2d = 2 * SEG_TOKENS * HEADS * HEAD_DIM * 2 * model_layers
     d2h = (4 + 4) * world  # commit's non-finite flag + the result read, per rank
 
     # ---------------------------------------------------- roofline (gather)
@@ -319,10 +316,10 @@ def run_gpu(args) -> None:
             "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": "nomas-8B INT8 commit + uniform rebuild (16 past frames) + newest segment",
-                       "layers": LAYERS, "heads": HEADS, "head_dim": HEAD_DIM, "segment_tokens": SEG_TOKENS,
+                       "layers": model_layers, "heads": HEADS, "head_dim": HEAD_DIM, "segment_tokens": SEG_TOKENS,
                        "tokens_per_frame": TPF, "frames_per_segment": FRAMES, "text_tokens": TEXT,
                        "past_frames": PAST, "archived_segments_at_first_timed_step": prefill + args.warmup + 1,
-                       "working_set_tokens": rebuild_tokens(), "bytes_per_step": step_bytes(LAYERS)["total"],
+                       "working_set_tokens": rebuild_tokens(), "bytes_per_step": step_bytes(model_layers)["total"],
                        "parallelism": f"layer-sharded x{world}", "l2": "inputs 3.8 GB per step > 126 MB L2"},
             "roofline": {"bound": "hbm", "achieved": round(gather_gbs, 1) if gather_gbs else None,
                          "peak": peaks["hbm_gbs"], "unit": "GB/s",
@@ -367,6 +364,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--layers", type=int, default=LAYERS,
+                    help="model layers (48 = the 8B geometry; fewer only for small profiling cases)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         raise SystemExit("--warmup must be >= 3")

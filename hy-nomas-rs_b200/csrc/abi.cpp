@@ -258,7 +258,7 @@ int nkv_int8_quantize(const void* k, const void* v, int32_t in_dtype, uint64_t r
     }
     need(k, "k"), need(v, "v"), need(kq, "kq"), need(vq, "vq"), need(ks, "ks"), need(vs, "vs");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    nkv::QuantJob job{k, v, kq, vq, ks, vs};
+    nkv::QuantJob job{k, v, kq, vq, ks, vs, nullptr};
     nkv::QuantJob* d_job = nullptr;
     uint32_t* d_flag = nullptr;
     nkv::check_cuda(cudaMallocAsync(reinterpret_cast<void**>(&d_job), sizeof(job), s), "cudaMallocAsync");

@@ -196,9 +196,10 @@ Bank::Bank(const nkv_cache_config& cfg, int n_layers, int layer_begin, int64_t b
   if (device < 0 || device >= n_dev) fail(NKV_ERR_ARGUMENT, "device " + std::to_string(device) + " out of range");
   DeviceScope ds(device_);
   NKV_CUDA(cudaStreamCreateWithFlags(&side_, cudaStreamNonBlocking));
-  NKV_CUDA(cudaMalloc(&d_flag_, sizeof(uint32_t)));
-  NKV_CUDA(cudaHostAlloc(&h_flag_, sizeof(uint32_t), cudaHostAllocDefault));
-  *h_flag_ = 0;
+  // [0]: any layer saw a non-finite value (aborts the gather); [1 + i]: layer i
+  NKV_CUDA(cudaMalloc(&d_flag_, sizeof(uint32_t) * (n_layers_ + 1)));
+  NKV_CUDA(cudaHostAlloc(&h_flag_, sizeof(uint32_t) * (n_layers_ + 1), cudaHostAllocDefault));
+  std::memset(h_flag_, 0, sizeof(uint32_t) * (n_layers_ + 1));
   if (cfg.storage == NKV_STORAGE_QVG) {
     cb_layer_ = size_t(2) * H_ * q_stages_ * q_E_ * D_;
     NKV_CUDA(cudaMalloc(&cb_dev_, cb_layer_ * n_layers_ * sizeof(float)));
@@ -470,7 +471,8 @@ void Bank::ensure_ws(uint64_t tokens, unsigned char** fresh, uint64_t* fresh_cap
   *fresh_cap = cap;
 }
 
-void Bank::fit_qvg(const nkv_segment_desc& s, int kv_dtype, const void* const* k, const void* const* v) {
+std::vector<int> Bank::fit_qvg(const nkv_segment_desc& s, int kv_dtype, const void* const* k, const void* const* v) {
+  std::vector<int> fitted_now;
   const size_t L = s.image_tokens + s.text_tokens, n = L * H_ * D_;
   const size_t esz = dtype_size(kv_dtype);
   std::vector<unsigned char> raw(n * esz);
@@ -513,7 +515,9 @@ void Bank::fit_qvg(const nkv_segment_desc& s, int kv_dtype, const void* const* k
     NKV_CUDA(cudaMemcpyAsync(cb_dev_ + cb_layer_ * i, out, cb_layer_ * 4, cudaMemcpyHostToDevice, stream_));
     NKV_CUDA(cudaStreamSynchronize(stream_));
     fitted_[i] = 1;
+    fitted_now.push_back(i);
   }
+  return fitted_now;
 }
 
 // commit_segment (history.rs:458-463).
@@ -533,7 +537,8 @@ void Bank::commit(const nkv_segment_desc& s, int kv_dtype, const void* const* k,
   unsigned char* fresh = nullptr;
   uint64_t fresh_cap = 0;
   try {
-    if (cfg_.storage == NKV_STORAGE_QVG) fit_qvg(s, kv_dtype, k, v);  // first commit only (history.rs:256-262)
+    std::vector<int> fitted_now;
+    if (cfg_.storage == NKV_STORAGE_QVG) fitted_now = fit_qvg(s, kv_dtype, k, v);  // history.rs:256-262
 
     archive_.push_back(r);
     pushed = true;
@@ -571,7 +576,7 @@ void Bank::commit(const nkv_segment_desc& s, int kv_dtype, const void* const* k,
       for (int i = 0; i < n_layers_; ++i) {
         unsigned char* lb = r.slab + size_t(i) * r.layer_stride;
         jobs.push_back({k[i], v[i], lb + r.off[0], lb + r.off[1], reinterpret_cast<float*>(lb + r.off[2]),
-                        reinterpret_cast<float*>(lb + r.off[3])});
+                        reinterpret_cast<float*>(lb + r.off[3]), d_flag_ + 1 + i});
       }
       jobs_off = stg_.add(jobs.data(), jobs.size() * sizeof(QuantJob));
     } else {
@@ -583,7 +588,7 @@ void Bank::commit(const nkv_segment_desc& s, int kv_dtype, const void* const* k,
         jobs.push_back({k[i], lb + r.off[0], reinterpret_cast<float*>(lb + r.off[2]), cb});
         jobs.push_back({v[i], lb + r.off[1], reinterpret_cast<float*>(lb + r.off[3]), cb + cb_layer_ / 2});
         tj.push_back({k[i], v[i], lb + r.off[4], lb + r.off[5], reinterpret_cast<float*>(lb + r.off[6]),
-                      reinterpret_cast<float*>(lb + r.off[7])});
+                      reinterpret_cast<float*>(lb + r.off[7]), d_flag_ + 1 + i});
       }
       jobs_off = stg_.add(jobs.data(), jobs.size() * sizeof(QvgEncodeJob));
       text_jobs_off = stg_.add(tj.data(), tj.size() * sizeof(QuantJob));
@@ -604,7 +609,7 @@ void Bank::commit(const nkv_segment_desc& s, int kv_dtype, const void* const* k,
     }
     stg_.upload(stream_);
 
-    NKV_CUDA(cudaMemsetAsync(d_flag_, 0, sizeof(uint32_t), stream_));
+    NKV_CUDA(cudaMemsetAsync(d_flag_, 0, sizeof(uint32_t) * (n_layers_ + 1), stream_));
     if (cfg_.storage == NKV_STORAGE_FLOAT) {
       tbegin(NKV_KERNEL_FLOAT_ARCHIVE);
       NKV_CUDA(launch_convert(static_cast<const ConvertJob*>(stg_.dev(jobs_off)), 2 * n_layers_,
@@ -629,14 +634,22 @@ void Bank::commit(const nkv_segment_desc& s, int kv_dtype, const void* const* k,
       }
     }
     if (n_tiles > 0) launch_gather_into(runs_off, tiles_off, n_tiles, outk_off, outv_off, plan.valid, runs_aligned, d_flag_);
-    NKV_CUDA(cudaMemcpyAsync(h_flag_, d_flag_, sizeof(uint32_t), cudaMemcpyDeviceToHost, stream_));
+    NKV_CUDA(cudaMemcpyAsync(h_flag_, d_flag_, sizeof(uint32_t) * (n_layers_ + 1), cudaMemcpyDeviceToHost,
+                             stream_));
     NKV_CUDA(cudaStreamSynchronize(stream_));
     collect_timing(false);
 
-    if (*h_flag_ != 0) {
+    if (h_flag_[0] != 0) {
       // quantize_kv_pair rejected the segment (int8.rs:99-117): nothing was
-      // archived and the working set was left untouched by the gather.
-      const bool k_bad = (*h_flag_ & 1u) != 0;
+      // archived and the working set was left untouched by the gather.  The
+      // error is the first failing layer's, as in KvBank::commit's loop
+      // (cache/mod.rs:264-266); layers after it never reach their first-commit
+      // QVG fit there, so their fit from this segment is dropped.
+      int first = 0;
+      while (first < n_layers_ && h_flag_[1 + first] == 0) ++first;
+      const bool k_bad = first < n_layers_ && (h_flag_[1 + first] & 1u) != 0;
+      for (int i : fitted_now)
+        if (i > first) fitted_[i] = 0;
       archive_.pop_back();
       pushed = false;
       total_frames_ -= s.frame_count;

@@ -141,7 +141,7 @@ class Bank {
   void validate(const nkv_segment_desc& s, int kv_dtype, const void* const* k, const void* const* v);
   Plan plan_rebuild();
   void add_runs(const Plan& plan, size_t& runs_off, size_t& tiles_off, int& n_tiles, bool& aligned);
-  void fit_qvg(const nkv_segment_desc& s, int kv_dtype, const void* const* k, const void* const* v);
+  std::vector<int> fit_qvg(const nkv_segment_desc& s, int kv_dtype, const void* const* k, const void* const* v);
   void launch_gather_into(size_t runs_off, size_t tiles_off, int n_tiles, size_t outk_off, size_t outv_off,
                           uint64_t out_L, bool vector_ok, const uint32_t* abort_flag);
   void ensure_ws(uint64_t tokens, unsigned char** fresh, uint64_t* fresh_cap);
@@ -182,7 +182,7 @@ class Bank {
   std::vector<char> fitted_;
   size_t cb_layer_ = 0;
 
-  uint32_t* d_flag_ = nullptr;
+  uint32_t* d_flag_ = nullptr;  // n_layers + 1 non-finite flags (see the constructor)
   uint32_t* h_flag_ = nullptr;
   Staging stg_;
 

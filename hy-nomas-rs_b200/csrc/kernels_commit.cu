@@ -38,7 +38,33 @@ __device__ __forceinline__ uint32_t quant_exact(float x, float s) {
   return dev::as_u8(t);
 }
 
-template <int IN_DT, int G>
+// 8 values of one row with scale s -> 8 packed code bytes (see above).
+__device__ __forceinline__ uint2 quant8(const float (&x)[8], float s) {
+  uint32_t b[8];
+  if (s >= FLT_MIN) {
+    const float r = __frcp_rn(s);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float y = __fmul_rn(x[j], r);
+      // round to nearest integer (|y| < 2^22), then check the tie band
+      const float t = __fadd_rn(__fadd_rn(y, 12582912.0f), -12582912.0f);
+      if (fabsf(__fadd_rn(y, -t)) >= 0.4999f) {
+        b[j] = quant_exact(x[j], s);
+      } else {
+        const float c = fminf(fmaxf(t, -127.0f), 127.0f);
+        b[j] = __float_as_uint(__fadd_rn(c, 8388736.0f)) & 0xFFu;  // 2^23 + 128 + c -> low byte
+      }
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) b[j] = quant_exact(x[j], s);
+  }
+  return make_uint2(b[0] | (b[1] << 8) | (b[2] << 16) | (b[3] << 24), b[4] | (b[5] << 8) | (b[6] << 16) | (b[7] << 24));
+}
+
+// R rows per thread and iteration: all R loads are issued before any of
+// them is consumed, so each thread keeps R x 16 bytes in flight.
+template <int IN_DT, int G, int R>
 __global__ void __launch_bounds__(256) k_int8_quantize(const QuantJob* __restrict__ jobs, uint64_t rows,
                                                        uint64_t in_row_offset, uint32_t* __restrict__ flag) {
   constexpr int D = 8 * G;
@@ -48,61 +74,49 @@ __global__ void __launch_bounds__(256) k_int8_quantize(const QuantJob* __restric
   uint8_t* q = side ? J.vq : J.kq;
   float* sc = side ? J.vs : J.ks;
   const int sub = threadIdx.x % G;
-  const uint64_t rows_per_cta = blockDim.x / G;
+  const uint64_t rows_per_pass = blockDim.x / G;
   const float inv127 = (float)(1.0 / 127.0);
   bool bad = false;
-  for (uint64_t base = (uint64_t)blockIdx.x * rows_per_cta; base < rows; base += (uint64_t)gridDim.x * rows_per_cta) {
-    const uint64_t row = base + threadIdx.x / G;
-    const bool active = row < rows;
-    float x[8];
-    if (active) {
-      dev::load8<IN_DT>(in, (in_row_offset + row) * D + sub * 8, x);
+  for (uint64_t base = (uint64_t)blockIdx.x * rows_per_pass * R; base < rows;
+       base += (uint64_t)gridDim.x * rows_per_pass * R) {
+    float x[R][8];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const uint64_t row = base + r * rows_per_pass + threadIdx.x / G;
+      if (row < rows) {
+        dev::load8<IN_DT>(in, (in_row_offset + row) * D + sub * 8, x[r]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) x[r][j] = 0.0f;
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const uint64_t row = base + r * rows_per_pass + threadIdx.x / G;
       if constexpr (IN_DT != BF16) {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) x[j] = dev::round_to<BF16>(x[j]);  // to_dtype(BF16), history.rs:249
+        for (int j = 0; j < 8; ++j) x[r][j] = dev::round_to<BF16>(x[r][j]);  // to_dtype(BF16), history.rs:249
       }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) x[j] = 0.0f;
-    }
-    float peak = 0.0f;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float a = fabsf(x[j]);
-      bad |= !(a < FLT_MAX);  // x != x || |x| >= f32::MAX (int8.rs:99-117)
-      peak = fmaxf(peak, a);
-    }
-#pragma unroll
-    for (int o = G / 2; o > 0; o >>= 1) peak = fmaxf(peak, __shfl_xor_sync(0xFFFFFFFFu, peak, o));
-    if (!active) continue;
-    // scale = where(peak > 0, peak * (f32)(1/127) + 0, 1)   (int8.rs:72)
-    const float s = peak > 0.0f ? __fadd_rn(__fmul_rn(peak, inv127), 0.0f) : 1.0f;
-    uint32_t b[8];
-    if (s >= FLT_MIN) {
-      const float r = __frcp_rn(s);
+      float peak = 0.0f;
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const float y = __fmul_rn(x[j], r);
-        // round to nearest integer (|y| < 2^22), then check the tie band
-        const float t = __fadd_rn(__fadd_rn(y, 12582912.0f), -12582912.0f);
-        if (fabsf(__fadd_rn(y, -t)) >= 0.4999f) {
-          b[j] = quant_exact(x[j], s);
-        } else {
-          const float c = fminf(fmaxf(t, -127.0f), 127.0f);
-          b[j] = __float_as_uint(__fadd_rn(c, 8388736.0f)) & 0xFFu;  // 2^23 + 128 + c -> low byte
-        }
+        const float a = fabsf(x[r][j]);
+        bad |= !(a < FLT_MAX);  // x != x || |x| >= f32::MAX (int8.rs:99-117)
+        peak = fmaxf(peak, a);
       }
-    } else {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) b[j] = quant_exact(x[j], s);
+      for (int o = G / 2; o > 0; o >>= 1) peak = fmaxf(peak, __shfl_xor_sync(0xFFFFFFFFu, peak, o));
+      if (row >= rows) continue;
+      // scale = where(peak > 0, peak * (f32)(1/127) + 0, 1)   (int8.rs:72)
+      const float s = peak > 0.0f ? __fadd_rn(__fmul_rn(peak, inv127), 0.0f) : 1.0f;
+      *reinterpret_cast<uint2*>(q + row * D + sub * 8) = quant8(x[r], s);
+      if (sub == 0) sc[row] = s;
     }
-    uint2 packed;
-    packed.x = b[0] | (b[1] << 8) | (b[2] << 16) | (b[3] << 24);
-    packed.y = b[4] | (b[5] << 8) | (b[6] << 16) | (b[7] << 24);
-    *reinterpret_cast<uint2*>(q + row * D + sub * 8) = packed;
-    if (sub == 0) sc[row] = s;
   }
-  if (__any_sync(0xFFFFFFFFu, bad) && (threadIdx.x & 31) == 0) atomicOr(flag, 1u << side);
+  if (__any_sync(0xFFFFFFFFu, bad) && (threadIdx.x & 31) == 0) {
+    atomicOr(flag, 1u << side);
+    if (J.flag) atomicOr(J.flag, 1u << side);
+  }
 }
 
 // Generic shape: one warp per row, any D, any alignment, exact division.
@@ -133,7 +147,10 @@ __global__ void __launch_bounds__(256) k_int8_quantize_generic(const QuantJob* _
       q[row * D + d] = (uint8_t)quant_exact(dev::round_to<BF16>(dev::load_elem<IN_DT>(in, ib + d)), s);
     if (lane == 0) sc[row] = s;
   }
-  if (__any_sync(0xFFFFFFFFu, bad) && lane == 0) atomicOr(flag, 1u << side);
+  if (__any_sync(0xFFFFFFFFu, bad) && lane == 0) {
+    atomicOr(flag, 1u << side);
+    if (J.flag) atomicOr(J.flag, 1u << side);
+  }
 }
 
 template <int IN_DT>
@@ -146,13 +163,14 @@ static cudaError_t quantize_dispatch(const QuantJob* jobs, int n_jobs, uint64_t 
     uint64_t cap = 148ull * 16;  // enough CTAs to fill every SM several times
     return dim3((unsigned)(need < cap ? need : cap), (unsigned)(2 * n_jobs));
   };
+  constexpr int R = 4;
   if (vec_ok) {
     switch (D) {
-      case 16: k_int8_quantize<IN_DT, 2><<<grid_for(threads / 2), threads, 0, s>>>(jobs, rows, off, flag); return cudaGetLastError();
-      case 32: k_int8_quantize<IN_DT, 4><<<grid_for(threads / 4), threads, 0, s>>>(jobs, rows, off, flag); return cudaGetLastError();
-      case 64: k_int8_quantize<IN_DT, 8><<<grid_for(threads / 8), threads, 0, s>>>(jobs, rows, off, flag); return cudaGetLastError();
-      case 128: k_int8_quantize<IN_DT, 16><<<grid_for(threads / 16), threads, 0, s>>>(jobs, rows, off, flag); return cudaGetLastError();
-      case 256: k_int8_quantize<IN_DT, 32><<<grid_for(threads / 32), threads, 0, s>>>(jobs, rows, off, flag); return cudaGetLastError();
+      case 16: k_int8_quantize<IN_DT, 2, R><<<grid_for(threads / 2 * R), threads, 0, s>>>(jobs, rows, off, flag); return cudaGetLastError();
+      case 32: k_int8_quantize<IN_DT, 4, R><<<grid_for(threads / 4 * R), threads, 0, s>>>(jobs, rows, off, flag); return cudaGetLastError();
+      case 64: k_int8_quantize<IN_DT, 8, R><<<grid_for(threads / 8 * R), threads, 0, s>>>(jobs, rows, off, flag); return cudaGetLastError();
+      case 128: k_int8_quantize<IN_DT, 16, R><<<grid_for(threads / 16 * R), threads, 0, s>>>(jobs, rows, off, flag); return cudaGetLastError();
+      case 256: k_int8_quantize<IN_DT, 32, R><<<grid_for(threads / 32 * R), threads, 0, s>>>(jobs, rows, off, flag); return cudaGetLastError();
       default: break;
     }
   }

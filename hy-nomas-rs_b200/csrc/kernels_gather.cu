@@ -75,10 +75,12 @@ __global__ void __launch_bounds__(kGatherThreads) k_gather(const GatherArgs a) {
   const GatherTile tile = a.tiles[blockIdx.x];
   const int layer = blockIdx.y;
   const int side = blockIdx.z;
-  const GatherRun run = a.runs[tile.run];
+  const GatherRun& run = a.runs[tile.run];
   const int H = a.H, D = a.D;
   const int64_t HD = (int64_t)H * D;
   const unsigned char* base = run.src + (int64_t)layer * run.layer_stride;
+  const int64_t off_data = side ? run.off[1] : run.off[0];
+  const int64_t off_scale = side ? run.off[3] : run.off[2];
   void* out_base = side ? a.out_v[layer] : a.out_k[layer];
   const int64_t out_tok = (int64_t)tile.b * a.out_L + run.dst_tok + tile.tok0;
   const int64_t src_tok = (int64_t)tile.b * run.src_L + run.src_tok + tile.tok0;
@@ -89,8 +91,8 @@ __global__ void __launch_bounds__(kGatherThreads) k_gather(const GatherArgs a) {
   constexpr int U = 4;
 
   if (run.kind == RUN_INT8) {
-    const uint8_t* codes = base + run.off[side] + src_tok * HD;
-    const float* scales = reinterpret_cast<const float*>(base + run.off[2 + side]) + src_tok * H;
+    const uint8_t* codes = base + off_data + src_tok * HD;
+    const float* scales = reinterpret_cast<const float*>(base + off_scale) + src_tok * H;
     for (int c0 = threadIdx.x; c0 < n_chunks; c0 += kGatherThreads * U) {
       uint4 w[U];
       float s[U];
@@ -116,7 +118,7 @@ __global__ void __launch_bounds__(kGatherThreads) k_gather(const GatherArgs a) {
     }
   } else if (run.kind == RUN_FLOAT) {
     const size_t esz = OUT_DT == F32 ? 4 : 2;
-    const uint4* src = reinterpret_cast<const uint4*>(base + run.off[side] + src_tok * HD * esz);
+    const uint4* src = reinterpret_cast<const uint4*>(base + off_data + src_tok * HD * esz);
     uint4* dst = reinterpret_cast<uint4*>(static_cast<unsigned char*>(out_base) + out_tok * HD * esz);
     const int64_t n16 = (int64_t)tile.ntok * HD * esz / 16;
     for (int64_t c0 = threadIdx.x; c0 < n16; c0 += (int64_t)kGatherThreads * U) {
@@ -135,8 +137,8 @@ __global__ void __launch_bounds__(kGatherThreads) k_gather(const GatherArgs a) {
   } else {  // RUN_QVG_VIDEO
     const int stages = a.stages, bits = a.bits, E = 1 << bits;
     const int bpt = (stages * bits + 7) / 8;
-    const uint8_t* codes = base + run.off[side];
-    const float* scales = reinterpret_cast<const float*>(base + run.off[2 + side]);
+    const uint8_t* codes = base + off_data;
+    const float* scales = reinterpret_cast<const float*>(base + off_scale);
     const float* cb = a.cb + (int64_t)layer * a.cb_layer_stride + (int64_t)side * H * stages * E * D;
     const uint32_t mask = (1u << bits) - 1u;
     for (int c = threadIdx.x; c < n_chunks; c += kGatherThreads) {
@@ -179,10 +181,12 @@ __global__ void __launch_bounds__(kGatherThreads) k_gather_generic(const GatherA
   const GatherTile tile = a.tiles[blockIdx.x];
   const int layer = blockIdx.y;
   const int side = blockIdx.z;
-  const GatherRun run = a.runs[tile.run];
+  const GatherRun& run = a.runs[tile.run];
   const int H = a.H, D = a.D;
   const int64_t HD = (int64_t)H * D;
   const unsigned char* base = run.src + (int64_t)layer * run.layer_stride;
+  const int64_t off_data = side ? run.off[1] : run.off[0];
+  const int64_t off_scale = side ? run.off[3] : run.off[2];
   void* out_base = side ? a.out_v[layer] : a.out_k[layer];
   const int64_t out_tok = (int64_t)tile.b * a.out_L + run.dst_tok + tile.tok0;
   const int64_t src_tok = (int64_t)tile.b * run.src_L + run.src_tok + tile.tok0;
@@ -194,24 +198,24 @@ __global__ void __launch_bounds__(kGatherThreads) k_gather_generic(const GatherA
     const int d = (int)(rem - (int64_t)h * D);
     float v;
     if (run.kind == RUN_INT8) {
-      const uint8_t q = base[run.off[side] + (src_tok + t) * HD + rem];
-      const float sc = reinterpret_cast<const float*>(base + run.off[2 + side])[(src_tok + t) * H + h];
+      const uint8_t q = base[off_data + (src_tok + t) * HD + rem];
+      const float sc = reinterpret_cast<const float*>(base + off_scale)[(src_tok + t) * H + h];
       v = __fmul_rn(__fadd_rn((float)q, -128.0f), sc);
     } else if (run.kind == RUN_FLOAT) {
       const int64_t j = (src_tok + t) * HD + rem;
-      if constexpr (OUT_DT == F32) v = reinterpret_cast<const float*>(base + run.off[side])[j];
+      if constexpr (OUT_DT == F32) v = reinterpret_cast<const float*>(base + off_data)[j];
       else {
         reinterpret_cast<unsigned short*>(out_base)[(out_tok + t) * HD + rem] =
-            reinterpret_cast<const unsigned short*>(base + run.off[side])[j];
+            reinterpret_cast<const unsigned short*>(base + off_data)[j];
         continue;
       }
     } else {
       const int stages = a.stages, bits = a.bits, E = 1 << bits, bpt = (stages * bits + 7) / 8;
       const int64_t tok = src_tok + t;
-      const uint8_t* cp = base + run.off[side] + (tok * H + h) * bpt;
+      const uint8_t* cp = base + off_data + (tok * H + h) * bpt;
       uint64_t packed = 0;
       for (int b = 0; b < bpt; ++b) packed |= (uint64_t)cp[b] << (8 * b);
-      const float* al = reinterpret_cast<const float*>(base + run.off[2 + side]) +
+      const float* al = reinterpret_cast<const float*>(base + off_scale) +
                         ((int64_t)h * run.n_blocks + tok / a.block) * stages;
       const float* cb = a.cb + (int64_t)layer * a.cb_layer_stride + (int64_t)side * H * stages * E * D;
       v = 0.0f;

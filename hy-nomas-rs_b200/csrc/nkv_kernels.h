@@ -23,10 +23,11 @@ struct QuantJob {
   uint8_t* vq;
   float* ks;
   float* vs;
+  uint32_t* flag;  // this job's non-finite bits (may be null)
 };
 // in_row_offset: rows of the input skipped before the first quantized row
-// (QVG text tokens start after the video tokens).  Sets bit 0 (k) / bit 1
-// (v) of *flag when a non-finite value is seen.
+// (QVG text tokens start after the video tokens).  A non-finite value sets
+// bit 0 (k) / bit 1 (v) of *flag and of the job's own flag.
 // aligned16: every k/v/kq/vq pointer of every job is 16-byte aligned.
 cudaError_t launch_int8_quantize(const QuantJob* jobs_dev, int n_jobs, uint64_t rows, uint64_t in_row_offset,
                                  int64_t D, int in_dtype, bool aligned16, uint32_t* flag, cudaStream_t s);

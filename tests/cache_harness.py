@@ -205,6 +205,11 @@ class Pair:
                                              f"first {bad[:3].tolist()}")
             if archive:
                 self.check_archive(layer)
+            if self.spec.storage == nk.NKV_STORAGE_QVG:
+                cbo, cbp = self.o.codebooks(layer), lp.qvg_codebooks()
+                assert (cbo is None) == (cbp is None), f"layer {layer} fitted state differs"
+                if cbo is not None:
+                    assert np.array_equal(cbo.view(np.uint32), cbp.view(np.uint32)), f"layer {layer} codebooks"
 
     def check_archive(self, layer):
         g = self.geo

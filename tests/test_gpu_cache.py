@@ -158,7 +158,7 @@ def test_qvg_text_nonfinite_rejected_video_nan_accepted(H):
     assert p.commit() is None  # fits codebooks
 
     def nan_text(layer, side, h):
-        if layer == 1 and side == 1:
+        if layer == 0 and side == 1:
             h[0, 64 + 3, 0, 0] = np.nan  # a text token of V
 
     err = p.commit(poison=nan_text)
@@ -183,9 +183,9 @@ def test_qvg_failed_first_commit_keeps_fitted_codebooks(H):
 
     err = p.commit(poison=inf_text)
     assert err is not None and "non-finite k" in err.msg
-    for layer in range(p.geo.n_layers):
-        cbo, cbp = p.o.codebooks(layer), p.p.layer(layer).qvg_codebooks()
-        assert cbo is not None and cbp is not None and np.array_equal(cbo, cbp)
+    # layer 0 fitted before its text failed; layer 1 was never reached
+    assert p.o.codebooks(0) is not None and p.o.codebooks(1) is None
+    p.check()
     assert p.commit() is None
     p.check()
     p.close()
@@ -198,7 +198,7 @@ def test_nonfinite_rejection_leaves_cache_unchanged(H, storage):
     assert p.commit() is None
 
     def poison(layer, side, h):
-        if layer == 1 and side == 0:
+        if layer == 0 and side == 0:
             h[0, 17, 2, 5] = np.float32(np.finfo(np.float32).max)  # |x| >= f32::MAX (int8.rs:110-116)
 
     err = p.commit(poison=poison)
@@ -209,6 +209,27 @@ def test_nonfinite_rejection_leaves_cache_unchanged(H, storage):
     p.check()
     assert p.commit() is None
     p.check()
+    p.close()
+
+
+def test_bank_commit_is_all_or_nothing(H):
+    """Deliberate deviation: the reference's KvBank::commit (cache/mod.rs:
+    257-268) stops at the first failing layer and leaves the layers before it
+    committed; the bank rejects the segment on every layer.  The error itself
+    (kind and message) is the reference's."""
+    p = _pair(H, "int8", "uniform", past=6, model_dtype="bf16", input_dtype="f32")
+    assert p.commit() is None
+
+    def poison(layer, side, h):
+        if layer == 1 and side == 1:
+            h[0, 3, 0, 0] = np.nan
+
+    err = p.commit(poison=poison)
+    assert err is not None and err.msg == "cannot quantize non-finite v values"
+    assert p.o.info(0)["n_segments"] == 2 and p.o.info(1)["n_segments"] == 1  # reference: partial
+    for layer in range(2):
+        assert p.p.layer(layer).n_segments() == 1  # bank: unchanged
+    assert p.p.metrics().archived_segments == 1 and p.p.metrics().rebuilds == 1
     p.close()
 
 

@@ -1,0 +1,133 @@
+"""World-size-2 gloo test of the layer-sharded bank's host logic on CPU.
+
+Each rank owns half the layers.  The per-rank bank is the CPU oracle (the
+test injects it through ShardedKvBank's bank_factory), so the test checks
+the sharding logic itself: layer partition, descriptor agreement, error
+propagation across ranks, and that the all-reduced metrics equal a single
+unsharded KvBank's (cache/mod.rs:305-319)."""
+import os
+import sys
+
+import numpy as np
+import pytest
+import torch.multiprocessing as mp
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+class OracleShard:
+    """Oracle bank with the KvBank methods ShardedKvBank calls."""
+
+    def __init__(self, orc, cfg, begin, count, H, D):
+        self.orc, self.begin = orc, begin
+        self.bank = orc.Bank(cfg, count, 1, H, D, orc.F32)
+
+    def commit_tensors(self, desc, ks, vs):
+        import nomas_kv as nk
+        seg = dict(segment_index=desc.segment_index, frame_start=desc.frame_start, frame_count=desc.frame_count,
+                   image_tokens=desc.image_tokens, text_tokens=desc.text_tokens, action_start=desc.action_start)
+        try:
+            self.bank.commit(seg, self.orc.F32, ks, vs)
+        except self.orc.OracleError as e:
+            raise nk._ERRORS[e.code](e.msg)
+
+    def rollback(self):
+        self.bank.rollback()
+
+    def park_all(self):
+        self.bank.park()
+
+    def unpark_all(self):
+        self.bank.unpark()
+
+    def metrics(self):
+        return self.bank.metrics()
+
+    def close(self):
+        self.bank.close()
+
+
+def _inputs(seed, layer, seg, L, H, D):
+    from nomas_kv import synth
+    k = synth.host_values(seed, 0.5, 1, L, H, D, layer, seg, 0, 0)
+    v = synth.host_values(seed, 0.5, 1, L, H, D, layer, seg, 1, 0)
+    return k, v
+
+
+def _worker(rank, world, port, q):
+    try:
+        for p in (ROOT, os.path.join(ROOT, "oracle"), os.path.join(ROOT, "hy-nomas-rs_b200")):
+            sys.path.insert(0, p)
+        import torch.distributed as dist
+        from datetime import timedelta
+        import nomas_kv as nk
+        import oracle as orc
+        from nomas_kv.sharded import ShardedKvBank
+
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+        n_layers, H, D, tpf, frames, text = 4, 2, 16, 8, 2, 3
+        L = frames * tpf + text
+        ocfg = orc.Config(storage=orc.INT8, sampling=orc.UNIFORM, past_frames=3)
+        sb = ShardedKvBank(nk.CacheConfig(), n_layers, 1, H, D, 0,
+                           bank_factory=lambda b, c: OracleShard(orc, ocfg, b, c, H, D))
+        assert (sb.begin, sb.count) == nk.partition_layers(n_layers, world, rank)
+        for s in range(3):
+            desc = nk._abi.nkv_segment_desc(s, s * frames, frames, frames * tpf, text, -1)
+            kv = [_inputs(0, sb.begin + i, s, L, H, D) for i in range(sb.count)]
+            sb.commit(desc, [k for k, _ in kv], [v for _, v in kv])
+        m = sb.metrics().as_dict()
+        # the same session on one unsharded bank of all layers
+        full = orc.Bank(ocfg, n_layers, 1, H, D, orc.F32)
+        for s in range(3):
+            kv = [_inputs(0, l, s, L, H, D) for l in range(n_layers)]
+            full.commit(dict(segment_index=s, frame_start=s * frames, frame_count=frames, image_tokens=frames * tpf,
+                             text_tokens=text, action_start=-1), orc.F32, [k for k, _ in kv], [v for _, v in kv])
+        assert m == full.metrics(), (m, full.metrics())
+        sb.rollback()
+        full.rollback()
+        assert sb.metrics().as_dict() == full.metrics()
+        full.close()
+        # descriptor disagreement is caught on every rank
+        bad = nk._abi.nkv_segment_desc(2, 4 + rank, frames, frames * tpf, text, -1)
+        try:
+            sb.commit(bad, [], [])
+            raise AssertionError("disagreement not detected")
+        except nk.CacheStateError:
+            pass
+        # a non-finite input on rank 1 only: every rank reports the failure
+        desc = nk._abi.nkv_segment_desc(2, 4, frames, frames * tpf, text, -1)
+        kv = [_inputs(0, sb.begin + i, 2, L, H, D) for i in range(sb.count)]
+        if rank == 1:
+            kv[0][0][0, 1, 0, 0] = np.nan
+        try:
+            sb.commit(desc, [k for k, _ in kv], [v for _, v in kv])
+            raise AssertionError("failure not propagated")
+        except nk.NomasError as e:
+            assert e.code == nk.MsgError.code
+        sb.close()
+        dist.destroy_process_group()
+        q.put((rank, "ok"))
+    except BaseException as e:  # noqa: BLE001
+        import traceback
+        q.put((rank, f"fail: {e!r}\n{traceback.format_exc()}"))
+
+
+def test_sharded_bank_two_gloo_ranks():
+    import socket
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = {}
+    for _ in procs:
+        r, msg = q.get(timeout=240)
+        results[r] = msg
+    for p in procs:
+        p.join(timeout=60)
+    assert results == {0: "ok", 1: "ok"}, results
