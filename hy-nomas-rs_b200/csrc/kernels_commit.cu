@@ -119,6 +119,118 @@ __global__ void __launch_bounds__(256) k_int8_quantize(const QuantJob* __restric
   }
 }
 
+// ---------------------------------------------------------------------------
+// BF16 input, head_dim = 16 * G: the commit kernel of the 8B geometry.
+// G threads per (token, head) row, 16 values (two 16-byte loads) per thread,
+// R rows per thread in flight.  Per value the work is 1 FMUL + 3 FADD + 1
+// compare on the quotient plus a quarter byte-permute to pack:
+//  * |x| max runs on the raw 16-bit patterns (max.u16x2 on |bits|): for
+//    non-negative bf16 the integer order is the float order, and inf / NaN
+//    patterns (>= 0x7F80) sort above every finite value, so the same max
+//    also answers the reference's non-finite scan (no finite bf16 reaches
+//    f32::MAX, int8.rs:110-116);
+//  * y = x * rcp(s) is rounded to an integer by adding 1.5 * 2^23, whose
+//    low byte is then (round(y) + 128) mod 256 after an XOR with 0x80.
+//    |x / s| < 127.5 for every value of the row (x <= peak, s = peak * (1 +
+//    O(2^-23)) / 127), so the reference's clamp to [-127, 127] never binds;
+//  * a thread whose quotients include one within 1e-4 of a half-integer
+//    recomputes its 16 values with the exact division path.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t max_u16x2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("max.u16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+template <int G, int R>
+__global__ void __launch_bounds__(256) k_int8_quantize_bf16(const QuantJob* __restrict__ jobs, uint64_t rows,
+                                                            uint64_t in_row_offset, uint32_t* __restrict__ flag) {
+  constexpr int D = 16 * G;
+  const QuantJob J = jobs[blockIdx.y >> 1];
+  const int side = blockIdx.y & 1;
+  const uint4* in = reinterpret_cast<const uint4*>(side ? J.v : J.k);
+  uint4* q = reinterpret_cast<uint4*>(side ? J.vq : J.kq);
+  float* sc = side ? J.vs : J.ks;
+  const int sub = threadIdx.x % G;
+  const uint64_t rows_per_pass = blockDim.x / G;
+  const float inv127 = (float)(1.0 / 127.0);
+  const float M = 12582912.0f;  // 1.5 * 2^23
+  uint32_t worst = 0;           // max |bits| seen: >= 0x7F80 means inf / NaN
+  for (uint64_t base = (uint64_t)blockIdx.x * rows_per_pass * R; base < rows;
+       base += (uint64_t)gridDim.x * rows_per_pass * R) {
+    uint4 w[R][2];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const uint64_t row = base + r * rows_per_pass + threadIdx.x / G;
+      if (row < rows) {
+        const uint4* p = in + ((in_row_offset + row) * D + sub * 16) / 8;
+        w[r][0] = __ldg(p);
+        w[r][1] = __ldg(p + 1);
+      } else {
+        w[r][0] = w[r][1] = make_uint4(0, 0, 0, 0);
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const uint64_t row = base + r * rows_per_pass + threadIdx.x / G;
+      const uint32_t ws[8] = {w[r][0].x, w[r][0].y, w[r][0].z, w[r][0].w,
+                              w[r][1].x, w[r][1].y, w[r][1].z, w[r][1].w};
+      uint32_t m2 = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) m2 = max_u16x2(m2, ws[j] & 0x7FFF7FFFu);
+      uint32_t m = max(m2 & 0xFFFFu, m2 >> 16);
+#pragma unroll
+      for (int o = G / 2; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+      worst = max(worst, m);
+      if (row >= rows) continue;
+      const float peak = __uint_as_float(m << 16);
+      // scale = where(peak > 0, peak * (f32)(1/127) + 0, 1)   (int8.rs:72)
+      const float s = peak > 0.0f ? __fadd_rn(__fmul_rn(peak, inv127), 0.0f) : 1.0f;
+      uint32_t out[4];
+      bool exact = !(s >= FLT_MIN);
+      if (!exact) {
+        const float rc = __frcp_rn(s);
+        uint32_t t[16];
+        bool tie = false;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float x0 = __uint_as_float(ws[j] << 16), x1 = __uint_as_float(ws[j] & 0xFFFF0000u);
+          const float y0 = __fmul_rn(x0, rc), y1 = __fmul_rn(x1, rc);
+          const float a0 = __fadd_rn(y0, M), a1 = __fadd_rn(y1, M);
+          tie |= fabsf(__fadd_rn(y0, -__fadd_rn(a0, -M))) >= 0.4999f;
+          tie |= fabsf(__fadd_rn(y1, -__fadd_rn(a1, -M))) >= 0.4999f;
+          t[2 * j] = __float_as_uint(a0);
+          t[2 * j + 1] = __float_as_uint(a1);
+        }
+        exact = tie;
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          out[k] = __byte_perm(__byte_perm(t[4 * k], t[4 * k + 1], 0x0040), __byte_perm(t[4 * k + 2], t[4 * k + 3], 0x0040),
+                               0x5410) ^ 0x80808080u;
+      }
+      if (exact) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          uint32_t b[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const uint32_t h = (ws[2 * k + e / 2] >> (16 * (e & 1))) & 0xFFFFu;
+            b[e] = quant_exact(__uint_as_float(h << 16), s);
+          }
+          out[k] = b[0] | (b[1] << 8) | (b[2] << 16) | (b[3] << 24);
+        }
+      }
+      q[(row * D + sub * 16) / 16] = make_uint4(out[0], out[1], out[2], out[3]);
+      if (sub == 0) sc[row] = s;
+    }
+  }
+  const bool bad = worst >= 0x7F80u;
+  if (__any_sync(0xFFFFFFFFu, bad) && (threadIdx.x & 31) == 0) {
+    atomicOr(flag, 1u << side);
+    if (J.flag) atomicOr(J.flag, 1u << side);
+  }
+}
+
 // Generic shape: one warp per row, any D, any alignment, exact division.
 template <int IN_DT>
 __global__ void __launch_bounds__(256) k_int8_quantize_generic(const QuantJob* __restrict__ jobs, uint64_t rows,
@@ -163,6 +275,19 @@ static cudaError_t quantize_dispatch(const QuantJob* jobs, int n_jobs, uint64_t 
     uint64_t cap = 148ull * 16;  // enough CTAs to fill every SM several times
     return dim3((unsigned)(need < cap ? need : cap), (unsigned)(2 * n_jobs));
   };
+  if constexpr (IN_DT == BF16) {
+    constexpr int R2 = 2;
+    if (vec_ok) {
+      switch (D) {
+        case 16: k_int8_quantize_bf16<1, R2><<<grid_for(threads / 1 * R2), threads, 0, s>>>(jobs, rows, off, flag); return cudaGetLastError();
+        case 32: k_int8_quantize_bf16<2, R2><<<grid_for(threads / 2 * R2), threads, 0, s>>>(jobs, rows, off, flag); return cudaGetLastError();
+        case 64: k_int8_quantize_bf16<4, R2><<<grid_for(threads / 4 * R2), threads, 0, s>>>(jobs, rows, off, flag); return cudaGetLastError();
+        case 128: k_int8_quantize_bf16<8, R2><<<grid_for(threads / 8 * R2), threads, 0, s>>>(jobs, rows, off, flag); return cudaGetLastError();
+        case 256: k_int8_quantize_bf16<16, R2><<<grid_for(threads / 16 * R2), threads, 0, s>>>(jobs, rows, off, flag); return cudaGetLastError();
+        default: break;
+      }
+    }
+  }
   constexpr int R = 4;
   if (vec_ok) {
     switch (D) {

@@ -63,6 +63,21 @@ def _bits(a: np.ndarray) -> np.ndarray:
     return a.view(np.uint32) if a.dtype == np.float32 else a.view(np.uint16) if a.itemsize == 2 else a
 
 
+def _nan_mask(a: np.ndarray, kind: str) -> np.ndarray:
+    b = _bits(a)
+    if b.dtype == np.uint32:
+        return (b & 0x7FFFFFFF) > 0x7F800000
+    if kind == "f16":
+        return (b & 0x7FFF) > 0x7C00
+    return (b & 0x7FFF) > 0x7F80
+
+
+def same_values(a: np.ndarray, b: np.ndarray, kind: str = "bf16") -> np.ndarray:
+    """Element-wise equality of bit patterns, NaN == NaN whatever the payload
+    (x86 and the GPU propagate NaN payloads differently; positions must match)."""
+    return (_bits(a) == _bits(b)) | (_nan_mask(a, kind) & _nan_mask(b, kind))
+
+
 def torch_to_raw(t) -> np.ndarray:
     import torch
     if t.dtype == torch.float32:
@@ -199,8 +214,9 @@ class Pair:
                 kp, vp = torch_to_raw(kp), torch_to_raw(vp)
                 assert kp.shape == ko.shape and vp.shape == vo.shape
                 for a, b, name in ((ko, kp, "k"), (vo, vp, "v")):
-                    if not np.array_equal(_bits(a), _bits(b)):
-                        bad = np.argwhere(_bits(a) != _bits(b))
+                    eq = same_values(a, b, self.geo.model_dtype)
+                    if not eq.all():
+                        bad = np.argwhere(~eq)
                         raise AssertionError(f"layer {layer} working-set {name} differs at {len(bad)} places, "
                                              f"first {bad[:3].tolist()}")
             if archive:
@@ -239,7 +255,12 @@ class Pair:
             parts += [kq.ravel(), vq.ravel(), ks.view(np.uint8).ravel(), vs.view(np.uint8).ravel()]
         ref = np.concatenate([p.ravel() for p in parts])
         assert ref.size == blob.size, (ref.size, blob.size)
-        assert np.array_equal(ref, blob), f"layer {layer} segment {pos} qvg payload differs"
+        # codes bytewise; the f32 alphas NaN-equivalent
+        nc = kc.size + vc.size
+        ns = ksc.size + vsc.size
+        assert np.array_equal(ref[:nc], blob[:nc]), f"layer {layer} segment {pos} qvg codes differ"
+        assert same_values(ref[nc:nc + 4 * ns].view(np.float32), blob[nc:nc + 4 * ns].copy().view(np.float32)).all()
+        assert np.array_equal(ref[nc + 4 * ns:], blob[nc + 4 * ns:]), f"layer {layer} segment {pos} text differs"
 
     def close(self):
         if self.p is not None:

@@ -175,7 +175,10 @@ def test_qvg_text_nonfinite_rejected_video_nan_accepted(H):
 
 
 def test_qvg_failed_first_commit_keeps_fitted_codebooks(H):
-    p = _pair(H, "qvg", "uniform", past=6, model_dtype="bf16", input_dtype="f32", tpf=32, text=8, frames=2)
+    """history.rs:256-276: the fit runs before the text is quantized, so a
+    first commit rejected for its text still freezes the codebooks."""
+    p = _pair(H, "qvg", "uniform", past=6, model_dtype="bf16", input_dtype="f32", tpf=32, text=8, frames=2,
+              n_layers=1)
 
     def inf_text(layer, side, h):
         if layer == 0 and side == 0:
@@ -183,11 +186,26 @@ def test_qvg_failed_first_commit_keeps_fitted_codebooks(H):
 
     err = p.commit(poison=inf_text)
     assert err is not None and "non-finite k" in err.msg
-    # layer 0 fitted before its text failed; layer 1 was never reached
-    assert p.o.codebooks(0) is not None and p.o.codebooks(1) is None
+    assert p.o.codebooks(0) is not None
     p.check()
     assert p.commit() is None
     p.check()
+    p.close()
+
+
+def test_qvg_bank_fit_state_after_failed_first_commit(H):
+    """In KvBank's loop a commit failing at layer 0 never reaches layer 1's
+    fit; the bank drops the fits of the layers after the first failing one."""
+    p = _pair(H, "qvg", "uniform", past=6, model_dtype="bf16", input_dtype="f32", tpf=32, text=8, frames=2)
+
+    def inf_text(layer, side, h):
+        if layer == 0 and side == 0:
+            h[0, 70, 0, 0] = np.inf
+
+    assert p.commit(poison=inf_text) is not None
+    assert p.o.codebooks(0) is not None and p.o.codebooks(1) is None
+    assert p.p.layer(0).qvg_codebooks() is not None and p.p.layer(1).qvg_codebooks() is None
+    assert np.array_equal(p.o.codebooks(0), p.p.layer(0).qvg_codebooks())
     p.close()
 
 
@@ -250,7 +268,8 @@ def test_geometry_and_chronology_errors(H):
 
 
 def test_tokens_per_frame_recorded_by_failed_first_commit(H):
-    p = _pair(H, "int8", "uniform", past=6)
+    # one layer: in a multi-layer KvBank only the first layer would record it
+    p = _pair(H, "int8", "uniform", past=6, n_layers=1)
     assert p.commit(frame_start=2) is not None  # fails after learning tpf = 64
     assert p.commit(frames=2, image_tokens=100, frame_start=0) is not None  # tpf 50 != 64
     p.check()
@@ -270,13 +289,28 @@ def test_rollback_errors(H):
 
 
 def test_capacity_overflow_archives_then_errors(H):
-    p = _pair(H, "int8", "uniform", past=6, capacity=300)
+    """history.rs:416-421: the rebuild fails after the segment was archived."""
+    p = _pair(H, "int8", "uniform", past=6, capacity=300, n_layers=1)
     assert p.commit() is None
     err = p.commit()
     assert err is not None and "capacity is 300" in err.msg
     p.check()  # archive grew, working set and rebuild counter did not
     assert p.rollback() is None
     p.check()
+    p.close()
+
+
+def test_capacity_overflow_in_a_bank_archives_every_layer(H):
+    """KvBank stops after the first layer's rebuild error; the bank keeps its
+    layers in lockstep, so every layer holds the archived segment (each
+    layer exactly as the reference's HistoryCache leaves it)."""
+    p = _pair(H, "int8", "uniform", past=6, capacity=300)
+    assert p.commit() is None
+    err = p.commit()
+    assert err is not None and "capacity is 300" in err.msg
+    for layer in range(2):
+        assert p.p.layer(layer).n_segments() == 2 and p.p.layer(layer).total_frames() == 6
+    assert p.o.info(0)["n_segments"] == 2 and p.o.layer_metrics(0) == p.p.layer(0).metrics().as_dict()
     p.close()
 
 
