@@ -23,10 +23,11 @@ namespace nkv {
 // per row.
 //
 // Per value the reference computes round_half_away(x / s) with an IEEE
-// division.  The kernel multiplies by the correctly rounded reciprocal
-// instead (|error| <= 2^-23 relative, i.e. < 1.6e-5 absolute for |x/s| <=
-// 127.01) and rounds to nearest; only when that quotient lies within 1e-4 of
-// a half-integer, where the two could disagree, does it redo the value with
+// division.  The kernel multiplies by an approximate reciprocal instead
+// (rcp.approx: 1 ulp; with the product's rounding the quotient is within
+// 2.3e-5 of x / s for |x / s| <= 127.01, and the IEEE quotient within 7.6e-6)
+// and rounds to nearest; only when that quotient lies within 1e-4 of a
+// half-integer, where the two could disagree, does it redo the value with
 // __fdiv_rn + roundf.  Outside that band both quotients round to the same
 // integer, so the codes are identical to the division-based reference.
 // ---------------------------------------------------------------------------
@@ -38,28 +39,56 @@ __device__ __forceinline__ uint32_t quant_exact(float x, float s) {
   return dev::as_u8(t);
 }
 
+// The exact per-value path kept out of line: inlined, the compiler turns the
+// rarely taken branch into predicated code that every thread issues.
+__device__ __noinline__ uint2 quant8_exact(float4 lo, float4 hi, float s) {
+  const float x[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+  uint32_t b[8];
+  for (int j = 0; j < 8; ++j) b[j] = quant_exact(x[j], s);
+  return make_uint2(b[0] | (b[1] << 8) | (b[2] << 16) | (b[3] << 24), b[4] | (b[5] << 8) | (b[6] << 16) | (b[7] << 24));
+}
+
+// 16 bf16 values (8 words) of one row with scale s, exact path.
+__device__ __noinline__ uint4 quant16_bf16_exact(uint4 w0, uint4 w1, float s) {
+  const uint32_t ws[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+  uint32_t out[4];
+  for (int k = 0; k < 4; ++k) {
+    uint32_t b[4];
+    for (int e = 0; e < 4; ++e) {
+      const uint32_t h = (ws[2 * k + e / 2] >> (16 * (e & 1))) & 0xFFFFu;
+      b[e] = quant_exact(__uint_as_float(h << 16), s);
+    }
+    out[k] = b[0] | (b[1] << 8) | (b[2] << 16) | (b[3] << 24);
+  }
+  return make_uint4(out[0], out[1], out[2], out[3]);
+}
+
+// Approximate reciprocal (max error 1 ulp) for s in [FLT_MIN, 1e37]; the
+// callers' tie band (1e-4) is far wider than the error it introduces.
+__device__ __forceinline__ float rcp_approx(float s) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(s));
+  return r;
+}
+
 // 8 values of one row with scale s -> 8 packed code bytes (see above).
 __device__ __forceinline__ uint2 quant8(const float (&x)[8], float s) {
   uint32_t b[8];
-  if (s >= FLT_MIN) {
-    const float r = __frcp_rn(s);
+  bool exact = !(s >= FLT_MIN && s <= 1e37f);
+  const float r = rcp_approx(s);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float y = __fmul_rn(x[j], r);
-      // round to nearest integer (|y| < 2^22), then check the tie band
-      const float t = __fadd_rn(__fadd_rn(y, 12582912.0f), -12582912.0f);
-      if (fabsf(__fadd_rn(y, -t)) >= 0.4999f) {
-        b[j] = quant_exact(x[j], s);
-      } else {
-        const float c = fminf(fmaxf(t, -127.0f), 127.0f);
-        b[j] = __float_as_uint(__fadd_rn(c, 8388736.0f)) & 0xFFu;  // 2^23 + 128 + c -> low byte
-      }
-    }
-  } else {
-#pragma unroll
-    for (int j = 0; j < 8; ++j) b[j] = quant_exact(x[j], s);
+  for (int j = 0; j < 8; ++j) {
+    const float y = __fmul_rn(x[j], r);
+    // round to nearest integer (|y| < 2^22), then check the tie band
+    const float t = __fadd_rn(__fadd_rn(y, 12582912.0f), -12582912.0f);
+    exact |= fabsf(__fadd_rn(y, -t)) >= 0.4999f;
+    b[j] = __float_as_uint(__fadd_rn(t, 8388736.0f)) & 0xFFu;  // 2^23 + 128 + t -> low byte
   }
-  return make_uint2(b[0] | (b[1] << 8) | (b[2] << 16) | (b[3] << 24), b[4] | (b[5] << 8) | (b[6] << 16) | (b[7] << 24));
+  uint2 out = make_uint2(b[0] | (b[1] << 8) | (b[2] << 16) | (b[3] << 24), b[4] | (b[5] << 8) | (b[6] << 16) | (b[7] << 24));
+  if (__any_sync(__activemask(), exact)) {
+    if (exact) out = quant8_exact(make_float4(x[0], x[1], x[2], x[3]), make_float4(x[4], x[5], x[6], x[7]), s);
+  }
+  return out;
 }
 
 // R rows per thread and iteration: all R loads are issued before any of
@@ -187,9 +216,9 @@ __global__ void __launch_bounds__(256) k_int8_quantize_bf16(const QuantJob* __re
       // scale = where(peak > 0, peak * (f32)(1/127) + 0, 1)   (int8.rs:72)
       const float s = peak > 0.0f ? __fadd_rn(__fmul_rn(peak, inv127), 0.0f) : 1.0f;
       uint32_t out[4];
-      bool exact = !(s >= FLT_MIN);
-      if (!exact) {
-        const float rc = __frcp_rn(s);
+      bool exact = !(s >= FLT_MIN && s <= 1e37f);
+      {
+        const float rc = rcp_approx(s);
         uint32_t t[16];
         bool tie = false;
 #pragma unroll
@@ -202,25 +231,17 @@ __global__ void __launch_bounds__(256) k_int8_quantize_bf16(const QuantJob* __re
           t[2 * j] = __float_as_uint(a0);
           t[2 * j + 1] = __float_as_uint(a1);
         }
-        exact = tie;
+        exact |= tie;
 #pragma unroll
         for (int k = 0; k < 4; ++k)
           out[k] = __byte_perm(__byte_perm(t[4 * k], t[4 * k + 1], 0x0040), __byte_perm(t[4 * k + 2], t[4 * k + 3], 0x0040),
                                0x5410) ^ 0x80808080u;
       }
-      if (exact) {
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          uint32_t b[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const uint32_t h = (ws[2 * k + e / 2] >> (16 * (e & 1))) & 0xFFFFu;
-            b[e] = quant_exact(__uint_as_float(h << 16), s);
-          }
-          out[k] = b[0] | (b[1] << 8) | (b[2] << 16) | (b[3] << 24);
-        }
+      uint4 o = make_uint4(out[0], out[1], out[2], out[3]);
+      if (__any_sync(__activemask(), exact)) {
+        if (exact) o = quant16_bf16_exact(w[r][0], w[r][1], s);
       }
-      q[(row * D + sub * 16) / 16] = make_uint4(out[0], out[1], out[2], out[3]);
+      q[(row * D + sub * 16) / 16] = o;
       if (sub == 0) sc[row] = s;
     }
   }
