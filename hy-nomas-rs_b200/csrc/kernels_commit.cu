@@ -23,13 +23,14 @@ namespace nkv {
 // per row.
 //
 // Per value the reference computes round_half_away(x / s) with an IEEE
-// division.  The kernel multiplies by an approximate reciprocal instead
-// (rcp.approx: 1 ulp; with the product's rounding the quotient is within
-// 2.3e-5 of x / s for |x / s| <= 127.01, and the IEEE quotient within 7.6e-6)
-// and rounds to nearest; only when that quotient lies within 1e-4 of a
-// half-integer, where the two could disagree, does it redo the value with
-// __fdiv_rn + roundf.  Outside that band both quotients round to the same
-// integer, so the codes are identical to the division-based reference.
+// division.  The kernels get the same correctly rounded quotient without a
+// divide: with r = RN(1/s) (one IEEE reciprocal per row), q0 = RN(x * r),
+// the residual e = x - s * q0 computed exactly by an FMA, and
+// q1 = RN(q0 + e * r), Markstein's theorem gives q1 = RN(x / s) whenever the
+// quotient is in the normal range (a subnormal quotient rounds to 0 either
+// way).  Round-half-away-from-zero of q1 is then round-to-nearest-even by
+// the 1.5 * 2^23 magic constant, corrected on exact .5 ties by a select.
+// Rows whose scale is subnormal (or above 1e37) take the IEEE division.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t quant_exact(float x, float s) {
   float t = roundf(__fdiv_rn(x, s));
@@ -63,32 +64,33 @@ __device__ __noinline__ uint4 quant16_bf16_exact(uint4 w0, uint4 w1, float s) {
   return make_uint4(out[0], out[1], out[2], out[3]);
 }
 
-// Approximate reciprocal (max error 1 ulp) for s in [FLT_MIN, 1e37]; the
-// callers' tie band (1e-4) is far wider than the error it introduces.
-__device__ __forceinline__ float rcp_approx(float s) {
-  float r;
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(s));
-  return r;
+// Code of one value: (round_half_away(RN(x / s)) + 128) in the low byte of
+// the returned f32 bit pattern's 8 LSBs XOR 0x80 (see kernel notes); valid
+// for s in [FLT_MIN, 1e37] with r = RN(1/s).
+__device__ __forceinline__ uint32_t code_bits(float x, float s, float r) {
+  const float M = 12582912.0f;  // 1.5 * 2^23
+  const float q0 = __fmul_rn(x, r);
+  const float e = __fmaf_rn(-q0, s, x);
+  const float q1 = __fmaf_rn(e, r, q0);                  // RN(x / s)
+  const float t = __fadd_rn(__fadd_rn(q1, M), -M);       // round to nearest even
+  const float hv = __fadd_rn(q1, copysignf(0.5f, q1));   // exact on a .5 tie
+  const float f = fabsf(__fadd_rn(q1, -t)) == 0.5f ? hv : t;
+  return __float_as_uint(__fadd_rn(f, M));               // low byte: f mod 256
 }
 
-// 8 values of one row with scale s -> 8 packed code bytes (see above).
+__device__ __forceinline__ uint32_t pack4(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410) ^ 0x80808080u;
+}
+
+// 8 values of one row with scale s -> 8 packed code bytes.
 __device__ __forceinline__ uint2 quant8(const float (&x)[8], float s) {
-  uint32_t b[8];
-  bool exact = !(s >= FLT_MIN && s <= 1e37f);
-  const float r = rcp_approx(s);
+  if (!(s >= FLT_MIN && s <= 1e37f))
+    return quant8_exact(make_float4(x[0], x[1], x[2], x[3]), make_float4(x[4], x[5], x[6], x[7]), s);
+  const float r = __frcp_rn(s);
+  uint32_t c[8];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const float y = __fmul_rn(x[j], r);
-    // round to nearest integer (|y| < 2^22), then check the tie band
-    const float t = __fadd_rn(__fadd_rn(y, 12582912.0f), -12582912.0f);
-    exact |= fabsf(__fadd_rn(y, -t)) >= 0.4999f;
-    b[j] = __float_as_uint(__fadd_rn(t, 8388736.0f)) & 0xFFu;  // 2^23 + 128 + t -> low byte
-  }
-  uint2 out = make_uint2(b[0] | (b[1] << 8) | (b[2] << 16) | (b[3] << 24), b[4] | (b[5] << 8) | (b[6] << 16) | (b[7] << 24));
-  if (__any_sync(__activemask(), exact)) {
-    if (exact) out = quant8_exact(make_float4(x[0], x[1], x[2], x[3]), make_float4(x[4], x[5], x[6], x[7]), s);
-  }
-  return out;
+  for (int j = 0; j < 8; ++j) c[j] = code_bits(x[j], s, r);
+  return make_uint2(pack4(c[0], c[1], c[2], c[3]), pack4(c[4], c[5], c[6], c[7]));
 }
 
 // R rows per thread and iteration: all R loads are issued before any of
@@ -151,19 +153,16 @@ __global__ void __launch_bounds__(256) k_int8_quantize(const QuantJob* __restric
 // ---------------------------------------------------------------------------
 // BF16 input, head_dim = 16 * G: the commit kernel of the 8B geometry.
 // G threads per (token, head) row, 16 values (two 16-byte loads) per thread,
-// R rows per thread in flight.  Per value the work is 1 FMUL + 3 FADD + 1
-// compare on the quotient plus a quarter byte-permute to pack:
+// R rows per thread in flight, branch-free per value (code_bits above):
 //  * |x| max runs on the raw 16-bit patterns (max.u16x2 on |bits|): for
 //    non-negative bf16 the integer order is the float order, and inf / NaN
 //    patterns (>= 0x7F80) sort above every finite value, so the same max
 //    also answers the reference's non-finite scan (no finite bf16 reaches
 //    f32::MAX, int8.rs:110-116);
-//  * y = x * rcp(s) is rounded to an integer by adding 1.5 * 2^23, whose
-//    low byte is then (round(y) + 128) mod 256 after an XOR with 0x80.
-//    |x / s| < 127.5 for every value of the row (x <= peak, s = peak * (1 +
-//    O(2^-23)) / 127), so the reference's clamp to [-127, 127] never binds;
-//  * a thread whose quotients include one within 1e-4 of a half-integer
-//    recomputes its 16 values with the exact division path.
+//  * the rounded quotient is placed in the low byte of M + f (M = 1.5 * 2^23)
+//    and an XOR with 0x80 makes it (f + 128) mod 256.  |x / s| < 127.5 for
+//    every value of the row (x <= peak, s = peak * (1 + O(2^-23)) / 127), so
+//    the reference's clamp to [-127, 127] never binds.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t max_u16x2(uint32_t a, uint32_t b) {
   uint32_t d;
@@ -215,31 +214,19 @@ __global__ void __launch_bounds__(256) k_int8_quantize_bf16(const QuantJob* __re
       const float peak = __uint_as_float(m << 16);
       // scale = where(peak > 0, peak * (f32)(1/127) + 0, 1)   (int8.rs:72)
       const float s = peak > 0.0f ? __fadd_rn(__fmul_rn(peak, inv127), 0.0f) : 1.0f;
-      uint32_t out[4];
-      bool exact = !(s >= FLT_MIN && s <= 1e37f);
-      {
-        const float rc = rcp_approx(s);
-        uint32_t t[16];
-        bool tie = false;
+      uint4 o;
+      if (s >= FLT_MIN && s <= 1e37f) {
+        const float rc = __frcp_rn(s);
+        uint32_t c[16];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          const float x0 = __uint_as_float(ws[j] << 16), x1 = __uint_as_float(ws[j] & 0xFFFF0000u);
-          const float y0 = __fmul_rn(x0, rc), y1 = __fmul_rn(x1, rc);
-          const float a0 = __fadd_rn(y0, M), a1 = __fadd_rn(y1, M);
-          tie |= fabsf(__fadd_rn(y0, -__fadd_rn(a0, -M))) >= 0.4999f;
-          tie |= fabsf(__fadd_rn(y1, -__fadd_rn(a1, -M))) >= 0.4999f;
-          t[2 * j] = __float_as_uint(a0);
-          t[2 * j + 1] = __float_as_uint(a1);
+          c[2 * j] = code_bits(__uint_as_float(ws[j] << 16), s, rc);
+          c[2 * j + 1] = code_bits(__uint_as_float(ws[j] & 0xFFFF0000u), s, rc);
         }
-        exact |= tie;
-#pragma unroll
-        for (int k = 0; k < 4; ++k)
-          out[k] = __byte_perm(__byte_perm(t[4 * k], t[4 * k + 1], 0x0040), __byte_perm(t[4 * k + 2], t[4 * k + 3], 0x0040),
-                               0x5410) ^ 0x80808080u;
-      }
-      uint4 o = make_uint4(out[0], out[1], out[2], out[3]);
-      if (__any_sync(__activemask(), exact)) {
-        if (exact) o = quant16_bf16_exact(w[r][0], w[r][1], s);
+        o = make_uint4(pack4(c[0], c[1], c[2], c[3]), pack4(c[4], c[5], c[6], c[7]),
+                       pack4(c[8], c[9], c[10], c[11]), pack4(c[12], c[13], c[14], c[15]));
+      } else {
+        o = quant16_bf16_exact(w[r][0], w[r][1], s);
       }
       q[(row * D + sub * 16) / 16] = o;
       if (sub == 0) sc[row] = s;
