@@ -55,6 +55,11 @@ void check_dtype(int32_t dt) {
 }
 }  // namespace
 
+namespace nkv {
+// Lets entry points outside this file report through nkv_last_error().
+void set_abi_error(const std::string& msg) { g_last_error = msg; }
+}  // namespace nkv
+
 extern "C" {
 
 const char* nkv_last_error(void) { return g_last_error.c_str(); }

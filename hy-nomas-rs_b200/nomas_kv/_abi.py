@@ -26,6 +26,7 @@ NKV_SAMPLING_RECENT, NKV_SAMPLING_UNIFORM, NKV_SAMPLING_RECENT_MIX, NKV_SAMPLING
 NKV_KERNEL_QUANTIZE, NKV_KERNEL_FLOAT_ARCHIVE, NKV_KERNEL_QVG_ENCODE, NKV_KERNEL_GATHER = 0, 1, 2, 3
 NKV_KERNEL_COUNT = 4
 KERNEL_NAMES = ("quantize", "float_archive", "qvg_encode", "gather")
+NKV_NOALLOC_MAX_LAYERS = 64
 
 
 class nkv_qvg_config(C.Structure):
@@ -141,6 +142,9 @@ SIGNATURES = {
     "nkv_qvg_encode": (C.c_int, [P, I32, P, I32, U64, I64, I64, U64, I32, I32, I32, P, P, P]),
     "nkv_qvg_decode": (C.c_int, [P, I32, P, P, U64, I64, I64, I32, I32, I32, P, P]),
     "nkv_synth_fill": (C.c_int, [P, I32, U64, I64, I64, U64, U64, P, P, P]),
+    "nkv_int8_quantize_layers_noalloc": (C.c_int, [C.POINTER(P), C.POINTER(P), I32, I32, U64, I64, C.POINTER(P),
+                                                   C.POINTER(P), C.POINTER(P), C.POINTER(P),
+                                                   C.POINTER(C.c_uint32), P]),
 }
 
 _lib = None
