@@ -40,6 +40,9 @@ SEG_TOKENS = FRAMES * TPF + TEXT  # 6496
 PAST = 16
 ARCHIVED = 32
 METRIC = "KV commit+rebuild GB/s (8B geometry, INT8, uniform rebuild)"
+METRIC_QVG = "KV commit+rebuild GB/s (8B geometry, QVG, uniform rebuild)"
+WORKLOADS = {"int8": "nomas-8B INT8 commit + uniform rebuild (16 past frames) + newest segment",
+             "qvg": "nomas-8B QVG (frozen codebooks) commit + uniform decode-gather rebuild + newest segment"}
 # SURVEY 8(d) algorithmic bytes per token per layer: K+V BF16 read (12288) +
 # u8 codes and f32 scales written (6336) for a commit; the reverse for a
 # gathered output token.
@@ -52,11 +55,34 @@ def rebuild_tokens() -> int:
     return PAST * TPF + PAST * TEXT  # 29056
 
 
-def step_bytes(n_layers: int) -> dict:
-    commit = SEG_TOKENS * BYTES_PER_TOKEN * n_layers
-    rebuild = rebuild_tokens() * BYTES_PER_TOKEN * n_layers
-    recent = SEG_TOKENS * BYTES_PER_TOKEN * n_layers
+# QVG: per video token and layer 12,288 B read + 48 code
+# bytes + 12 scale bytes written = 12,348 B for an encode, the reverse for a
+# decode-gathered token (codebooks are cache-resident); text stays INT8.
+QVG_BYTES_PER_VIDEO_TOKEN = 2 * HEADS * HEAD_DIM * 2 + 2 * HEADS + 2 * HEADS * 4 * 4 // 64  # 12,348
+
+
+def step_bytes(n_layers: int, workload: str = "int8") -> dict:
+    if workload == "qvg":
+        video = FRAMES * TPF
+        commit = (video * QVG_BYTES_PER_VIDEO_TOKEN + TEXT * BYTES_PER_TOKEN) * n_layers
+        rebuild = (PAST * TPF * QVG_BYTES_PER_VIDEO_TOKEN + PAST * TEXT * BYTES_PER_TOKEN) * n_layers
+        recent = commit
+    else:
+        commit = SEG_TOKENS * BYTES_PER_TOKEN * n_layers
+        rebuild = rebuild_tokens() * BYTES_PER_TOKEN * n_layers
+        recent = SEG_TOKENS * BYTES_PER_TOKEN * n_layers
     return {"commit": commit, "rebuild": rebuild, "recent": recent, "total": commit + rebuild + recent}
+
+
+def qvg_codebooks(layer: int):
+    """Frozen synthetic codebooks of BASELINE configs[2]: per (layer, side,
+    head, stage) 4 codewords x 128 dims ~ N(0, sigma_s), sigma = 1, .5, .25, .125."""
+    import numpy as np
+    rng = np.random.default_rng(1000 + layer)
+    cb = np.zeros((2, HEADS, 4, 4, HEAD_DIM), np.float32)
+    for s, sig in enumerate((1.0, 0.5, 0.25, 0.125)):
+        cb[:, :, s] = rng.standard_normal((2, HEADS, 4, HEAD_DIM)).astype(np.float32) * np.float32(sig)
+    return cb
 
 
 def load_peaks() -> dict:
@@ -180,8 +206,13 @@ def run_gpu(args) -> None:
     model_layers = args.layers
     begin, n_layers = nk.partition_layers(model_layers, world, rank)
     stream = torch.cuda.current_stream(dev)
-    cfg = nk.CacheConfig(storage=nk.CacheStorage.int8(), sampling=nk.HistorySampling.uniform(), past_frames=PAST)
+    wl = args.workload
+    storage = nk.CacheStorage.qvg_() if wl == "qvg" else nk.CacheStorage.int8()
+    cfg = nk.CacheConfig(storage=storage, sampling=nk.HistorySampling.uniform(), past_frames=PAST)
     bank = nk.KvBank(cfg, n_layers, 1, HEADS, HEAD_DIM, torch.bfloat16, device=dev, layer_begin=begin)
+    if wl == "qvg":
+        for i in range(n_layers):
+            bank.layer(i).set_qvg_codebooks(qvg_codebooks(begin + i))
     gen = synth.DeviceGen(dev, seed=0, key_sigma=1.0)
     desc = lambda i: nk._abi.nkv_segment_desc(i, i * FRAMES, FRAMES, FRAMES * TPF, TEXT, 0)  # noqa: E731
 
@@ -243,7 +274,7 @@ def run_gpu(args) -> None:
     if world > 1:
         dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
     ms_max = float(ms_t.item())
-    bytes_all = step_bytes(model_layers)["total"] * args.steps
+    bytes_all = step_bytes(model_layers, wl)["total"] * args.steps
     value = bytes_all / (ms_max / 1e3) / 1e9
 
     # ---------------------------------------------------- timed: e2e (host buffers)
@@ -285,7 +316,7 @@ def run_gpu(args) -> None:
     ems = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(ems, op=dist.ReduceOp.MAX)
-    e2e_value = step_bytes(model_layers)["total"] * e2e_steps / (float(ems.item()) / 1e3) / 1e9
+    e2e_value = step_bytes(model_layers, wl)["total"] * e2e_steps / (float(ems.item()) / 1e3) / 1e9
     h2d = 2 * SEG_TOKENS * HEADS * HEAD_DIM * 2 * model_layers
     d2h = (4 + 4) * world  # commit's non-finite flag + the result read, per rank
 
@@ -293,11 +324,19 @@ def run_gpu(args) -> None:
     peaks = load_peaks()
     g_launch, g_ms = kst["gather"]
     q_launch, q_ms = kst["quantize"]
-    sb = step_bytes(n_layers)
+    e_launch, e_ms = kst["qvg_encode"]
+    sb = step_bytes(n_layers, wl)
     gather_bytes = (sb["rebuild"] + sb["recent"]) * args.steps
     gather_gbs = gather_bytes / (g_ms / 1e3) / 1e9 if g_ms > 0 else None
-    quant_gbs = sb["commit"] * args.steps / (q_ms / 1e3) / 1e9 if q_ms > 0 else None
-    launches = g_launch + q_launch
+    if wl == "qvg":
+        enc_bytes = FRAMES * TPF * QVG_BYTES_PER_VIDEO_TOKEN * n_layers * args.steps
+        txt_bytes = TEXT * BYTES_PER_TOKEN * n_layers * args.steps
+        quant_gbs = txt_bytes / (q_ms / 1e3) / 1e9 if q_ms > 0 else None
+        enc_gbs = enc_bytes / (e_ms / 1e3) / 1e9 if e_ms > 0 else None
+    else:
+        quant_gbs = sb["commit"] * args.steps / (q_ms / 1e3) / 1e9 if q_ms > 0 else None
+        enc_gbs = None
+    launches = g_launch + q_launch + e_launch
     traffic = None
     tp = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(tp):
@@ -312,10 +351,10 @@ def run_gpu(args) -> None:
 
     if rank == 0:
         out = {
-            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "metric": METRIC if wl == "int8" else METRIC_QVG, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "nomas-8B INT8 commit + uniform rebuild (16 past frames) + newest segment",
+            "config": {"workload": WORKLOADS[wl],
                        "layers": model_layers, "heads": HEADS, "head_dim": HEAD_DIM, "segment_tokens": SEG_TOKENS,
                        "tokens_per_frame": TPF, "frames_per_segment": FRAMES, "text_tokens": TEXT,
                        "past_frames": PAST, "archived_segments_at_first_timed_step": prefill + args.warmup + 1,
@@ -327,7 +366,9 @@ def run_gpu(args) -> None:
                          "traffic": traffic, "kernel": "k_gather (rebuild + newest segment)",
                          "peak_src": peaks["src"], "launches": g_launch,
                          "quantize_gbs": round(quant_gbs, 1) if quant_gbs else None,
-                         "quantize_frac": round(quant_gbs / peaks["hbm_gbs"], 4) if quant_gbs else None},
+                         "quantize_frac": round(quant_gbs / peaks["hbm_gbs"], 4) if quant_gbs else None,
+                         "qvg_encode_gbs": round(enc_gbs, 1) if enc_gbs else None,
+                         "qvg_encode_frac": round(enc_gbs / peaks["hbm_gbs"], 4) if enc_gbs else None},
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "steps": e2e_steps},
             "gpu_launches": launches,
@@ -364,6 +405,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--workload", default="int8", choices=["int8", "qvg"],
+                    help="int8 = BASELINE configs[1] (the headline); qvg = configs[2]")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="model layers (48 = the 8B geometry; fewer only for small profiling cases)")
     args = ap.parse_args()

@@ -24,7 +24,7 @@ BUILD = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "nomas_kv", "libnomas_kv.so")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
-SOURCES = ["kernels_commit.cu", "kernels_gather.cu", "bank.cpp", "abi.cpp", "qvg_fit.cpp", "noalloc.cu"]
+SOURCES = ["kernels_commit.cu", "kernels_gather.cu", "kernels_qvg.cu", "bank.cpp", "abi.cpp", "qvg_fit.cpp", "noalloc.cu"]
 HEADERS = ["nkv_kernels.h", "nkv_device.cuh", "nkv_policy.h", "nkv_qvg_fit.h", "bank.h"]
 
 # -fmad=false / -ffp-contract=off: the reference rounds every multiply and

@@ -317,8 +317,9 @@ int nkv_qvg_encode(const float* cb_dev, int32_t side, const void* x, int32_t in_
     nkv::QvgEncodeJob* d_job = nullptr;
     nkv::check_cuda(cudaMallocAsync(reinterpret_cast<void**>(&d_job), sizeof(job), s), "cudaMallocAsync");
     nkv::check_cuda(cudaMemcpyAsync(d_job, &job, sizeof(job), cudaMemcpyHostToDevice, s), "cudaMemcpyAsync");
+    const bool aligned = (reinterpret_cast<uintptr_t>(x) & 15u) == 0;
     nkv::check_cuda(nkv::launch_qvg_encode(d_job, 1, in_dtype, L, int(heads), int(head_dim), tokens, stages, bits,
-                                           block, s),
+                                           block, aligned, s),
                     "qvg encode launch");
     nkv::check_cuda(cudaFreeAsync(d_job, s), "cudaFreeAsync");
     nkv::check_cuda(cudaStreamSynchronize(s), "cudaStreamSynchronize");

@@ -623,7 +623,7 @@ void Bank::commit(const nkv_segment_desc& s, int kv_dtype, const void* const* k,
     } else {
       tbegin(NKV_KERNEL_QVG_ENCODE);
       NKV_CUDA(launch_qvg_encode(static_cast<const QvgEncodeJob*>(stg_.dev(jobs_off)), 2 * n_layers_, kv_dtype, L,
-                                 int(H_), int(D_), s.image_tokens, q_stages_, q_bits_, q_block_, stream_));
+                                 int(H_), int(D_), s.image_tokens, q_stages_, q_bits_, q_block_, in_aligned, stream_));
       tend(NKV_KERNEL_QVG_ENCODE);
       if (s.text_tokens > 0) {
         tbegin(NKV_KERNEL_QUANTIZE);

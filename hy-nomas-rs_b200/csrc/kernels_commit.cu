@@ -470,8 +470,11 @@ static size_t qvg_encode_smem(int D, int block, int E) {
 }
 
 cudaError_t launch_qvg_encode(const QvgEncodeJob* jobs_dev, int n_jobs, int in_dtype, uint64_t L, int H, int D,
-                              uint64_t tokens, int stages, int bits, int block, cudaStream_t s) {
+                              uint64_t tokens, int stages, int bits, int block, bool aligned16, cudaStream_t s) {
   if (tokens == 0 || n_jobs == 0 || H == 0) return cudaSuccess;
+  cudaError_t fast_err = cudaSuccess;
+  if (launch_qvg_encode_d128(jobs_dev, n_jobs, in_dtype, H, D, tokens, stages, bits, block, aligned16, s, &fast_err))
+    return fast_err;
   const int E = 1 << bits;
   const size_t smem = qvg_encode_smem(D, block, E);
   const uint64_t n_blocks = (tokens + block - 1) / block;

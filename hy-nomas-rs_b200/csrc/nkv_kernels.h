@@ -50,8 +50,13 @@ struct QvgEncodeJob {
   float* scales;    // [H][n_blocks][stages]
   const float* cb;  // [H][stages][E][D]
 };
+// aligned16: every job's input is 16-byte aligned (enables the d128 kernel).
 cudaError_t launch_qvg_encode(const QvgEncodeJob* jobs_dev, int n_jobs, int in_dtype, uint64_t L, int H, int D,
-                              uint64_t tokens, int stages, int bits, int block, cudaStream_t s);
+                              uint64_t tokens, int stages, int bits, int block, bool aligned16, cudaStream_t s);
+// The specialised encoder of kernels_qvg.cu (2 bits, head_dim 128, block 64,
+// <= 4 stages, aligned inputs); false when the shape does not qualify.
+bool launch_qvg_encode_d128(const QvgEncodeJob* jobs_dev, int n_jobs, int in_dtype, int H, int D, uint64_t tokens,
+                            int stages, int bits, int block, bool aligned16, cudaStream_t s, cudaError_t* err);
 // Dynamic shared memory the encode kernel needs (the bank rejects configs
 // above the per-CTA limit at creation).
 size_t qvg_encode_smem_bytes(int D, int block, int bits);

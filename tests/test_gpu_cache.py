@@ -125,6 +125,17 @@ def test_qvg_fit_on_first_commit_matches_oracle(H):
     p.close()
 
 
+@pytest.mark.parametrize("input_dtype", ["bf16", "f32"])
+def test_qvg_head_dim_128_fast_encoder_in_the_bank(H, input_dtype):
+    """head_dim 128 with the default codec takes the screened d128 encoder."""
+    p = _pair(H, "qvg", "uniform", past=4, model_dtype="bf16", input_dtype=input_dtype, heads=2, head_dim=128,
+              tpf=40, frames=2, text=5)
+    for _ in range(3):
+        assert p.commit() is None
+        p.check()
+    p.close()
+
+
 def test_qvg_frozen_codebooks_and_partial_blocks(H):
     """Frozen synthetic codebooks (BASELINE config 3 style), a last block of
     fewer than 64 tokens, and the sigma_s = 1, .5, .25, .125 stage scales."""

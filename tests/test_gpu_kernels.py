@@ -189,3 +189,34 @@ def test_qvg_ties_and_degenerate_blocks(orc, nkv, torch):
     x = np.zeros((1, 70, H, D), np.float32)
     x[0, :35] = 1.0
     _qvg_pair(orc, nkv, torch, x, cb, 0, 70)
+
+
+def test_qvg_d128_fast_path_ties_nan_and_extremes(orc, nkv, torch):
+    """head_dim 128 / 2 bits / block 64 takes the screened encoder; duplicate
+    codewords force its exact path, NaN rows and extreme magnitudes its
+    fallbacks."""
+    H, D = 3, 128
+    rng = np.random.default_rng(9)
+    cb = (rng.standard_normal((2, H, 4, 4, D)) * 0.5).astype(np.float32)
+    cb[:, 0, :, 3] = cb[:, 0, :, 1]  # head 0: entries 1 and 3 identical
+    cb[:, 1, 2, :] = 0.25  # head 1, stage 2: all four entries identical
+    x = rng.standard_normal((1, 200, H, D)).astype(np.float32)
+    x[0, 10, 2, 7] = np.nan
+    x[0, 70:75, 2] *= 1e30
+    x[0, 80:85, 1] *= 1e-30
+    x[0, 130:140, 0] = cb[0, 0, 0, 1] + cb[0, 0, 1, 1]  # exactly on codewords
+    for side in (0, 1):
+        cbs = np.ascontiguousarray(cb)
+        _, L, _, _ = x.shape
+        codes_r, scales_r = orc.qvg_encode(cbs, side, x, 196)
+        cbd = _dev(torch, cbs)
+        xd = _dev(torch, np.ascontiguousarray(x))
+        codes = torch.zeros(196 * H, dtype=torch.uint8, device="cuda")
+        scales = torch.zeros(H * 4 * 4, dtype=torch.float32, device="cuda")
+        rc = nkv.lib().nkv_qvg_encode(_ptr(cbd), side, _ptr(xd), 0, L, H, D, 196, 4, 2, 64, _ptr(codes), _ptr(scales),
+                                      None)
+        assert rc == 0, nkv.lib().nkv_last_error()
+        assert np.array_equal(codes.cpu().numpy(), codes_r)
+        s = scales.cpu().numpy()
+        same = (s.view(np.uint32) == scales_r.view(np.uint32)) | (np.isnan(s) & np.isnan(scales_r))
+        assert same.all()
