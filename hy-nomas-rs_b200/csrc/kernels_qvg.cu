@@ -18,7 +18,8 @@
 // codewords, NaN) the thread computes the reference's sequential f64
 // distances exactly.  Step 2 is the reference's computation itself: products
 // of f32 values are exact in f64, so the FMA chain in d order reproduces its
-// rounding.  Step 3 is two f32 roundings, as in the reference.
+// rounding.  Step 3 is two f32 roundings, as in the reference (scalar
+// instructions: see the update below).
 //
 // One CTA of 64 threads per (layer x side, head, group of blocks); thread t
 // owns token t of the current block, its residual in registers.
@@ -198,13 +199,16 @@ __global__ void __launch_bounds__(QB, 6) k_qvg_encode_d128(const QvgEncodeJob* _
       }
       __syncthreads();
       if (active) {
-        const float na = -sm.alpha;
-        const float2 na2 = make_float2(na, na);
+        const float alpha = sm.alpha;
         const float* ec = sm.e32[s][c];
+        // r - f32(alpha * e) with two roundings (qvg.rs:232-237).  Scalar on
+        // purpose: a packed f32x2 multiply feeding a packed add was found
+        // contracted into one fused rounding even with explicit .rn.
 #pragma unroll
         for (int k = 0; k < QD / 2; ++k) {
           const float2 e2 = *reinterpret_cast<const float2*>(&ec[2 * k]);
-          r[k] = __fadd2_rn(r[k], __fmul2_rn(na2, e2));  // r - f32(alpha * e)
+          r[k].x = __fsub_rn(r[k].x, __fmul_rn(alpha, e2.x));
+          r[k].y = __fsub_rn(r[k].y, __fmul_rn(alpha, e2.y));
         }
         packed |= (uint32_t)c << (2 * s);
       }
