@@ -322,12 +322,16 @@ def run_gpu(args) -> None:
 
     # ---------------------------------------------------- roofline (gather)
     peaks = load_peaks()
+    # the dominant launch is the rebuild gather of each commit; the newest-
+    # segment decode runs the same kernel and is reported beside it
     g_launch, g_ms = kst["gather"]
+    d_launch, d_ms = kst["segment_decode"]
     q_launch, q_ms = kst["quantize"]
     e_launch, e_ms = kst["qvg_encode"]
     sb = step_bytes(n_layers, wl)
-    gather_bytes = (sb["rebuild"] + sb["recent"]) * args.steps
+    gather_bytes = sb["rebuild"] * args.steps
     gather_gbs = gather_bytes / (g_ms / 1e3) / 1e9 if g_ms > 0 else None
+    dec_gbs = sb["recent"] * args.steps / (d_ms / 1e3) / 1e9 if d_ms > 0 else None
     if wl == "qvg":
         enc_bytes = FRAMES * TPF * QVG_BYTES_PER_VIDEO_TOKEN * n_layers * args.steps
         txt_bytes = TEXT * BYTES_PER_TOKEN * n_layers * args.steps
@@ -336,18 +340,28 @@ def run_gpu(args) -> None:
     else:
         quant_gbs = sb["commit"] * args.steps / (q_ms / 1e3) / 1e9 if q_ms > 0 else None
         enc_gbs = None
-    launches = g_launch + q_launch + e_launch
+    launches = g_launch + d_launch + q_launch + e_launch
+    # DRAM bytes of one rebuild-gather launch, from an ncu capture of the
+    # same kernel (scaled from the captured layer count to this one)
     traffic = None
     tp = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(tp):
-        traffic = json.load(open(tp)).get("gather_bytes_per_launch")
+        t = json.load(open(tp)).get(f"{wl}_rebuild_gather")
+        if t:
+            traffic = int(t["dram_bytes"] / t["layers"] * n_layers)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         try:
             cpu = cpu_sample(min(os.cpu_count() or 1, 8))
+            one = cpu_sample(1)
+            cpu["single_thread_value"] = one["value"]
+            cpu["single_thread_sample"] = one["sample"]
         except Exception as e:  # noqa: BLE001
             cpu = {"value": None, "unit": "GB/s", "cores": 0, "kind": "port", "sample": f"failed: {e}"}
+    sec = ms_max / 1e3
+    tok = {"commit": round(SEG_TOKENS * args.steps / sec), "rebuild_out": round(rebuild_tokens() * args.steps / sec),
+           "newest_segment_out": round(SEG_TOKENS * args.steps / sec), "unit": "segment tokens/s (all layers)"}
 
     if rank == 0:
         out = {
@@ -358,13 +372,17 @@ def run_gpu(args) -> None:
                        "layers": model_layers, "heads": HEADS, "head_dim": HEAD_DIM, "segment_tokens": SEG_TOKENS,
                        "tokens_per_frame": TPF, "frames_per_segment": FRAMES, "text_tokens": TEXT,
                        "past_frames": PAST, "archived_segments_at_first_timed_step": prefill + args.warmup + 1,
-                       "working_set_tokens": rebuild_tokens(), "bytes_per_step": step_bytes(model_layers)["total"],
+                       "working_set_tokens": rebuild_tokens(), "bytes_per_step": step_bytes(model_layers, wl)["total"],
                        "parallelism": f"layer-sharded x{world}", "l2": "inputs 3.8 GB per step > 126 MB L2"},
+            "tokens_per_s": tok,
             "roofline": {"bound": "hbm", "achieved": round(gather_gbs, 1) if gather_gbs else None,
                          "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": round(gather_gbs / peaks["hbm_gbs"], 4) if gather_gbs else None,
-                         "traffic": traffic, "kernel": "k_gather (rebuild + newest segment)",
+                         "traffic": traffic, "kernel": "k_gather (rebuild launch of each commit)",
+                         "algorithmic_bytes_per_launch": sb["rebuild"],
                          "peak_src": peaks["src"], "launches": g_launch,
+                         "segment_decode_gbs": round(dec_gbs, 1) if dec_gbs else None,
+                         "segment_decode_frac": round(dec_gbs / peaks["hbm_gbs"], 4) if dec_gbs else None,
                          "quantize_gbs": round(quant_gbs, 1) if quant_gbs else None,
                          "quantize_frac": round(quant_gbs / peaks["hbm_gbs"], 4) if quant_gbs else None,
                          "qvg_encode_gbs": round(enc_gbs, 1) if enc_gbs else None,

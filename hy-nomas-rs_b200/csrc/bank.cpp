@@ -428,7 +428,7 @@ void Bank::add_runs(const Plan& plan, size_t& runs_off, size_t& tiles_off, int& 
 }
 
 void Bank::launch_gather_into(size_t runs_off, size_t tiles_off, int n_tiles, size_t outk_off, size_t outv_off,
-                              uint64_t out_L, bool vector_ok, const uint32_t* abort_flag) {
+                              uint64_t out_L, bool vector_ok, const uint32_t* abort_flag, int timing_id) {
   if (n_tiles == 0) return;
   GatherArgs a{};
   a.runs = static_cast<const GatherRun*>(stg_.dev(runs_off));
@@ -445,9 +445,9 @@ void Bank::launch_gather_into(size_t runs_off, size_t tiles_off, int n_tiles, si
   a.stages = q_stages_, a.bits = q_bits_, a.block = q_block_;
   a.abort_flag = abort_flag;
   const bool hd_ok = ((H_ * D_) % 16) == 0;
-  tbegin(NKV_KERNEL_GATHER);
+  tbegin(timing_id);
   NKV_CUDA(launch_gather(a, vector_ok && hd_ok, stream_));
-  tend(NKV_KERNEL_GATHER);
+  tend(timing_id);
 }
 
 size_t Bank::ws_plane_bytes(uint64_t cap) const { return align_up(size_t(B_) * cap * H_ * D_ * dtype_size(dtype_)); }
@@ -473,6 +473,9 @@ void Bank::ensure_ws(uint64_t tokens, unsigned char** fresh, uint64_t* fresh_cap
 
 std::vector<int> Bank::fit_qvg(const nkv_segment_desc& s, int kv_dtype, const void* const* k, const void* const* v) {
   std::vector<int> fitted_now;
+  bool all_fitted = true;
+  for (int i = 0; i < n_layers_; ++i) all_fitted &= fitted_[i] != 0;
+  if (all_fitted) return fitted_now;  // the usual case: no host staging at all
   const size_t L = s.image_tokens + s.text_tokens, n = L * H_ * D_;
   const size_t esz = dtype_size(kv_dtype);
   std::vector<unsigned char> raw(n * esz);
@@ -845,7 +848,8 @@ void Bank::decode_segment(uint64_t pos, void* const* k_out, void* const* v_out) 
   const size_t outk_off = stg_.add(k_out, n_layers_ * sizeof(void*));
   const size_t outv_off = stg_.add(v_out, n_layers_ * sizeof(void*));
   stg_.upload(stream_);
-  launch_gather_into(runs_off, tiles_off, n_tiles, outk_off, outv_off, p.valid, aligned, nullptr);
+  launch_gather_into(runs_off, tiles_off, n_tiles, outk_off, outv_off, p.valid, aligned, nullptr,
+                     NKV_KERNEL_SEGMENT_DECODE);
 }
 
 void Bank::synchronize() {

@@ -143,7 +143,8 @@ class Bank {
   void add_runs(const Plan& plan, size_t& runs_off, size_t& tiles_off, int& n_tiles, bool& aligned);
   std::vector<int> fit_qvg(const nkv_segment_desc& s, int kv_dtype, const void* const* k, const void* const* v);
   void launch_gather_into(size_t runs_off, size_t tiles_off, int n_tiles, size_t outk_off, size_t outv_off,
-                          uint64_t out_L, bool vector_ok, const uint32_t* abort_flag);
+                          uint64_t out_L, bool vector_ok, const uint32_t* abort_flag,
+                          int timing_id = NKV_KERNEL_GATHER);
   void ensure_ws(uint64_t tokens, unsigned char** fresh, uint64_t* fresh_cap);
   unsigned char* ws_plane(unsigned char* base, uint64_t cap, int layer, int side) const;
   size_t ws_plane_bytes(uint64_t cap) const;

@@ -144,8 +144,9 @@ enum {
   NKV_KERNEL_QUANTIZE = 0,      /* INT8 commit: quantize K/V + non-finite scan       */
   NKV_KERNEL_FLOAT_ARCHIVE = 1, /* FLOAT commit: dtype conversion into the archive   */
   NKV_KERNEL_QVG_ENCODE = 2,    /* QVG commit: residual VQ encode of video tokens    */
-  NKV_KERNEL_GATHER = 3,        /* rebuild / decode_segment: gather + dequant/decode */
-  NKV_KERNEL_COUNT = 4
+  NKV_KERNEL_GATHER = 3,        /* rebuild: gather + dequant/decode                  */
+  NKV_KERNEL_SEGMENT_DECODE = 4, /* nkv_bank_decode_segment: the same gather kernel  */
+  NKV_KERNEL_COUNT = 5
 };
 
 typedef struct nkv_bank nkv_bank;
