@@ -386,10 +386,15 @@ Plan Bank::plan_rebuild() {
 }
 
 // Device run/tile tables for a plan, appended to the staging area.
-void Bank::add_runs(const Plan& plan, size_t& runs_off, size_t& tiles_off, int& n_tiles, bool& aligned) {
+GatherTables Bank::add_runs(const Plan& plan, bool outputs_aligned) {
   constexpr int64_t kTile = 32;
   std::vector<GatherRun> runs;
   std::vector<GatherTile> tiles;
+  std::vector<GatherQvgTile> qtiles;
+  // video runs of the default codec go to the table-driven decoder: tiles of
+  // <= 64 tokens inside one payload block (one alpha per head and stage)
+  const bool qvg_fast = cfg_.storage == NKV_STORAGE_QVG && qvg_gather_fast_ok(int(H_), int(D_), q_stages_, q_bits_) &&
+                        B_ == 1 && outputs_aligned;
   runs.reserve(plan.runs.size());
   for (const auto& rs : plan.runs) {
     const Rec& r = archive_[rs.rec];
@@ -417,23 +422,40 @@ void Bank::add_runs(const Plan& plan, size_t& runs_off, size_t& tiles_off, int& 
     }
     const int32_t run_id = int32_t(runs.size());
     runs.push_back(g);
+    if (g.kind == RUN_QVG_VIDEO && qvg_fast) {
+      const int64_t blk_tokens = q_block_;
+      for (int64_t t0 = 0; t0 < rs.ntok;) {
+        const int64_t tok = rs.src_tok + t0;
+        const int64_t blk = tok / blk_tokens;
+        const int64_t end = std::min<int64_t>({rs.ntok, (blk + 1) * blk_tokens - rs.src_tok, t0 + kQvgTileTokens});
+        qtiles.push_back({run_id, int32_t(t0), int32_t(end - t0), int32_t(blk)});
+        t0 = end;
+      }
+      continue;
+    }
     for (int64_t b = 0; b < B_; ++b)
       for (int64_t t0 = 0; t0 < rs.ntok; t0 += kTile)
         tiles.push_back({run_id, int32_t(b), int32_t(t0), int32_t(std::min<int64_t>(kTile, rs.ntok - t0))});
   }
-  aligned = true;  // slabs, components and working-set planes are 256-byte aligned
-  runs_off = stg_.add(runs.data(), runs.size() * sizeof(GatherRun));
-  tiles_off = stg_.add(tiles.data(), tiles.size() * sizeof(GatherTile));
-  n_tiles = int(tiles.size());
+  GatherTables t;
+  t.aligned = true;  // slabs, components and working-set planes are 256-byte aligned
+  t.runs_off = stg_.add(runs.data(), runs.size() * sizeof(GatherRun));
+  t.tiles_off = stg_.add(tiles.data(), tiles.size() * sizeof(GatherTile));
+  t.n_tiles = int(tiles.size());
+  t.qtiles_off = stg_.add(qtiles.data(), qtiles.size() * sizeof(GatherQvgTile));
+  t.n_qtiles = int(qtiles.size());
+  return t;
 }
 
-void Bank::launch_gather_into(size_t runs_off, size_t tiles_off, int n_tiles, size_t outk_off, size_t outv_off,
-                              uint64_t out_L, bool vector_ok, const uint32_t* abort_flag, int timing_id) {
-  if (n_tiles == 0) return;
+void Bank::launch_gather_into(const GatherTables& t, size_t outk_off, size_t outv_off, uint64_t out_L,
+                              bool vector_ok, const uint32_t* abort_flag, int timing_id) {
+  if (t.n_tiles + t.n_qtiles == 0) return;
   GatherArgs a{};
-  a.runs = static_cast<const GatherRun*>(stg_.dev(runs_off));
-  a.tiles = static_cast<const GatherTile*>(stg_.dev(tiles_off));
-  a.n_tiles = n_tiles;
+  a.runs = static_cast<const GatherRun*>(stg_.dev(t.runs_off));
+  a.tiles = static_cast<const GatherTile*>(stg_.dev(t.tiles_off));
+  a.n_tiles = t.n_tiles;
+  a.qtiles = static_cast<const GatherQvgTile*>(stg_.dev(t.qtiles_off));
+  a.n_qtiles = t.n_qtiles;
   a.n_layers = n_layers_;
   a.out_k = static_cast<void* const*>(stg_.dev(outk_off));
   a.out_v = static_cast<void* const*>(stg_.dev(outv_off));
@@ -597,14 +619,13 @@ void Bank::commit(const nkv_segment_desc& s, int kv_dtype, const void* const* k,
       text_jobs_off = stg_.add(tj.data(), tj.size() * sizeof(QuantJob));
     }
 
-    size_t runs_off = 0, tiles_off = 0, outk_off = 0, outv_off = 0;
-    int n_tiles = 0;
-    bool runs_aligned = true;
+    size_t outk_off = 0, outv_off = 0;
+    GatherTables gt;
     if (plan_ok && plan.valid > 0) {
       ensure_ws(plan.valid, &fresh, &fresh_cap);
       unsigned char* base = fresh ? fresh : ws_;
       const uint64_t cap = fresh ? fresh_cap : ws_cap_;
-      add_runs(plan, runs_off, tiles_off, n_tiles, runs_aligned);
+      gt = add_runs(plan);
       std::vector<void*> ok(n_layers_), ov(n_layers_);
       for (int i = 0; i < n_layers_; ++i) ok[i] = ws_plane(base, cap, i, 0), ov[i] = ws_plane(base, cap, i, 1);
       outk_off = stg_.add(ok.data(), ok.size() * sizeof(void*));
@@ -636,7 +657,7 @@ void Bank::commit(const nkv_segment_desc& s, int kv_dtype, const void* const* k,
         tend(NKV_KERNEL_QUANTIZE);
       }
     }
-    if (n_tiles > 0) launch_gather_into(runs_off, tiles_off, n_tiles, outk_off, outv_off, plan.valid, runs_aligned, d_flag_);
+    if (gt.n_tiles + gt.n_qtiles > 0) launch_gather_into(gt, outk_off, outv_off, plan.valid, gt.aligned, d_flag_);
     NKV_CUDA(cudaMemcpyAsync(h_flag_, d_flag_, sizeof(uint32_t) * (n_layers_ + 1), cudaMemcpyDeviceToHost,
                              stream_));
     NKV_CUDA(cudaStreamSynchronize(stream_));
@@ -699,10 +720,7 @@ void Bank::rebuild_now() {
   if (plan.valid > 0) {
     ensure_ws(plan.valid, &fresh, &fresh_cap);
     stg_.begin();
-    size_t runs_off, tiles_off;
-    int n_tiles;
-    bool aligned;
-    add_runs(plan, runs_off, tiles_off, n_tiles, aligned);
+    const GatherTables gt = add_runs(plan);
     unsigned char* base = fresh ? fresh : ws_;
     const uint64_t cap = fresh ? fresh_cap : ws_cap_;
     std::vector<void*> ok(n_layers_), ov(n_layers_);
@@ -711,7 +729,7 @@ void Bank::rebuild_now() {
     const size_t outv_off = stg_.add(ov.data(), ov.size() * sizeof(void*));
     stg_.upload(stream_);
     try {
-      launch_gather_into(runs_off, tiles_off, n_tiles, outk_off, outv_off, plan.valid, aligned, nullptr);
+      launch_gather_into(gt, outk_off, outv_off, plan.valid, gt.aligned, nullptr);
     } catch (...) {
       if (fresh) cudaFree(fresh);
       throw;
@@ -840,16 +858,14 @@ void Bank::decode_segment(uint64_t pos, void* const* k_out, void* const* v_out) 
   }
   p.valid = uint64_t(Lv + Lt);
   stg_.begin();
-  size_t runs_off, tiles_off;
-  int n_tiles;
-  bool aligned;
-  add_runs(p, runs_off, tiles_off, n_tiles, aligned);
+  bool aligned = true;
   for (int i = 0; i < n_layers_; ++i) aligned &= aligned16(k_out[i]) && aligned16(v_out[i]);
+  const GatherTables gt = add_runs(p, aligned);
+  aligned &= gt.aligned;
   const size_t outk_off = stg_.add(k_out, n_layers_ * sizeof(void*));
   const size_t outv_off = stg_.add(v_out, n_layers_ * sizeof(void*));
   stg_.upload(stream_);
-  launch_gather_into(runs_off, tiles_off, n_tiles, outk_off, outv_off, p.valid, aligned, nullptr,
-                     NKV_KERNEL_SEGMENT_DECODE);
+  launch_gather_into(gt, outk_off, outv_off, p.valid, aligned, nullptr, NKV_KERNEL_SEGMENT_DECODE);
 }
 
 void Bank::synchronize() {

@@ -107,6 +107,13 @@ struct Plan {
   uint64_t valid = 0;
 };
 
+// Staging offsets of one gather's device tables.
+struct GatherTables {
+  size_t runs_off = 0, tiles_off = 0, qtiles_off = 0;
+  int n_tiles = 0, n_qtiles = 0;
+  bool aligned = true;
+};
+
 class Bank {
  public:
   Bank(const nkv_cache_config& cfg, int n_layers, int layer_begin, int64_t batch, int64_t heads, int64_t head_dim,
@@ -140,11 +147,10 @@ class Bank {
   Rec make_rec(const nkv_segment_desc& s) const;
   void validate(const nkv_segment_desc& s, int kv_dtype, const void* const* k, const void* const* v);
   Plan plan_rebuild();
-  void add_runs(const Plan& plan, size_t& runs_off, size_t& tiles_off, int& n_tiles, bool& aligned);
+  GatherTables add_runs(const Plan& plan, bool outputs_aligned = true);
   std::vector<int> fit_qvg(const nkv_segment_desc& s, int kv_dtype, const void* const* k, const void* const* v);
-  void launch_gather_into(size_t runs_off, size_t tiles_off, int n_tiles, size_t outk_off, size_t outv_off,
-                          uint64_t out_L, bool vector_ok, const uint32_t* abort_flag,
-                          int timing_id = NKV_KERNEL_GATHER);
+  void launch_gather_into(const GatherTables& t, size_t outk_off, size_t outv_off, uint64_t out_L, bool vector_ok,
+                          const uint32_t* abort_flag, int timing_id = NKV_KERNEL_GATHER);
   void ensure_ws(uint64_t tokens, unsigned char** fresh, uint64_t* fresh_cap);
   unsigned char* ws_plane(unsigned char* base, uint64_t cap, int layer, int side) const;
   size_t ws_plane_bytes(uint64_t cap) const;

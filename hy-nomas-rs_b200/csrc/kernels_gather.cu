@@ -228,8 +228,128 @@ __global__ void __launch_bounds__(kGatherThreads) k_gather_generic(const GatherA
   }
 }
 
+// ---------------------------------------------------------------------------
+// Table-driven QVG video decode (qvg.rs:259-300) for the default codec
+// (4 stages x 2 bits, head_dim 128).  Inside one 64-token payload block the
+// alphas are fixed, so per (block, head) the reference's decode
+//   out = (((+0 + a0 e0[c0]) + a1 e1[c1]) + a2 e2[c2]) + a3 e3[c3]
+// (every product and sum rounded to f32, in this order) takes its first two
+// steps from a 16-row table Q01[c0][c1] = RN(RN(+0 + RN(a0 e0[c0])) + RN(a1 e1[c1]))
+// and the last two from P2[c2] = RN(a2 e2[c2]) and P3[c3] = RN(a3 e3[c3]):
+// three shared-memory reads and two adds per value instead of four
+// codebook reads, four multiplies and four adds.  The tables are built with
+// the same f32 operations, so every output is bit-identical.
+//
+// CTA: one tile (<= 64 tokens of one block) x kQvgHeads heads x (layer, side);
+// 8 threads per (token, head) row, thread l handles float4 columns l, l+8,
+// l+16, l+24 so each quarter-warp reads 128 contiguous bytes per table row.
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr int kQvgHeads = 4;
+constexpr int kQvgThreads = 256;
+constexpr int kQD = 128;
+
+struct QvgTables {
+  float q01[kQvgHeads][16][kQD];
+  float p2[kQvgHeads][4][kQD];
+  float p3[kQvgHeads][4][kQD];
+};  // 48 KB
+
+template <int OUT_DT>
+__device__ __forceinline__ void store4(void* out, uint64_t i, float a, float b, float c, float d) {
+  if constexpr (OUT_DT == F32) {
+    *reinterpret_cast<float4*>(static_cast<float*>(out) + i) = make_float4(a, b, c, d);
+  } else {
+    uint32_t w0, w1;
+    if constexpr (OUT_DT == BF16) {
+      w0 = (dev::bf16_bits(a) & 0xFFFFu) | (dev::bf16_bits(b) << 16);
+      w1 = (dev::bf16_bits(c) & 0xFFFFu) | (dev::bf16_bits(d) << 16);
+    } else {
+      w0 = (dev::f16_bits(a) & 0xFFFFu) | (dev::f16_bits(b) << 16);
+      w1 = (dev::f16_bits(c) & 0xFFFFu) | (dev::f16_bits(d) << 16);
+    }
+    *reinterpret_cast<uint2*>(static_cast<unsigned short*>(out) + i) = make_uint2(w0, w1);
+  }
+}
+
+}  // namespace
+
+template <int OUT_DT>
+__global__ void __launch_bounds__(kQvgThreads) k_gather_qvg(const GatherArgs a) {
+  if (a.abort_flag && *a.abort_flag) return;
+  __shared__ __align__(16) QvgTables T;
+  const GatherQvgTile tile = a.qtiles[blockIdx.x];
+  const int layer = (int)(blockIdx.z >> 1), side = (int)(blockIdx.z & 1);
+  const int H = a.H;
+  const int h0 = (int)blockIdx.y * kQvgHeads;
+  const int nh = min(kQvgHeads, H - h0);
+  const GatherRun& run = a.runs[tile.run];
+  const unsigned char* base = run.src + (int64_t)layer * run.layer_stride;
+  const uint8_t* codes = base + (side ? run.off[1] : run.off[0]);
+  const float* scales = reinterpret_cast<const float*>(base + (side ? run.off[3] : run.off[2]));
+  const float* cb = a.cb + (int64_t)layer * a.cb_layer_stride + (int64_t)side * H * 16 * kQD;
+
+  // ---- tables of this block's alpha-scaled codewords, thread per (head, d)
+  for (int i = threadIdx.x; i < nh * kQD; i += kQvgThreads) {
+    const int hh = i / kQD, d = i % kQD, h = h0 + hh;
+    const float* al = scales + ((int64_t)h * run.n_blocks + tile.blk) * 4;
+    const float* e = cb + (int64_t)h * 16 * kQD + d;  // [stage][entry][d]
+    const float a0 = __ldg(al), a1 = __ldg(al + 1), a2 = __ldg(al + 2), a3 = __ldg(al + 3);
+    float p0[4], p1[4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      p0[c] = __fadd_rn(0.0f, __fmul_rn(a0, __ldg(e + (0 * 4 + c) * kQD)));  // out = +0, out += a0 e0
+      p1[c] = __fmul_rn(a1, __ldg(e + (1 * 4 + c) * kQD));
+      T.p2[hh][c][d] = __fmul_rn(a2, __ldg(e + (2 * 4 + c) * kQD));
+      T.p3[hh][c][d] = __fmul_rn(a3, __ldg(e + (3 * 4 + c) * kQD));
+    }
+#pragma unroll
+    for (int c0 = 0; c0 < 4; ++c0)
+#pragma unroll
+      for (int c1 = 0; c1 < 4; ++c1) T.q01[hh][c0 * 4 + c1][d] = __fadd_rn(p0[c0], p1[c1]);
+  }
+  __syncthreads();
+
+  // ---- decode: 8 threads per (token, head) row
+  const int grp = threadIdx.x >> 3, l8 = threadIdx.x & 7;
+  const int n_items = tile.ntok * nh;
+  const int64_t src0 = run.src_tok + tile.tok0;
+  const int64_t dst0 = run.dst_tok + tile.tok0;  // batch 1
+  void* out = side ? a.out_v[layer] : a.out_k[layer];
+  for (int it = grp; it < n_items; it += kQvgThreads / 8) {
+    const int t = it / nh, hh = it - t * nh, h = h0 + hh;
+    const uint32_t code = __ldg(codes + (src0 + t) * H + h);  // stage s at bits 2s, 2s+1
+    const float* q = T.q01[hh][(code & 3u) * 4 + ((code >> 2) & 3u)];
+    const float* r2 = T.p2[hh][(code >> 4) & 3u];
+    const float* r3 = T.p3[hh][(code >> 6) & 3u];
+    const uint64_t ob = ((uint64_t)(dst0 + t) * H + h) * kQD;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int d = 4 * l8 + 32 * j;
+      const float4 x = *reinterpret_cast<const float4*>(q + d);
+      const float4 y = *reinterpret_cast<const float4*>(r2 + d);
+      const float4 z = *reinterpret_cast<const float4*>(r3 + d);
+      store4<OUT_DT>(out, ob + d, __fadd_rn(__fadd_rn(x.x, y.x), z.x), __fadd_rn(__fadd_rn(x.y, y.y), z.y),
+                     __fadd_rn(__fadd_rn(x.z, y.z), z.z), __fadd_rn(__fadd_rn(x.w, y.w), z.w));
+    }
+  }
+}
+
 cudaError_t launch_gather(const GatherArgs& a, bool vector_ok, cudaStream_t s) {
-  if (a.n_tiles == 0 || a.n_layers == 0) return cudaSuccess;
+  if (a.n_layers == 0) return cudaSuccess;
+  if (a.n_qtiles > 0) {
+    if (!vector_ok || a.D != kQD || a.n_layers > 32767) return cudaErrorInvalidValue;
+    dim3 qgrid((unsigned)a.n_qtiles, (unsigned)((a.H + kQvgHeads - 1) / kQvgHeads), (unsigned)(2 * a.n_layers));
+    switch (a.out_dtype) {
+      case F32: k_gather_qvg<F32><<<qgrid, kQvgThreads, 0, s>>>(a); break;
+      case BF16: k_gather_qvg<BF16><<<qgrid, kQvgThreads, 0, s>>>(a); break;
+      default: k_gather_qvg<F16><<<qgrid, kQvgThreads, 0, s>>>(a); break;
+    }
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  if (a.n_tiles == 0) return cudaSuccess;
   dim3 grid((unsigned)a.n_tiles, (unsigned)a.n_layers, 2);
   const bool vec = vector_ok && (a.D % 16) == 0;
   switch (a.out_dtype) {

@@ -91,10 +91,29 @@ struct GatherTile {
   int32_t ntok;
 };
 
+// Work unit of the table-driven QVG decoder: `ntok` (<= kQvgTileTokens)
+// video tokens of run `run` starting `tok0` tokens into it, all inside the
+// payload block `blk` (so one alpha per head and stage); batch is 1.
+struct GatherQvgTile {
+  int32_t run;
+  int32_t tok0;
+  int32_t ntok;
+  int32_t blk;
+};
+constexpr int kQvgTileTokens = 64;
+
+// The table-driven decoder handles the reference's default codec shape:
+// 4 stages of 2 bits (one code byte per token and head), head_dim 128.
+inline bool qvg_gather_fast_ok(int H, int D, int stages, int bits) {
+  return D == 128 && stages == 4 && bits == 2 && H >= 1;
+}
+
 struct GatherArgs {
   const GatherRun* runs;
   const GatherTile* tiles;
   int32_t n_tiles;
+  const GatherQvgTile* qtiles;  // QVG video tiles for k_gather_qvg
+  int32_t n_qtiles;
   int32_t n_layers;
   void* const* out_k;  // [n_layers] output bases (device array)
   void* const* out_v;
@@ -112,7 +131,9 @@ struct GatherArgs {
 };
 
 // vector_ok: all run sources and outputs are 16-byte aligned (the kernel
-// additionally needs head_dim % 16 == 0 for its vector path).
+// additionally needs head_dim % 16 == 0 for its vector path).  QVG video
+// tiles (a.qtiles) need vector_ok (the host only builds them for aligned
+// outputs); without it they are an argument error.
 cudaError_t launch_gather(const GatherArgs& a, bool vector_ok, cudaStream_t s);
 
 // ------------------------------------------------------- standalone ops ---

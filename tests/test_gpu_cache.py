@@ -472,3 +472,81 @@ def test_decode_segment_matches_oracle(H):
                 assert np.array_equal(H.torch_to_raw(ko[layer]), kr)
                 assert np.array_equal(H.torch_to_raw(vo[layer]), vr)
         p.close()
+
+
+def _sigma_codebooks(p, seed):
+    rng = np.random.default_rng(seed)
+    cbs = []
+    for _ in range(p.geo.n_layers):
+        cb = np.zeros((2, p.geo.heads, 4, 4, p.geo.head_dim), np.float32)
+        for s, sig in enumerate((1.0, 0.5, 0.25, 0.125)):
+            cb[:, :, s] = rng.standard_normal(cb[:, :, s].shape).astype(np.float32) * np.float32(sig)
+        cbs.append(cb)
+    return cbs
+
+
+@pytest.mark.parametrize("model_dtype", ["bf16", "f16", "f32"])
+def test_qvg_table_gather_d128_ragged_heads_and_blocks(H, model_dtype):
+    """head_dim 128 with the default codec takes the table-driven decoder:
+    6 heads (a group of 4 and a group of 2), 100-token frames so frame runs
+    start and end inside 64-token payload blocks, frozen codebooks."""
+    p = _pair(H, "qvg", "uniform", past=4, model_dtype=model_dtype, input_dtype="bf16", heads=6, head_dim=128,
+              tpf=100, frames=3, text=9)
+    p.set_codebooks(_sigma_codebooks(p, 11))
+    for _ in range(4):
+        assert p.commit() is None
+        p.check()
+    p.close()
+
+
+@pytest.mark.parametrize("sampling", ["recent_mix", "temporal09"])
+def test_qvg_table_gather_d128_fitted_codebooks(H, sampling):
+    p = _pair(H, "qvg", sampling, past=4, model_dtype="bf16", input_dtype="f32", heads=5, head_dim=128,
+              tpf=70, frames=2, text=6)
+    for _ in range(5):
+        assert p.commit() is None
+        p.check()
+    assert p.rollback() is None
+    p.check()
+    p.close()
+
+
+def test_qvg_table_gather_d128_video_nan(H):
+    p = _pair(H, "qvg", "uniform", past=4, model_dtype="bf16", input_dtype="f32", heads=4, head_dim=128,
+              tpf=64, frames=2, text=4)
+    p.set_codebooks(_sigma_codebooks(p, 3))
+
+    def nan_video(layer, side, h):
+        if side == 0:
+            h[0, 70, 3, 100] = np.nan
+            h[0, 5, 0, :] = np.inf
+
+    assert p.commit(poison=nan_video) is None
+    p.check()
+    assert p.commit() is None
+    p.check()
+    p.close()
+
+
+def test_qvg_decode_segment_d128_aligned_and_unaligned_outputs(H):
+    """Aligned caller buffers take the table-driven decoder, unaligned ones
+    the element-wise kernel; both must equal the oracle."""
+    import torch
+    p = _pair(H, "qvg", "uniform", past=4, model_dtype="bf16", input_dtype="bf16", heads=4, head_dim=128,
+              tpf=90, frames=2, text=5)
+    for _ in range(3):
+        assert p.commit() is None
+    L = 2 * 90 + 5
+    n = L * 4 * 128
+    for offset in (0, 1):
+        ko = [torch.empty(n + offset, dtype=torch.bfloat16, device="cuda")[offset:].view(1, L, 4, 128)
+              for _ in range(2)]
+        vo = [torch.empty(n + offset, dtype=torch.bfloat16, device="cuda")[offset:].view(1, L, 4, 128)
+              for _ in range(2)]
+        for pos in range(3):
+            p.p.decode_segment(pos, ko, vo)
+            for layer in range(2):
+                kr, vr = p.o.decode_segment(layer, pos, L)
+                assert np.array_equal(H.torch_to_raw(ko[layer]), kr), (offset, pos, layer)
+                assert np.array_equal(H.torch_to_raw(vo[layer]), vr), (offset, pos, layer)
+    p.close()
