@@ -234,32 +234,50 @@ __global__ void __launch_bounds__(kGatherThreads) k_gather_generic(const GatherA
 // alphas are fixed, so per (block, head) the reference's decode
 //   out = (((+0 + a0 e0[c0]) + a1 e1[c1]) + a2 e2[c2]) + a3 e3[c3]
 // (every product and sum rounded to f32, in this order) takes its first two
-// steps from a 16-row table Q01[c0][c1] = RN(RN(+0 + RN(a0 e0[c0])) + RN(a1 e1[c1]))
-// and the last two from P2[c2] = RN(a2 e2[c2]) and P3[c3] = RN(a3 e3[c3]):
-// three shared-memory reads and two adds per value instead of four
-// codebook reads, four multiplies and four adds.  The tables are built with
-// the same f32 operations, so every output is bit-identical.
+// steps from a 16-row table Q01[c0][c1] = RN(RN(+0 + RN(a0 e0[c0])) + RN(a1 e1[c1])),
+// the third from P2[c2] = RN(a2 e2[c2]) and the last from P3[c3] =
+// RN(a3 e3[c3]).  The tables are built with the same f32 operations, so
+// every output is bit-identical.  Q01 and P2 live in shared memory; P3 lives
+// in registers: warp w always serves head w % 4 and lane l always columns
+// 4l..4l+3, so its 4 x 4 P3 values are fixed and three selects pick the row.
+// Per value that is 8 bytes of shared-memory reads (the kernel's limit)
+// instead of 16 bytes of codebook rows through L1.
 //
 // CTA: one tile (<= 64 tokens of one block) x kQvgHeads heads x (layer, side);
-// 8 threads per (token, head) row, thread l handles float4 columns l, l+8,
-// l+16, l+24 so each quarter-warp reads 128 contiguous bytes per table row.
+// warp w decodes tokens w / 4, w / 4 + 2, ... of head w % 4, one 128-value
+// row per warp instruction.
 // ---------------------------------------------------------------------------
 namespace {
 
 constexpr int kQvgHeads = 4;
 constexpr int kQvgThreads = 256;
 constexpr int kQD = 128;
+static_assert(kQvgThreads == 2 * kQvgHeads * 32, "two warps per head");
 
 struct QvgTables {
-  float q01[kQvgHeads][16][kQD];
-  float p2[kQvgHeads][4][kQD];
-  float p3[kQvgHeads][4][kQD];
-};  // 48 KB
+  float q01[kQvgHeads][16][kQD];              // 32 KB
+  float p2[kQvgHeads][4][kQD];                // 8 KB
+  uint8_t code[kQvgTileTokens * kQvgHeads];   // the tile's packed codes, [token][head slot]
+};  // 40.25 KB (dynamic shared memory)
 
-template <int OUT_DT>
+__device__ __forceinline__ bool finite_f32(float v) { return (__float_as_uint(v) & 0x7FFFFFFFu) < 0x7F800000u; }
+
+// FAST: no value can be NaN, so the hardware pair converters give the same
+// bits as the integer rounding.
+template <int OUT_DT, bool FAST>
 __device__ __forceinline__ void store4(void* out, uint64_t i, float a, float b, float c, float d) {
   if constexpr (OUT_DT == F32) {
     *reinterpret_cast<float4*>(static_cast<float*>(out) + i) = make_float4(a, b, c, d);
+  } else if constexpr (FAST) {
+    uint32_t w0, w1;
+    if constexpr (OUT_DT == BF16) {
+      w0 = dev::bf16x2_bits_nonnan(a, b);
+      w1 = dev::bf16x2_bits_nonnan(c, d);
+    } else {
+      w0 = dev::f16x2_bits_nonnan(a, b);
+      w1 = dev::f16x2_bits_nonnan(c, d);
+    }
+    *reinterpret_cast<uint2*>(static_cast<unsigned short*>(out) + i) = make_uint2(w0, w1);
   } else {
     uint32_t w0, w1;
     if constexpr (OUT_DT == BF16) {
@@ -273,12 +291,36 @@ __device__ __forceinline__ void store4(void* out, uint64_t i, float a, float b, 
   }
 }
 
+// P3 row c of this lane's 4 columns, by three selects (no local memory).
+__device__ __forceinline__ float4 pick4(const float4 (&p)[4], uint32_t c) {
+  const bool b0 = c & 1u, b1 = c & 2u;
+  const float4 lo = b0 ? p[1] : p[0];
+  const float4 hi = b0 ? p[3] : p[2];
+  return b1 ? hi : lo;
+}
+
+template <int OUT_DT, bool FAST>
+__device__ __forceinline__ void decode_rows(void* out, const QvgTables& T, const float4 (&p3)[4], int ntok,
+                                            int64_t dst0, int H, int h, int hh, int tpar, int lane) {
+  const int d = 4 * lane;
+  for (int t = tpar; t < ntok; t += 2) {
+    const uint32_t code = T.code[t * kQvgHeads + hh];  // stage s at bits 2s, 2s+1
+    const float4 x = *reinterpret_cast<const float4*>(&T.q01[hh][(code & 3u) * 4 + ((code >> 2) & 3u)][d]);
+    const float4 y = *reinterpret_cast<const float4*>(&T.p2[hh][(code >> 4) & 3u][d]);
+    const float4 z = pick4(p3, code >> 6);
+    store4<OUT_DT, FAST>(out, ((uint64_t)(dst0 + t) * H + h) * kQD + d, __fadd_rn(__fadd_rn(x.x, y.x), z.x),
+                         __fadd_rn(__fadd_rn(x.y, y.y), z.y), __fadd_rn(__fadd_rn(x.z, y.z), z.z),
+                         __fadd_rn(__fadd_rn(x.w, y.w), z.w));
+  }
+}
+
 }  // namespace
 
 template <int OUT_DT>
 __global__ void __launch_bounds__(kQvgThreads) k_gather_qvg(const GatherArgs a) {
   if (a.abort_flag && *a.abort_flag) return;
-  __shared__ __align__(16) QvgTables T;
+  extern __shared__ __align__(16) unsigned char qvg_smem[];
+  QvgTables& T = *reinterpret_cast<QvgTables*>(qvg_smem);
   const GatherQvgTile tile = a.qtiles[blockIdx.x];
   const int layer = (int)(blockIdx.z >> 1), side = (int)(blockIdx.z & 1);
   const int H = a.H;
@@ -289,51 +331,80 @@ __global__ void __launch_bounds__(kQvgThreads) k_gather_qvg(const GatherArgs a) 
   const uint8_t* codes = base + (side ? run.off[1] : run.off[0]);
   const float* scales = reinterpret_cast<const float*>(base + (side ? run.off[3] : run.off[2]));
   const float* cb = a.cb + (int64_t)layer * a.cb_layer_stride + (int64_t)side * H * 16 * kQD;
+  const int64_t src0 = run.src_tok + tile.tok0;
+  uint32_t nonfinite = 0;  // any table entry inf or NaN
 
-  // ---- tables of this block's alpha-scaled codewords, thread per (head, d)
-  for (int i = threadIdx.x; i < nh * kQD; i += kQvgThreads) {
-    const int hh = i / kQD, d = i % kQD, h = h0 + hh;
-    const float* al = scales + ((int64_t)h * run.n_blocks + tile.blk) * 4;
-    const float* e = cb + (int64_t)h * 16 * kQD + d;  // [stage][entry][d]
-    const float a0 = __ldg(al), a1 = __ldg(al + 1), a2 = __ldg(al + 2), a3 = __ldg(al + 3);
-    float p0[4], p1[4];
+  // ---- the tile's codes, kQvgHeads slots per token (slots >= nh unused)
+  for (int i = threadIdx.x; i < tile.ntok * kQvgHeads; i += kQvgThreads) {
+    const int t = i / kQvgHeads, hh = i % kQvgHeads;
+    if (hh < nh) T.code[i] = __ldg(codes + (src0 + t) * H + h0 + hh);
+  }
+
+  // ---- this lane's P3 values: head w % 4, columns 4 lane .. 4 lane + 3
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int hh = warp % kQvgHeads, tpar = warp / kQvgHeads;
+  float4 p3[4];
+  if (hh < nh) {
+    const int h = h0 + hh;
+    const float a3 = __ldg(scales + ((int64_t)h * run.n_blocks + tile.blk) * 4 + 3);
+    const float4* e3 = reinterpret_cast<const float4*>(cb + ((int64_t)h * 16 + 12) * kQD) + lane;
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
-      p0[c] = __fadd_rn(0.0f, __fmul_rn(a0, __ldg(e + (0 * 4 + c) * kQD)));  // out = +0, out += a0 e0
-      p1[c] = __fmul_rn(a1, __ldg(e + (1 * 4 + c) * kQD));
-      T.p2[hh][c][d] = __fmul_rn(a2, __ldg(e + (2 * 4 + c) * kQD));
-      T.p3[hh][c][d] = __fmul_rn(a3, __ldg(e + (3 * 4 + c) * kQD));
+      const float4 e = __ldg(e3 + c * (kQD / 4));
+      p3[c] = make_float4(__fmul_rn(a3, e.x), __fmul_rn(a3, e.y), __fmul_rn(a3, e.z), __fmul_rn(a3, e.w));
+      nonfinite |= !(finite_f32(p3[c].x) && finite_f32(p3[c].y) && finite_f32(p3[c].z) && finite_f32(p3[c].w));
     }
-#pragma unroll
-    for (int c0 = 0; c0 < 4; ++c0)
-#pragma unroll
-      for (int c1 = 0; c1 < 4; ++c1) T.q01[hh][c0 * 4 + c1][d] = __fadd_rn(p0[c0], p1[c1]);
   }
-  __syncthreads();
 
-  // ---- decode: 8 threads per (token, head) row
-  const int grp = threadIdx.x >> 3, l8 = threadIdx.x & 7;
-  const int n_items = tile.ntok * nh;
-  const int64_t src0 = run.src_tok + tile.tok0;
-  const int64_t dst0 = run.dst_tok + tile.tok0;  // batch 1
-  void* out = side ? a.out_v[layer] : a.out_k[layer];
-  for (int it = grp; it < n_items; it += kQvgThreads / 8) {
-    const int t = it / nh, hh = it - t * nh, h = h0 + hh;
-    const uint32_t code = __ldg(codes + (src0 + t) * H + h);  // stage s at bits 2s, 2s+1
-    const float* q = T.q01[hh][(code & 3u) * 4 + ((code >> 2) & 3u)];
-    const float* r2 = T.p2[hh][(code >> 4) & 3u];
-    const float* r3 = T.p3[hh][(code >> 6) & 3u];
-    const uint64_t ob = ((uint64_t)(dst0 + t) * H + h) * kQD;
+  // ---- Q01 and P2 in shared memory, thread per (head, d): <= 2 items each,
+  // all loads issued before any use
+  static_assert(kQvgHeads * kQD <= 2 * kQvgThreads, "two table items per thread");
+  float ev[2][12], av[2][3];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int d = 4 * l8 + 32 * j;
-      const float4 x = *reinterpret_cast<const float4*>(q + d);
-      const float4 y = *reinterpret_cast<const float4*>(r2 + d);
-      const float4 z = *reinterpret_cast<const float4*>(r3 + d);
-      store4<OUT_DT>(out, ob + d, __fadd_rn(__fadd_rn(x.x, y.x), z.x), __fadd_rn(__fadd_rn(x.y, y.y), z.y),
-                     __fadd_rn(__fadd_rn(x.z, y.z), z.z), __fadd_rn(__fadd_rn(x.w, y.w), z.w));
+  for (int k = 0; k < 2; ++k) {
+    const int i = threadIdx.x + k * kQvgThreads;
+    if (i < nh * kQD) {
+      const int ih = i / kQD, d = i % kQD, h = h0 + ih;
+      const float* al = scales + ((int64_t)h * run.n_blocks + tile.blk) * 4;
+      const float* e = cb + (int64_t)h * 16 * kQD + d;  // [stage][entry][d]
+#pragma unroll
+      for (int s2 = 0; s2 < 3; ++s2) av[k][s2] = __ldg(al + s2);
+#pragma unroll
+      for (int r = 0; r < 12; ++r) ev[k][r] = __ldg(e + r * kQD);
     }
   }
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const int i = threadIdx.x + k * kQvgThreads;
+    if (i < nh * kQD) {
+      const int ih = i / kQD, d = i % kQD;
+      float p0[4], p1[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        p0[c] = __fadd_rn(0.0f, __fmul_rn(av[k][0], ev[k][c]));  // out = +0, out += a0 e0
+        p1[c] = __fmul_rn(av[k][1], ev[k][4 + c]);
+        const float v2 = __fmul_rn(av[k][2], ev[k][8 + c]);
+        T.p2[ih][c][d] = v2;
+        nonfinite |= !finite_f32(v2);
+      }
+#pragma unroll
+      for (int c0 = 0; c0 < 4; ++c0)
+#pragma unroll
+        for (int c1 = 0; c1 < 4; ++c1) {
+          const float q = __fadd_rn(p0[c0], p1[c1]);
+          T.q01[ih][c0 * 4 + c1][d] = q;
+          nonfinite |= !finite_f32(q);
+        }
+    }
+  }
+  // With every table entry finite no output is NaN (finite sums can only
+  // overflow to +-inf), so the hardware converters are exact.
+  const bool all_finite = __syncthreads_and(nonfinite == 0) != 0;
+  if (hh >= nh) return;
+  void* out = side ? a.out_v[layer] : a.out_k[layer];
+  const int64_t dst0 = run.dst_tok + tile.tok0;  // batch 1
+  if (all_finite) decode_rows<OUT_DT, true>(out, T, p3, tile.ntok, dst0, H, h0 + hh, hh, tpar, lane);
+  else decode_rows<OUT_DT, false>(out, T, p3, tile.ntok, dst0, H, h0 + hh, hh, tpar, lane);
 }
 
 cudaError_t launch_gather(const GatherArgs& a, bool vector_ok, cudaStream_t s) {
@@ -341,12 +412,29 @@ cudaError_t launch_gather(const GatherArgs& a, bool vector_ok, cudaStream_t s) {
   if (a.n_qtiles > 0) {
     if (!vector_ok || a.D != kQD || a.n_layers > 32767) return cudaErrorInvalidValue;
     dim3 qgrid((unsigned)a.n_qtiles, (unsigned)((a.H + kQvgHeads - 1) / kQvgHeads), (unsigned)(2 * a.n_layers));
+    const int smem = (int)sizeof(QvgTables);
+    // above the 48 KB default: opt in (set on every launch, so it holds on
+    // whichever device is current)
+    auto prep = [&](const void* fn, int) -> cudaError_t {
+      return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    };
+    cudaError_t e = cudaSuccess;
     switch (a.out_dtype) {
-      case F32: k_gather_qvg<F32><<<qgrid, kQvgThreads, 0, s>>>(a); break;
-      case BF16: k_gather_qvg<BF16><<<qgrid, kQvgThreads, 0, s>>>(a); break;
-      default: k_gather_qvg<F16><<<qgrid, kQvgThreads, 0, s>>>(a); break;
+      case F32:
+        if ((e = prep((const void*)k_gather_qvg<F32>, 0)) == cudaSuccess)
+          k_gather_qvg<F32><<<qgrid, kQvgThreads, smem, s>>>(a);
+        break;
+      case BF16:
+        if ((e = prep((const void*)k_gather_qvg<BF16>, 1)) == cudaSuccess)
+          k_gather_qvg<BF16><<<qgrid, kQvgThreads, smem, s>>>(a);
+        break;
+      default:
+        if ((e = prep((const void*)k_gather_qvg<F16>, 2)) == cudaSuccess)
+          k_gather_qvg<F16><<<qgrid, kQvgThreads, smem, s>>>(a);
+        break;
     }
-    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }
   if (a.n_tiles == 0) return cudaSuccess;

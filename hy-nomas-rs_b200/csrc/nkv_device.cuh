@@ -5,6 +5,7 @@
 // the hardware converters (whose NaN payload handling differs from half's).
 #pragma once
 
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -27,6 +28,20 @@ __device__ __forceinline__ uint32_t bf16_bits_finite(float x) {
   uint32_t u = __float_as_uint(x);
   return (u + 0x7FFFu + ((u >> 16) & 1u)) >> 16;
 }
+// Two f32 -> packed bf16 pair (a in the low half) by the hardware converter:
+// round to nearest even, equal to bf16_bits for every non-NaN input (checked
+// over all 2^32 patterns by tests/cuda/convert_check.cu); only NaN payloads
+// differ, so callers use it where no input can be NaN.
+__device__ __forceinline__ uint32_t bf16x2_bits_nonnan(float a, float b) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+// The same for IEEE binary16 (equal to f16_bits for every non-NaN input).
+__device__ __forceinline__ uint32_t f16x2_bits_nonnan(float a, float b) {
+  const __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
 // bf16 bits -> f32 (half's bf16_to_f32: NaN gets the quiet bit).
 __device__ __forceinline__ float bf16_value(uint32_t b) {
   b &= 0xFFFFu;

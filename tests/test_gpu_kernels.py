@@ -220,3 +220,19 @@ def test_qvg_d128_fast_path_ties_nan_and_extremes(orc, nkv, torch):
         s = scales.cpu().numpy()
         same = (s.view(np.uint32) == scales_r.view(np.uint32)) | (np.isnan(s) & np.isnan(scales_r))
         assert same.all()
+
+
+def test_hardware_pair_converters_equal_integer_rounding_off_nan(tmp_path):
+    """The no-NaN fast paths convert with the hardware bf16x2 / f16x2
+    converters; they must equal the library's integer round-to-nearest-even
+    on every non-NaN f32 (all 2^32 patterns, both lanes)."""
+    import os
+    import subprocess
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    exe = str(tmp_path / "convert_check")
+    subprocess.run(["nvcc", "-std=c++17", "-O3", "-gencode", "arch=compute_100a,code=sm_100a", "-fmad=false",
+                    "-I", os.path.join(root, "hy-nomas-rs_b200", "csrc"), os.path.join(root, "tests", "cuda",
+                                                                                    "convert_check.cu"),
+                    "-o", exe], check=True, capture_output=True)
+    out = subprocess.run([exe], check=True, capture_output=True, text=True, timeout=120).stdout
+    assert out.split() == ["bf16_mismatches", "0", "f16_mismatches", "0"], out
