@@ -39,8 +39,10 @@ __device__ __forceinline__ void dequant16(const uint4 w, float s, float (&o)[16]
 }
 
 // Store 16 f32 values rounded to OUT_DT at element offset `i` (16-aligned).
-template <int OUT_DT>
-__device__ __forceinline__ void store16(void* out, uint64_t i, const float (&v)[16], bool finite) {
+// NONNAN: no value is NaN (dequantized INT8), so the hardware pair
+// converters give the reference's bits.
+template <int OUT_DT, bool NONNAN>
+__device__ __forceinline__ void store16(void* out, uint64_t i, const float (&v)[16]) {
   if constexpr (OUT_DT == F32) {
     float4* p = reinterpret_cast<float4*>(static_cast<float*>(out) + i);
 #pragma unroll
@@ -49,15 +51,15 @@ __device__ __forceinline__ void store16(void* out, uint64_t i, const float (&v)[
     uint32_t w[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      uint32_t lo, hi;
-      if constexpr (OUT_DT == BF16) {
-        lo = finite ? dev::bf16_bits_finite(v[2 * j]) : dev::bf16_bits(v[2 * j]);
-        hi = finite ? dev::bf16_bits_finite(v[2 * j + 1]) : dev::bf16_bits(v[2 * j + 1]);
+      if constexpr (NONNAN && OUT_DT == BF16) {
+        w[j] = dev::bf16x2_bits_nonnan(v[2 * j], v[2 * j + 1]);
+      } else if constexpr (NONNAN) {
+        w[j] = dev::f16x2_bits_nonnan(v[2 * j], v[2 * j + 1]);
+      } else if constexpr (OUT_DT == BF16) {
+        w[j] = (dev::bf16_bits(v[2 * j]) & 0xFFFFu) | (dev::bf16_bits(v[2 * j + 1]) << 16);
       } else {
-        lo = dev::f16_bits(v[2 * j]);
-        hi = dev::f16_bits(v[2 * j + 1]);
+        w[j] = (dev::f16_bits(v[2 * j]) & 0xFFFFu) | (dev::f16_bits(v[2 * j + 1]) << 16);
       }
-      w[j] = (lo & 0xFFFFu) | (hi << 16);
     }
     uint4* p = reinterpret_cast<uint4*>(static_cast<unsigned short*>(out) + i);
     p[0] = make_uint4(w[0], w[1], w[2], w[3]);
@@ -112,7 +114,7 @@ __global__ void __launch_bounds__(kGatherThreads) k_gather(const GatherArgs a) {
         if (c < n_chunks) {
           float v[16];
           dequant16(w[u], s[u], v);
-          store16<OUT_DT>(out_base, (uint64_t)(out_tok * HD + (int64_t)c * 16), v, true);
+          store16<OUT_DT, true>(out_base, (uint64_t)(out_tok * HD + (int64_t)c * 16), v);
         }
       }
     }
@@ -168,7 +170,7 @@ __global__ void __launch_bounds__(kGatherThreads) k_gather(const GatherArgs a) {
           v[4 * j + 3] = __fadd_rn(v[4 * j + 3], __fmul_rn(alpha, q.w));
         }
       }
-      store16<OUT_DT>(out_base, (uint64_t)(out_tok * HD + (int64_t)c * 16), v, false);
+      store16<OUT_DT, false>(out_base, (uint64_t)(out_tok * HD + (int64_t)c * 16), v);
     }
   }
 }

@@ -18,8 +18,10 @@
 // codewords, NaN) the thread computes the reference's sequential f64
 // distances exactly.  Step 2 is the reference's computation itself: products
 // of f32 values are exact in f64, so the FMA chain in d order reproduces its
-// rounding.  Step 3 is two f32 roundings, as in the reference (scalar
-// instructions: see the update below).
+// rounding.  Step 3 is two f32 roundings, as in the reference: warp 0 builds
+// the stage's table -f32(alpha * e_c) with scalar multiplies, and each token
+// adds its row with packed f32x2 adds (no multiply in the thread's data flow,
+// so nothing can be contracted into one rounding).
 //
 // One CTA of 64 threads per (layer x side, head, group of blocks); thread t
 // owns token t of the current block, its residual in registers.
@@ -45,9 +47,9 @@ struct QvgSmem {
   double ee[QSMAX][QE];            // sequential f64 sum of e_d^2 (the den inner sum)
   float enorm[QSMAX][QE];          // upper bounds of |e_i|
   float unorm[QSMAX][3];           // upper bounds of |e_i - e_0|
-  double inner[QB];                // per-token numerator inner sums
-  int code[QB];
-  float alpha;
+  double inner[QB];                // per-token numerator inner sums (+0 for idle threads)
+  double dv[QB];                   // per-token denominator inner sums (+0 for idle threads)
+  float nP[QE][QD + 4];            // -f32(alpha * e_c) of the current stage (rows padded)
 };
 
 }  // namespace
@@ -116,14 +118,19 @@ __global__ void __launch_bounds__(QB, 6) k_qvg_encode_d128(const QvgEncodeJob* _
         // ---- f32 screen of the nearest codeword
         float2 g1 = make_float2(0.0f, 0.0f), g2 = g1, g3 = g1, rr2 = g1;
 #pragma unroll
-        for (int k = 0; k < QD / 2; ++k) {
-          const float2 u1 = *reinterpret_cast<const float2*>(&sm.u[s][0][2 * k]);
-          const float2 u2 = *reinterpret_cast<const float2*>(&sm.u[s][1][2 * k]);
-          const float2 u3 = *reinterpret_cast<const float2*>(&sm.u[s][2][2 * k]);
-          g1 = __ffma2_rn(r[k], u1, g1);
-          g2 = __ffma2_rn(r[k], u2, g2);
-          g3 = __ffma2_rn(r[k], u3, g3);
-          rr2 = __ffma2_rn(r[k], r[k], rr2);
+        for (int k = 0; k < QD / 4; ++k) {
+          const float4 u1 = *reinterpret_cast<const float4*>(&sm.u[s][0][4 * k]);
+          const float4 u2 = *reinterpret_cast<const float4*>(&sm.u[s][1][4 * k]);
+          const float4 u3 = *reinterpret_cast<const float4*>(&sm.u[s][2][4 * k]);
+          const float2 ra = r[2 * k], rb = r[2 * k + 1];
+          g1 = __ffma2_rn(ra, make_float2(u1.x, u1.y), g1);
+          g2 = __ffma2_rn(ra, make_float2(u2.x, u2.y), g2);
+          g3 = __ffma2_rn(ra, make_float2(u3.x, u3.y), g3);
+          rr2 = __ffma2_rn(ra, ra, rr2);
+          g1 = __ffma2_rn(rb, make_float2(u1.z, u1.w), g1);
+          g2 = __ffma2_rn(rb, make_float2(u2.z, u2.w), g2);
+          g3 = __ffma2_rn(rb, make_float2(u3.z, u3.w), g3);
+          rr2 = __ffma2_rn(rb, rb, rr2);
         }
         const double rn = sqrt((double)__fadd_rn(rr2.x, rr2.y)) * (1.0 + 2e-5);  // >= |r|
         const double G[4] = {0.0, (double)__fadd_rn(g1.x, g1.y), (double)__fadd_rn(g2.x, g2.y),
@@ -183,32 +190,40 @@ __global__ void __launch_bounds__(QB, 6) k_qvg_encode_d128(const QvgEncodeJob* _
           acc = fma((double)r[k].x, ec[2 * k], acc);
           acc = fma((double)r[k].y, ec[2 * k + 1], acc);
         }
-        sm.inner[t] = acc;
-        sm.code[t] = c;
       }
+      sm.inner[t] = acc;                    // +0 for idle threads
+      sm.dv[t] = active ? sm.ee[s][c] : 0.0;
       __syncthreads();
-      if (t == 0) {
-        double num = 0.0, den = 0.0;
-        for (int i = 0; i < n; ++i) {
-          num = __dadd_rn(num, sm.inner[i]);
-          den = __dadd_rn(den, sm.ee[s][sm.code[i]]);
+      if (t < 32) {
+        // warp 0: the block's sums in token order (qvg.rs:220-229) on lane 0.
+        // Idle tokens add +0, which leaves a sum started at +0 unchanged.
+        float alpha = 0.0f;
+        if (t == 0) {
+          double num = 0.0, den = 0.0;
+#pragma unroll
+          for (int i = 0; i < QB; ++i) {
+            num = __dadd_rn(num, sm.inner[i]);
+            den = __dadd_rn(den, sm.dv[i]);
+          }
+          alpha = den > 1e-12 ? __double2float_rn(__ddiv_rn(num, den)) : 1.0f;  // qvg.rs:230
+          J.scales[((size_t)h * n_blocks + blk) * stages + s] = alpha;
         }
-        const float alpha = den > 1e-12 ? __double2float_rn(__ddiv_rn(num, den)) : 1.0f;  // qvg.rs:230
-        sm.alpha = alpha;
-        J.scales[((size_t)h * n_blocks + blk) * stages + s] = alpha;
+        alpha = __shfl_sync(0xFFFFFFFFu, alpha, 0);
+        // the stage's -f32(alpha * e) rows: one rounding per product, as the
+        // reference's alpha * e[d] (qvg.rs:232-237)
+#pragma unroll
+        for (int i = t; i < QE * QD; i += 32) sm.nP[i / QD][i % QD] = __fmul_rn(-alpha, sm.e32[s][i / QD][i % QD]);
       }
       __syncthreads();
       if (active) {
-        const float alpha = sm.alpha;
-        const float* ec = sm.e32[s][c];
-        // r - f32(alpha * e) with two roundings (qvg.rs:232-237).  Scalar on
-        // purpose: a packed f32x2 multiply feeding a packed add was found
-        // contracted into one fused rounding even with explicit .rn.
+        // r + (-f32(alpha * e)): the second rounding.  The table comes from
+        // memory, so no multiply can be fused into these packed adds.
+        const float* np = sm.nP[c];
 #pragma unroll
-        for (int k = 0; k < QD / 2; ++k) {
-          const float2 e2 = *reinterpret_cast<const float2*>(&ec[2 * k]);
-          r[k].x = __fsub_rn(r[k].x, __fmul_rn(alpha, e2.x));
-          r[k].y = __fsub_rn(r[k].y, __fmul_rn(alpha, e2.y));
+        for (int k = 0; k < QD / 4; ++k) {
+          const float4 q = *reinterpret_cast<const float4*>(&np[4 * k]);
+          r[2 * k] = __fadd2_rn(r[2 * k], make_float2(q.x, q.y));
+          r[2 * k + 1] = __fadd2_rn(r[2 * k + 1], make_float2(q.z, q.w));
         }
         packed |= (uint32_t)c << (2 * s);
       }

@@ -23,11 +23,6 @@ __device__ __forceinline__ uint32_t bf16_bits(float x) {
   if ((u & 0x7FFFFFFFu) > 0x7F800000u) return (u >> 16) | 0x40u;
   return (u + 0x7FFFu + ((u >> 16) & 1u)) >> 16;
 }
-// Same for values known not to be NaN (dequantized outputs).
-__device__ __forceinline__ uint32_t bf16_bits_finite(float x) {
-  uint32_t u = __float_as_uint(x);
-  return (u + 0x7FFFu + ((u >> 16) & 1u)) >> 16;
-}
 // Two f32 -> packed bf16 pair (a in the low half) by the hardware converter:
 // round to nearest even, equal to bf16_bits for every non-NaN input (checked
 // over all 2^32 patterns by tests/cuda/convert_check.cu); only NaN payloads
