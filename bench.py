@@ -41,6 +41,10 @@ PAST = 16
 ARCHIVED = 32
 METRIC = "KV commit+rebuild GB/s (8B geometry, INT8, uniform rebuild)"
 METRIC_QVG = "KV commit+rebuild GB/s (8B geometry, QVG, uniform rebuild)"
+# BASELINE configs[4] (box run): the same turn with a phase-swapped cache,
+# park + unpark of the working set every turn, over a 64-segment archive.
+METRIC_SWAP = "KV turn GB/s incl. phase swap (8B geometry, {}, uniform rebuild, park + unpark)"
+ARCHIVED_SWAP = 64
 WORKLOADS = {"int8": "nomas-8B INT8 commit + uniform rebuild (16 past frames) + newest segment",
              "qvg": "nomas-8B QVG (frozen codebooks) commit + uniform decode-gather rebuild + newest segment"}
 # SURVEY 8(d) algorithmic bytes per token per layer: K+V BF16 read (12288) +
@@ -61,7 +65,12 @@ def rebuild_tokens() -> int:
 QVG_BYTES_PER_VIDEO_TOKEN = 2 * HEADS * HEAD_DIM * 2 + 2 * HEADS + 2 * HEADS * 4 * 4 // 64  # 12,348
 
 
-def step_bytes(n_layers: int, workload: str = "int8") -> dict:
+def working_set_bytes(n_layers: int) -> int:
+    """Rebuilt K and V working set in BF16 (what park copies out and unpark back)."""
+    return rebuild_tokens() * 2 * HEADS * HEAD_DIM * 2 * n_layers
+
+
+def step_bytes(n_layers: int, workload: str = "int8", swap: bool = False) -> dict:
     if workload == "qvg":
         video = FRAMES * TPF
         commit = (video * QVG_BYTES_PER_VIDEO_TOKEN + TEXT * BYTES_PER_TOKEN) * n_layers
@@ -71,7 +80,9 @@ def step_bytes(n_layers: int, workload: str = "int8") -> dict:
         commit = SEG_TOKENS * BYTES_PER_TOKEN * n_layers
         rebuild = rebuild_tokens() * BYTES_PER_TOKEN * n_layers
         recent = SEG_TOKENS * BYTES_PER_TOKEN * n_layers
-    return {"commit": commit, "rebuild": rebuild, "recent": recent, "total": commit + rebuild + recent}
+    sw = 2 * working_set_bytes(n_layers) if swap else 0  # park (D2H) + unpark (H2D)
+    return {"commit": commit, "rebuild": rebuild, "recent": recent, "swap": sw,
+            "total": commit + rebuild + recent + sw}
 
 
 def qvg_codebooks(layer: int):
@@ -107,6 +118,7 @@ class ClockSampler:
         self.gpu = int(ids[local_index]) if local_index < len(ids) else local_index
         self.samples: list[tuple[float, float, int]] = []
         self._stop = threading.Event()
+        self._ready = threading.Event()  # first sample taken (or sampling failed)
         self._t = None
         self.err = None
 
@@ -121,15 +133,35 @@ class ClockSampler:
             while not self._stop.is_set():
                 sm = float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
                 self.samples.append((sm, smax, int(get_reasons(h))))
+                self._ready.set()
                 time.sleep(0.005)
             pynvml.nvmlShutdown()
         except Exception as e:  # noqa: BLE001
             self.err = repr(e)
+            self._smi_loop()
+        finally:
+            self._ready.set()
+
+    def _smi_loop(self):
+        """nvidia-smi polling when NVML is not usable."""
+        import subprocess
+        q = "clocks.sm,clocks.max.sm,clocks_event_reasons.active"
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                                      "-i", str(self.gpu)], capture_output=True, text=True, timeout=5).stdout
+                sm, smax, reasons = [x.strip() for x in out.strip().split(",")]
+                self.samples.append((float(sm), float(smax), int(reasons, 16)))
+            except Exception as e:  # noqa: BLE001
+                self.err = f"{self.err}; nvidia-smi: {e!r}"
+                return
+            self._ready.set()
+            time.sleep(0.02)
 
     def start(self):
         self._t = threading.Thread(target=self._loop, daemon=True)
         self._t.start()
-        time.sleep(0.02)
+        self._ready.wait(timeout=5.0)  # so a short timed region still gets samples
 
     def stop(self) -> dict:
         self._stop.set()
@@ -208,7 +240,8 @@ def run_gpu(args) -> None:
     stream = torch.cuda.current_stream(dev)
     wl = args.workload
     storage = nk.CacheStorage.qvg_() if wl == "qvg" else nk.CacheStorage.int8()
-    cfg = nk.CacheConfig(storage=storage, sampling=nk.HistorySampling.uniform(), past_frames=PAST)
+    swap = args.swap
+    cfg = nk.CacheConfig(storage=storage, sampling=nk.HistorySampling.uniform(), past_frames=PAST, phase_swap=swap)
     bank = nk.KvBank(cfg, n_layers, 1, HEADS, HEAD_DIM, torch.bfloat16, device=dev, layer_begin=begin)
     if wl == "qvg":
         for i in range(n_layers):
@@ -216,8 +249,10 @@ def run_gpu(args) -> None:
     gen = synth.DeviceGen(dev, seed=0, key_sigma=1.0)
     desc = lambda i: nk._abi.nkv_segment_desc(i, i * FRAMES, FRAMES, FRAMES * TPF, TEXT, 0)  # noqa: E731
 
-    e2e_steps = min(args.steps, 4)
-    prefill = max(1, ARCHIVED - 1 - args.warmup)
+    # the swap run holds a 64-segment archive (~142 GB at 48 layers on one
+    # GPU): fewer e2e turns, and the e2e staging reuses a resident input set
+    e2e_steps = min(args.steps, 2 if swap else 4)
+    prefill = max(1, (ARCHIVED_SWAP if swap else ARCHIVED) - 1 - args.warmup)
     total_segments = prefill + args.warmup + args.steps + args.warmup + e2e_steps
     bank.reserve(bank.segment_bytes(desc(0)) * n_layers * total_segments, rebuild_tokens())
 
@@ -235,15 +270,30 @@ def run_gpu(args) -> None:
     recent_v = [torch.empty(shape, dtype=torch.bfloat16, device=dev) for _ in range(n_layers)]
 
     seg = 0
+    swap_ms = [0.0, 0.0]  # park, unpark: device time on the bank's stream
+    sev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
 
-    def step(ks, vs):
+    def step(ks, vs, swap_now=True):
         nonlocal seg
         bank.commit_tensors(desc(seg), ks, vs)  # validate + quantize + rebuild (one sync for the error flag)
         bank.decode_segment(seg, recent_k, recent_v)  # the newest archived segment in full
         seg += 1
+        if swap and swap_now:
+            # phase_swap.rs:42-92: the working set goes to host memory and back;
+            # both calls return after their copies completed
+            sev[0].record(stream)
+            bank.park_all()
+            sev[1].record(stream)
+            bank.unpark_all()
+            sev[2].record(stream)
+            sev[2].synchronize()
+            swap_ms[0] += sev[0].elapsed_time(sev[1])
+            swap_ms[1] += sev[1].elapsed_time(sev[2])
 
+    # the prefill only builds the archive: no swaps while the working set is
+    # still growing (a re-grown set would briefly coexist with its successor)
     for _ in range(prefill):
-        step(*sets[seg % 2])
+        step(*sets[seg % 2], swap_now=False)
     for _ in range(args.warmup):
         step(*sets[seg % 2])
     assert bank.layer(0).valid_len() == rebuild_tokens(), bank.layer(0).valid_len()
@@ -257,6 +307,7 @@ def run_gpu(args) -> None:
         dist.barrier()
     torch.cuda.synchronize()
     clocks.start()
+    swap_ms[0] = swap_ms[1] = 0.0
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     t0.record(stream)
@@ -274,8 +325,20 @@ def run_gpu(args) -> None:
     if world > 1:
         dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
     ms_max = float(ms_t.item())
-    bytes_all = step_bytes(model_layers, wl)["total"] * args.steps
+    bytes_all = step_bytes(model_layers, wl, swap)["total"] * args.steps
     value = bytes_all / (ms_max / 1e3) / 1e9
+    swap_info = None
+    if swap:
+        wsb = working_set_bytes(n_layers) * args.steps
+        pt = torch.tensor(swap_ms, dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(pt, op=dist.ReduceOp.MAX)
+        swap_info = {"bytes_per_direction_per_step": working_set_bytes(model_layers),
+                     "park_gbs_per_gpu": round(wsb / (float(pt[0]) / 1e3) / 1e9, 2),
+                     "unpark_gbs_per_gpu": round(wsb / (float(pt[1]) / 1e3) / 1e9, 2),
+                     "park_ms_per_step": round(float(pt[0]) / args.steps, 3),
+                     "unpark_ms_per_step": round(float(pt[1]) / args.steps, 3),
+                     "bound": "host link (PCIe), per GPU"}
 
     # ---------------------------------------------------- timed: e2e (host buffers)
     host = []
@@ -286,8 +349,11 @@ def run_gpu(args) -> None:
             hk[i].copy_(sets[s][0][i])
             hv[i].copy_(sets[s][1][i])
         host.append((hk, hv))
-    stage_k = [torch.empty(shape, dtype=torch.bfloat16, device=dev) for _ in range(n_layers)]
-    stage_v = [torch.empty(shape, dtype=torch.bfloat16, device=dev) for _ in range(n_layers)]
+    if swap:
+        stage_k, stage_v = sets[0]
+    else:
+        stage_k = [torch.empty(shape, dtype=torch.bfloat16, device=dev) for _ in range(n_layers)]
+        stage_v = [torch.empty(shape, dtype=torch.bfloat16, device=dev) for _ in range(n_layers)]
     flag_host = torch.empty(1, dtype=torch.int32, pin_memory=True)
     vlen_dev = torch.empty(1, dtype=torch.int32, device=dev)
 
@@ -316,7 +382,7 @@ def run_gpu(args) -> None:
     ems = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(ems, op=dist.ReduceOp.MAX)
-    e2e_value = step_bytes(model_layers, wl)["total"] * e2e_steps / (float(ems.item()) / 1e3) / 1e9
+    e2e_value = step_bytes(model_layers, wl, swap)["total"] * e2e_steps / (float(ems.item()) / 1e3) / 1e9
     h2d = 2 * SEG_TOKENS * HEADS * HEAD_DIM * 2 * model_layers
     d2h = (4 + 4) * world  # commit's non-finite flag + the result read, per rank
 
@@ -365,16 +431,19 @@ def run_gpu(args) -> None:
 
     if rank == 0:
         out = {
-            "metric": METRIC if wl == "int8" else METRIC_QVG, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "metric": (METRIC_SWAP.format(wl.upper()) if swap else METRIC if wl == "int8" else METRIC_QVG),
+            "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": WORKLOADS[wl],
+            "config": {"workload": WORKLOADS[wl] + (" + park/unpark (phase swap) every turn" if swap else ""),
                        "layers": model_layers, "heads": HEADS, "head_dim": HEAD_DIM, "segment_tokens": SEG_TOKENS,
                        "tokens_per_frame": TPF, "frames_per_segment": FRAMES, "text_tokens": TEXT,
                        "past_frames": PAST, "archived_segments_at_first_timed_step": prefill + args.warmup + 1,
-                       "working_set_tokens": rebuild_tokens(), "bytes_per_step": step_bytes(model_layers, wl)["total"],
+                       "phase_swap": swap,
+                       "working_set_tokens": rebuild_tokens(), "bytes_per_step": step_bytes(model_layers, wl, swap)["total"],
                        "parallelism": f"layer-sharded x{world}", "l2": "inputs 3.8 GB per step > 126 MB L2"},
             "tokens_per_s": tok,
+            "phase_swap": swap_info,
             "roofline": {"bound": "hbm", "achieved": round(gather_gbs, 1) if gather_gbs else None,
                          "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": round(gather_gbs / peaks["hbm_gbs"], 4) if gather_gbs else None,
@@ -425,6 +494,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--workload", default="int8", choices=["int8", "qvg"],
                     help="int8 = BASELINE configs[1] (the headline); qvg = configs[2]")
+    ap.add_argument("--swap", action="store_true",
+                    help="BASELINE configs[4]: phase-swapped cache, park + unpark every turn, 64-segment archive")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="model layers (48 = the 8B geometry; fewer only for small profiling cases)")
     args = ap.parse_args()
