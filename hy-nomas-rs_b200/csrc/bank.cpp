@@ -16,7 +16,6 @@
 #include <cstring>
 #include <thread>
 
-#include "nkv_qvg_fit.h"
 
 namespace nkv {
 
@@ -495,53 +494,58 @@ void Bank::ensure_ws(uint64_t tokens, unsigned char** fresh, uint64_t* fresh_cap
 
 std::vector<int> Bank::fit_qvg(const nkv_segment_desc& s, int kv_dtype, const void* const* k, const void* const* v) {
   std::vector<int> fitted_now;
-  bool all_fitted = true;
-  for (int i = 0; i < n_layers_; ++i) all_fitted &= fitted_[i] != 0;
-  if (all_fitted) return fitted_now;  // the usual case: no host staging at all
-  const size_t L = s.image_tokens + s.text_tokens, n = L * H_ * D_;
-  const size_t esz = dtype_size(kv_dtype);
-  std::vector<unsigned char> raw(n * esz);
-  std::vector<float> kf(n), vf(n);
-  auto to_f32 = [&](std::vector<float>& dst) {
-    if (kv_dtype == NKV_F32) {
-      std::memcpy(dst.data(), raw.data(), n * 4);
-      return;
-    }
-    const uint16_t* h = reinterpret_cast<const uint16_t*>(raw.data());
-    for (size_t i = 0; i < n; ++i) {
-      uint32_t b = h[i];
-      uint32_t u;
-      if (kv_dtype == NKV_BF16) {
-        if ((b & 0x7FFFu) > 0x7F80u) b |= 0x40u;
-        u = b << 16;
-      } else {  // IEEE binary16, exact
-        const uint32_t sign = (b & 0x8000u) << 16, e = (b >> 10) & 0x1Fu, m = b & 0x3FFu;
-        if (e == 0x1F) u = sign | 0x7F800000u | (m ? (0x00400000u | (m << 13)) : 0u);
-        else if (e == 0) {
-          float f = float(m) * 5.9604644775390625e-8f;  // m * 2^-24, exact
-          std::memcpy(&u, &f, 4);
-          u |= sign;
-        } else u = sign | ((e + 112u) << 23) | (m << 13);
-      }
-      std::memcpy(&dst[i], &u, 4);
-    }
+  for (int i = 0; i < n_layers_; ++i)
+    if (!fitted_[i]) fitted_now.push_back(i);
+  if (fitted_now.empty()) return fitted_now;  // the usual case
+  // history.rs:256-262: fit on the whole first segment, every unfitted layer,
+  // on the device (kernels_qvg_fit.cu), in chunks of ~1 GB of scratch
+  const uint64_t L = s.image_tokens + s.text_tokens;
+  const size_t per = qvg_fit_scratch_bytes(L, int(D_), q_E_);
+  const size_t cb_head = size_t(q_stages_) * q_E_ * D_;
+  std::vector<QvgFitTask> tasks;
+  for (int i : fitted_now)
+    for (int side = 0; side < 2; ++side)
+      for (int64_t h = 0; h < H_; ++h)
+        tasks.push_back({side ? v[i] : k[i], cb_dev_ + cb_layer_ * i + (cb_layer_ / 2) * side + cb_head * h,
+                         nullptr, nullptr, nullptr, nullptr, cfg_.qvg.codebook_seed + uint64_t(h), int32_t(h)});
+  const size_t chunk = std::max<size_t>(1, std::min(tasks.size(), (size_t(1) << 30) / per));
+  unsigned char* scratch = nullptr;
+  QvgFitTask* d_tasks = nullptr;
+  NKV_CUDA(cudaMalloc(&scratch, chunk * per));
+  auto release = [&]() {
+    cudaStreamSynchronize(stream_);
+    cudaFree(scratch);
+    if (d_tasks) cudaFree(d_tasks);
   };
-  const int threads = std::max(1u, std::thread::hardware_concurrency());
-  for (int i = 0; i < n_layers_; ++i) {
-    if (fitted_[i]) continue;
-    NKV_CUDA(cudaMemcpyAsync(raw.data(), k[i], n * esz, cudaMemcpyDeviceToHost, stream_));
-    NKV_CUDA(cudaStreamSynchronize(stream_));
-    to_f32(kf);
-    NKV_CUDA(cudaMemcpyAsync(raw.data(), v[i], n * esz, cudaMemcpyDeviceToHost, stream_));
-    NKV_CUDA(cudaStreamSynchronize(stream_));
-    to_f32(vf);
-    float* out = cb_host_.data() + cb_layer_ * i;
-    qvg_fit_layer(kf.data(), vf.data(), L, H_, D_, q_stages_, q_E_, cfg_.qvg.codebook_seed, out, threads);
-    NKV_CUDA(cudaMemcpyAsync(cb_dev_ + cb_layer_ * i, out, cb_layer_ * 4, cudaMemcpyHostToDevice, stream_));
-    NKV_CUDA(cudaStreamSynchronize(stream_));
-    fitted_[i] = 1;
-    fitted_now.push_back(i);
+  try {
+    NKV_CUDA(cudaMalloc(reinterpret_cast<void**>(&d_tasks), chunk * sizeof(QvgFitTask)));
+    auto up = [](size_t b) { return (b + 255) & ~size_t(255); };
+    for (size_t c0 = 0; c0 < tasks.size(); c0 += chunk) {
+      const size_t m = std::min(chunk, tasks.size() - c0);
+      for (size_t j = 0; j < m; ++j) {
+        unsigned char* p = scratch + j * per;
+        QvgFitTask& t = tasks[c0 + j];
+        t.res = reinterpret_cast<float*>(p);
+        p += up(L * D_ * 4);
+        t.dmin = reinterpret_cast<double*>(p);
+        p += up(L * 8);
+        t.sums = reinterpret_cast<double*>(p);
+        p += up(size_t(q_E_) * D_ * 8);
+        t.codes = p;
+      }
+      NKV_CUDA(cudaMemcpyAsync(d_tasks, tasks.data() + c0, m * sizeof(QvgFitTask), cudaMemcpyHostToDevice, stream_));
+      NKV_CUDA(launch_qvg_fit(d_tasks, int(m), kv_dtype, L, int(H_), int(D_), q_stages_, q_E_, stream_));
+      NKV_CUDA(cudaStreamSynchronize(stream_));  // the host task array is reused by the next chunk
+    }
+    for (int i : fitted_now)
+      NKV_CUDA(cudaMemcpyAsync(cb_host_.data() + cb_layer_ * i, cb_dev_ + cb_layer_ * i, cb_layer_ * sizeof(float),
+                               cudaMemcpyDeviceToHost, stream_));
+  } catch (...) {
+    release();
+    throw;
   }
+  release();
+  for (int i : fitted_now) fitted_[i] = 1;
   return fitted_now;
 }
 

@@ -61,6 +61,25 @@ bool launch_qvg_encode_d128(const QvgEncodeJob* jobs_dev, int n_jobs, int in_dty
 // above the per-CTA limit at creation).
 size_t qvg_encode_smem_bytes(int D, int block, int bits);
 
+// ------------------------------------------------------------ QVG fit ---
+// One (layer, side, head) codebook fit (QvgCodec::fit, cache/qvg.rs:130-167,
+// 351-442) on the first committed segment.  Scratch (per task, from
+// qvg_fit_scratch_bytes): the residual rows, the farthest-point distances,
+// the Lloyd sums and the per-token entry indices.
+struct QvgFitTask {
+  const void* x;    // (L, H, D) K or V of the segment, in_dtype
+  float* out;       // [stages][E][D] codebooks of this (side, head)
+  float* res;       // n x D
+  double* dmin;     // n
+  double* sums;     // E x D
+  uint8_t* codes;   // n
+  uint64_t seed;    // codebook_seed + head
+  int32_t h;
+};
+size_t qvg_fit_scratch_bytes(uint64_t n, int D, int E);
+cudaError_t launch_qvg_fit(const QvgFitTask* tasks_dev, int n_tasks, int in_dtype, uint64_t n, int H, int D,
+                           int stages, int E, cudaStream_t s);
+
 // -------------------------------------------------------------- gather ---
 enum RunKind : int32_t { RUN_FLOAT = 0, RUN_INT8 = 1, RUN_QVG_VIDEO = 2 };
 

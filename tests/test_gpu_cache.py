@@ -550,3 +550,54 @@ def test_qvg_decode_segment_d128_aligned_and_unaligned_outputs(H):
                 assert np.array_equal(H.torch_to_raw(ko[layer]), kr), (offset, pos, layer)
                 assert np.array_equal(H.torch_to_raw(vo[layer]), vr), (offset, pos, layer)
     p.close()
+
+
+def _qvg_pair(H, stages, bits, block=64, **geo):
+    import nomas_kv as nk
+    spec = H.Spec(storage=STORAGES["qvg"], sampling=SAMPLINGS["uniform"][0], past_frames=4,
+                  qvg=nk.QvgConfig(stages=stages, bits_per_stage=bits, block_size=block))
+    return H.Pair(H.Geometry(**geo), spec)
+
+
+@pytest.mark.parametrize("stages,bits,head_dim,input_dtype", [(4, 2, 128, "bf16"), (2, 3, 32, "f32"),
+                                                              (3, 4, 24, "f16"), (8, 2, 16, "bf16"),
+                                                              (1, 8, 8, "f32")])
+def test_qvg_device_fit_matches_oracle(H, stages, bits, head_dim, input_dtype):
+    """The first commit fits every layer's codebooks on the device
+    (farthest-point init + two Lloyd iterations per stage, qvg.rs:351-442);
+    they must equal the oracle's bit for bit, as must everything after."""
+    p = _qvg_pair(H, stages, bits, model_dtype="bf16", input_dtype=input_dtype, heads=3, head_dim=head_dim, tpf=40,
+                  frames=2, text=7)
+    for _ in range(3):
+        assert p.commit() is None
+        p.check()
+    p.close()
+
+
+def test_qvg_device_fit_identical_rows_take_the_jitter_path(H):
+    """Rows that all coincide make the farthest-point total 0 (<= 1e-12):
+    the reference copies entry 0 and nudges its first value by k * 1e-3."""
+    p = _qvg_pair(H, 4, 2, model_dtype="f32", input_dtype="f32", heads=2, head_dim=16, tpf=32, frames=2, text=4)
+
+    def constant(layer, side, h):
+        h[...] = 0.75 if side == 0 else -1.25
+
+    assert p.commit(poison=constant) is None
+    p.check()
+    assert p.commit() is None
+    p.check()
+    p.close()
+
+
+def test_qvg_device_fit_with_nan_and_inf_rows(H):
+    """Non-finite values in the fitted video rows (not checked by the
+    reference before the fit) must steer the fit exactly as on the CPU."""
+    p = _qvg_pair(H, 4, 2, model_dtype="bf16", input_dtype="f32", heads=2, head_dim=32, tpf=32, frames=2, text=0)
+
+    def poison(layer, side, h):
+        h[0, 3, 1, 5] = np.nan
+        h[0, 40, 0, :] = np.inf
+
+    assert p.commit(poison=poison) is None
+    p.check()
+    p.close()
