@@ -216,7 +216,8 @@ def test_qvg_bank_fit_state_after_failed_first_commit(H):
     assert p.commit(poison=inf_text) is not None
     assert p.o.codebooks(0) is not None and p.o.codebooks(1) is None
     assert p.p.layer(0).qvg_codebooks() is not None and p.p.layer(1).qvg_codebooks() is None
-    assert np.array_equal(p.o.codebooks(0).view(np.uint32), p.p.layer(0).qvg_codebooks().view(np.uint32))
+    # bitwise; the inf in the fitted rows makes NaN entries, compared by position
+    assert H.same_values(p.o.codebooks(0), p.p.layer(0).qvg_codebooks(), "f32").all()
     p.close()
 
 
