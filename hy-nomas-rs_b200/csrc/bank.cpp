@@ -498,7 +498,7 @@ std::vector<int> Bank::fit_qvg(const nkv_segment_desc& s, int kv_dtype, const vo
     if (!fitted_[i]) fitted_now.push_back(i);
   if (fitted_now.empty()) return fitted_now;  // the usual case
   // history.rs:256-262: fit on the whole first segment, every unfitted layer,
-  // on the device (kernels_qvg_fit.cu), in chunks of ~1 GB of scratch
+  // on the device (kernels_qvg_fit.cu), in chunks of ~4 GB of scratch
   const uint64_t L = s.image_tokens + s.text_tokens;
   const size_t per = qvg_fit_scratch_bytes(L, int(D_), q_E_);
   const size_t cb_head = size_t(q_stages_) * q_E_ * D_;
@@ -508,7 +508,7 @@ std::vector<int> Bank::fit_qvg(const nkv_segment_desc& s, int kv_dtype, const vo
       for (int64_t h = 0; h < H_; ++h)
         tasks.push_back({side ? v[i] : k[i], cb_dev_ + cb_layer_ * i + (cb_layer_ / 2) * side + cb_head * h,
                          nullptr, nullptr, nullptr, nullptr, cfg_.qvg.codebook_seed + uint64_t(h), int32_t(h)});
-  const size_t chunk = std::max<size_t>(1, std::min(tasks.size(), (size_t(1) << 30) / per));
+  const size_t chunk = std::max<size_t>(1, std::min(tasks.size(), (size_t(4) << 30) / per));
   unsigned char* scratch = nullptr;
   QvgFitTask* d_tasks = nullptr;
   NKV_CUDA(cudaMalloc(&scratch, chunk * per));
@@ -534,7 +534,9 @@ std::vector<int> Bank::fit_qvg(const nkv_segment_desc& s, int kv_dtype, const vo
         t.codes = p;
       }
       NKV_CUDA(cudaMemcpyAsync(d_tasks, tasks.data() + c0, m * sizeof(QvgFitTask), cudaMemcpyHostToDevice, stream_));
+      tbegin(NKV_KERNEL_QVG_FIT);
       NKV_CUDA(launch_qvg_fit(d_tasks, int(m), kv_dtype, L, int(H_), int(D_), q_stages_, q_E_, stream_));
+      tend(NKV_KERNEL_QVG_FIT);
       NKV_CUDA(cudaStreamSynchronize(stream_));  // the host task array is reused by the next chunk
     }
     for (int i : fitted_now)

@@ -25,6 +25,21 @@ namespace nkv {
 namespace {
 
 constexpr int FT = 256;  // threads per fit
+constexpr size_t kFitCountsBytes = 256 * sizeof(int);  // E <= 256 (8 bits per stage)
+constexpr size_t kFitSharedSums = 40 * 1024;           // Lloyd sums in shared memory up to this size
+constexpr size_t kFitSharedDmin = 96 * 1024;           // farthest-point distances likewise (n <= 12,288)
+
+// Dynamic shared memory of one fit: counts, then the Lloyd sums and the
+// farthest-point distances when each fits its budget (else global scratch).
+__host__ __device__ size_t fit_smem_bytes(uint64_t n, int D, int E, size_t* sums_off, size_t* dmin_off) {
+  size_t off = kFitCountsBytes;
+  const size_t sums = (size_t)E * D * 8, dmin = (size_t)n * 8;
+  *sums_off = sums <= kFitSharedSums ? off : 0;
+  off += sums <= kFitSharedSums ? sums : 0;
+  *dmin_off = dmin <= kFitSharedDmin ? off : 0;
+  off += dmin <= kFitSharedDmin ? dmin : 0;
+  return off;
+}
 
 struct SplitMix64 {
   uint64_t state;
@@ -59,17 +74,71 @@ __device__ int nearest_row(const float* cb, int E, int D, const float* x) {
   return best;
 }
 
+// head_dim 128 (the default): a token's residual row lives in registers for
+// a whole pass, loaded with 32 vector loads issued up front.
+constexpr int RD = 128;
+struct Row128 {
+  float4 v[RD / 4];
+};
+__device__ __forceinline__ void load_row(const float* r, Row128& x) {
+#pragma unroll
+  for (int k = 0; k < RD / 4; ++k) x.v[k] = reinterpret_cast<const float4*>(r)[k];
+}
+// sequential f64 sum_d (x_d - c_d)^2 over float4 chunks [K0, K1), continuing
+// acc (compile-time bounds keep the row in registers)
+template <int K0, int K1>
+__device__ __forceinline__ double dist_chunks(const Row128& x, const float* c, double acc) {
+#pragma unroll
+  for (int k = K0; k < K1; ++k) {
+    const float4 c4 = reinterpret_cast<const float4*>(c)[k];
+    double diff = __dsub_rn((double)x.v[k].x, (double)c4.x);
+    acc = __dadd_rn(acc, __dmul_rn(diff, diff));
+    diff = __dsub_rn((double)x.v[k].y, (double)c4.y);
+    acc = __dadd_rn(acc, __dmul_rn(diff, diff));
+    diff = __dsub_rn((double)x.v[k].z, (double)c4.z);
+    acc = __dadd_rn(acc, __dmul_rn(diff, diff));
+    diff = __dsub_rn((double)x.v[k].w, (double)c4.w);
+    acc = __dadd_rn(acc, __dmul_rn(diff, diff));
+  }
+  return acc;
+}
+// nearest_row for a register row; the early exit is checked every 32 values
+// (a partial sum already >= the best can only grow, so the argmin is the same)
+__device__ __forceinline__ int nearest_row128(const float* cb, int E, const Row128& x) {
+  int best = 0;
+  double best_d = __longlong_as_double(0x7FF0000000000000ll);
+  for (int e = 0; e < E; ++e) {
+    const float* c = cb + (size_t)e * RD;
+    double acc = dist_chunks<0, 8>(x, c, 0.0);
+    if (!(acc >= best_d)) acc = dist_chunks<8, 16>(x, c, acc);
+    if (!(acc >= best_d)) acc = dist_chunks<16, 24>(x, c, acc);
+    if (!(acc >= best_d)) acc = dist_chunks<24, 32>(x, c, acc);
+    if (acc < best_d) {
+      best_d = acc;
+      best = e;
+    }
+  }
+  return best;
+}
+
 }  // namespace
 
 template <int IN_DT>
-__global__ void __launch_bounds__(FT) k_qvg_fit(const QvgFitTask* __restrict__ tasks, uint64_t n, int H, int D,
+__global__ void __launch_bounds__(FT, 1) k_qvg_fit(const QvgFitTask* __restrict__ tasks, uint64_t n, int H, int D,
                                                  int stages, int E) {
-  extern __shared__ int fit_counts[];  // [E]
+  // dynamic shared memory: [E] counts, then (when they fit) the [E][D] Lloyd
+  // sums and the [n] farthest-point distances
+  extern __shared__ __align__(16) unsigned char fit_smem[];
+  size_t sums_off, dmin_off;
+  fit_smem_bytes(n, D, E, &sums_off, &dmin_off);
+  int* fit_counts = reinterpret_cast<int*>(fit_smem);
   __shared__ uint64_t s_idx;
   __shared__ int s_jitter;
   const QvgFitTask T = tasks[blockIdx.x];
   const int t = threadIdx.x;
   float* res = T.res;  // n x D
+  double* sums = sums_off ? reinterpret_cast<double*>(fit_smem + sums_off) : T.sums;
+  double* dmin = dmin_off ? reinterpret_cast<double*>(fit_smem + dmin_off) : T.dmin;
 
   // ---- residual = the committed K or V of this head, as f32
   for (uint64_t j = t; j < n * (uint64_t)D; j += FT) {
@@ -88,7 +157,7 @@ __global__ void __launch_bounds__(FT) k_qvg_fit(const QvgFitTask* __restrict__ t
     }
     // ---- farthest_point_init (qvg.rs:396-442)
     if (t == 0) s_idx = (uint64_t)(rng.uniform() * (double)n) % n;
-    for (uint64_t i = t; i < n; i += FT) T.dmin[i] = __longlong_as_double(0x7FF0000000000000ll);
+    for (uint64_t i = t; i < n; i += FT) dmin[i] = __longlong_as_double(0x7FF0000000000000ll);
     __syncthreads();
     for (int d = t; d < D; d += FT) cb[d] = res[s_idx * D + d];
     __syncthreads();
@@ -97,29 +166,40 @@ __global__ void __launch_bounds__(FT) k_qvg_fit(const QvgFitTask* __restrict__ t
       for (uint64_t i = t; i < n; i += FT) {
         const float* r = res + i * D;
         double dd = 0.0;
-        for (int d = 0; d < D; ++d) {
-          const double diff = __dsub_rn((double)r[d], (double)last[d]);
-          dd = __dadd_rn(dd, __dmul_rn(diff, diff));
+        if (D == RD) {
+          Row128 x;
+          load_row(r, x);
+          dd = dist_chunks<0, RD / 4>(x, last, 0.0);
+        } else {
+          for (int d = 0; d < D; ++d) {
+            const double diff = __dsub_rn((double)r[d], (double)last[d]);
+            dd = __dadd_rn(dd, __dmul_rn(diff, diff));
+          }
         }
-        if (dd < T.dmin[i]) T.dmin[i] = dd;
+        if (dd < dmin[i]) dmin[i] = dd;
       }
       __syncthreads();
       if (t == 0) {
         double total = 0.0;
-        for (uint64_t i = 0; i < n; ++i) total = __dadd_rn(total, T.dmin[i]);
+#pragma unroll 4
+        for (uint64_t i = 0; i < n; ++i) total = __dadd_rn(total, dmin[i]);
         if (total <= 1e-12) {
           s_jitter = 1;  // every row coincides with an entry: jitter a copy of the first
         } else {
           s_jitter = 0;
           double pick = __dmul_rn(rng.uniform(), total);
-          uint64_t idx = n - 1;
-          for (uint64_t i = 0; i < n; ++i) {
-            pick = __dsub_rn(pick, T.dmin[i]);
-            if (pick <= 0.0) {
-              idx = i;
-              break;
-            }
+          uint64_t idx = n - 1, i = 0;
+          bool found = false;
+          // the reference's scan, four loads issued ahead of the dependent subtractions
+          for (; i + 4 <= n && !found; i += 4) {
+            const double d0 = dmin[i], d1 = dmin[i + 1], d2 = dmin[i + 2], d3 = dmin[i + 3];
+            if ((pick = __dsub_rn(pick, d0)) <= 0.0) idx = i, found = true;
+            else if ((pick = __dsub_rn(pick, d1)) <= 0.0) idx = i + 1, found = true;
+            else if ((pick = __dsub_rn(pick, d2)) <= 0.0) idx = i + 2, found = true;
+            else if ((pick = __dsub_rn(pick, d3)) <= 0.0) idx = i + 3, found = true;
           }
+          for (; i < n && !found; ++i)
+            if ((pick = __dsub_rn(pick, dmin[i])) <= 0.0) idx = i, found = true;
           s_idx = idx;
         }
       }
@@ -137,22 +217,44 @@ __global__ void __launch_bounds__(FT) k_qvg_fit(const QvgFitTask* __restrict__ t
       for (int c = t; c < E; c += FT) fit_counts[c] = 0;
       __syncthreads();
       for (uint64_t i = t; i < n; i += FT) {
-        const int c = nearest_row(cb, E, D, res + i * D);
+        int c;
+        if (D == RD) {
+          Row128 x;
+          load_row(res + i * D, x);
+          c = nearest_row128(cb, E, x);
+        } else {
+          c = nearest_row(cb, E, D, res + i * D);
+        }
         T.codes[i] = (uint8_t)c;
         atomicAdd(&fit_counts[c], 1);
       }
       __syncthreads();
       for (int d = t; d < D; d += FT) {
-        for (int c = 0; c < E; ++c) T.sums[(size_t)c * D + d] = 0.0;
-        for (uint64_t i = 0; i < n; ++i) {
-          double* sc = T.sums + (size_t)T.codes[i] * D + d;
+        for (int c = 0; c < E; ++c) sums[(size_t)c * D + d] = 0.0;
+        uint64_t i = 0;
+        for (; i + 8 <= n; i += 8) {  // eight tokens' loads ahead of the in-order adds
+          float rv[8];
+          int cv[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            cv[u] = T.codes[i + u];
+            rv[u] = res[(i + u) * D + d];
+          }
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            double* sc = sums + (size_t)cv[u] * D + d;
+            *sc = __dadd_rn(*sc, (double)rv[u]);
+          }
+        }
+        for (; i < n; ++i) {
+          double* sc = sums + (size_t)T.codes[i] * D + d;
           *sc = __dadd_rn(*sc, (double)res[i * D + d]);
         }
       }
       __syncthreads();
       for (int j = t; j < E * D; j += FT) {
         const int c = j / D;
-        if (fit_counts[c] > 0) cb[j] = __double2float_rn(__ddiv_rn(T.sums[j], (double)fit_counts[c]));
+        if (fit_counts[c] > 0) cb[j] = __double2float_rn(__ddiv_rn(sums[j], (double)fit_counts[c]));
       }
       __syncthreads();
     }
@@ -160,8 +262,20 @@ __global__ void __launch_bounds__(FT) k_qvg_fit(const QvgFitTask* __restrict__ t
     if (s + 1 < stages) {
       for (uint64_t i = t; i < n; i += FT) {
         float* r = res + i * D;
-        const float* c = cb + (size_t)nearest_row(cb, E, D, r) * D;
-        for (int d = 0; d < D; ++d) r[d] = __fsub_rn(r[d], c[d]);
+        if (D == RD) {
+          Row128 x;
+          load_row(r, x);
+          const float4* c = reinterpret_cast<const float4*>(cb + (size_t)nearest_row128(cb, E, x) * RD);
+#pragma unroll
+          for (int k = 0; k < RD / 4; ++k) {
+            const float4 c4 = c[k];
+            reinterpret_cast<float4*>(r)[k] = make_float4(__fsub_rn(x.v[k].x, c4.x), __fsub_rn(x.v[k].y, c4.y),
+                                                          __fsub_rn(x.v[k].z, c4.z), __fsub_rn(x.v[k].w, c4.w));
+          }
+        } else {
+          const float* c = cb + (size_t)nearest_row(cb, E, D, r) * D;
+          for (int d = 0; d < D; ++d) r[d] = __fsub_rn(r[d], c[d]);
+        }
       }
       __syncthreads();
     }
@@ -176,12 +290,24 @@ size_t qvg_fit_scratch_bytes(uint64_t n, int D, int E) {
 cudaError_t launch_qvg_fit(const QvgFitTask* tasks_dev, int n_tasks, int in_dtype, uint64_t n, int H, int D,
                            int stages, int E, cudaStream_t s) {
   if (n_tasks == 0) return cudaSuccess;
-  const size_t smem = (size_t)E * sizeof(int);
+  size_t so, dof;
+  const size_t smem = fit_smem_bytes(n, D, E, &so, &dof);
+  cudaError_t e = cudaSuccess;
   switch (in_dtype) {
-    case F32: k_qvg_fit<F32><<<n_tasks, FT, smem, s>>>(tasks_dev, n, H, D, stages, E); break;
-    case BF16: k_qvg_fit<BF16><<<n_tasks, FT, smem, s>>>(tasks_dev, n, H, D, stages, E); break;
-    default: k_qvg_fit<F16><<<n_tasks, FT, smem, s>>>(tasks_dev, n, H, D, stages, E); break;
+    case F32:
+      e = cudaFuncSetAttribute(k_qvg_fit<F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e == cudaSuccess) k_qvg_fit<F32><<<n_tasks, FT, smem, s>>>(tasks_dev, n, H, D, stages, E);
+      break;
+    case BF16:
+      e = cudaFuncSetAttribute(k_qvg_fit<BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e == cudaSuccess) k_qvg_fit<BF16><<<n_tasks, FT, smem, s>>>(tasks_dev, n, H, D, stages, E);
+      break;
+    default:
+      e = cudaFuncSetAttribute(k_qvg_fit<F16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e == cudaSuccess) k_qvg_fit<F16><<<n_tasks, FT, smem, s>>>(tasks_dev, n, H, D, stages, E);
+      break;
   }
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 

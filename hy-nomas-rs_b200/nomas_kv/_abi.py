@@ -25,8 +25,9 @@ NKV_SAMPLING_RECENT, NKV_SAMPLING_UNIFORM, NKV_SAMPLING_RECENT_MIX, NKV_SAMPLING
 
 NKV_KERNEL_QUANTIZE, NKV_KERNEL_FLOAT_ARCHIVE, NKV_KERNEL_QVG_ENCODE, NKV_KERNEL_GATHER = 0, 1, 2, 3
 NKV_KERNEL_SEGMENT_DECODE = 4
-NKV_KERNEL_COUNT = 5
-KERNEL_NAMES = ("quantize", "float_archive", "qvg_encode", "gather", "segment_decode")
+NKV_KERNEL_QVG_FIT = 5
+NKV_KERNEL_COUNT = 6
+KERNEL_NAMES = ("quantize", "float_archive", "qvg_encode", "gather", "segment_decode", "qvg_fit")
 NKV_NOALLOC_MAX_LAYERS = 64
 
 

@@ -146,7 +146,8 @@ enum {
   NKV_KERNEL_QVG_ENCODE = 2,    /* QVG commit: residual VQ encode of video tokens    */
   NKV_KERNEL_GATHER = 3,        /* rebuild: gather + dequant/decode                  */
   NKV_KERNEL_SEGMENT_DECODE = 4, /* nkv_bank_decode_segment: the same gather kernel  */
-  NKV_KERNEL_COUNT = 5
+  NKV_KERNEL_QVG_FIT = 5,       /* first QVG commit: device codebook fit             */
+  NKV_KERNEL_COUNT = 6
 };
 
 typedef struct nkv_bank nkv_bank;
