@@ -301,19 +301,31 @@ __device__ __forceinline__ float4 pick4(const float4 (&p)[4], uint32_t c) {
   return b1 ? hi : lo;
 }
 
+// One output row: the 4 values of this lane for the token whose code is `code`.
+template <int OUT_DT, bool FAST>
+__device__ __forceinline__ void decode4(void* out, uint64_t o, const QvgTables& T, const float4 (&p3)[4], int hh,
+                                        int d, uint32_t code) {
+  const float4 x = *reinterpret_cast<const float4*>(&T.q01[hh][(code & 3u) * 4 + ((code >> 2) & 3u)][d]);
+  const float4 y = *reinterpret_cast<const float4*>(&T.p2[hh][(code >> 4) & 3u][d]);
+  const float4 z = pick4(p3, code >> 6);
+  store4<OUT_DT, FAST>(out, o, __fadd_rn(__fadd_rn(x.x, y.x), z.x), __fadd_rn(__fadd_rn(x.y, y.y), z.y),
+                       __fadd_rn(__fadd_rn(x.z, y.z), z.z), __fadd_rn(__fadd_rn(x.w, y.w), z.w));
+}
+
 template <int OUT_DT, bool FAST>
 __device__ __forceinline__ void decode_rows(void* out, const QvgTables& T, const float4 (&p3)[4], int ntok,
                                             int64_t dst0, int H, int h, int hh, int tpar, int lane) {
   const int d = 4 * lane;
-  for (int t = tpar; t < ntok; t += 2) {
-    const uint32_t code = T.code[t * kQvgHeads + hh];  // stage s at bits 2s, 2s+1
-    const float4 x = *reinterpret_cast<const float4*>(&T.q01[hh][(code & 3u) * 4 + ((code >> 2) & 3u)][d]);
-    const float4 y = *reinterpret_cast<const float4*>(&T.p2[hh][(code >> 4) & 3u][d]);
-    const float4 z = pick4(p3, code >> 6);
-    store4<OUT_DT, FAST>(out, ((uint64_t)(dst0 + t) * H + h) * kQD + d, __fadd_rn(__fadd_rn(x.x, y.x), z.x),
-                         __fadd_rn(__fadd_rn(x.y, y.y), z.y), __fadd_rn(__fadd_rn(x.z, y.z), z.z),
-                         __fadd_rn(__fadd_rn(x.w, y.w), z.w));
+  const uint64_t step = (uint64_t)2 * H * kQD;  // two tokens on
+  uint64_t o = ((uint64_t)(dst0 + tpar) * H + h) * kQD + d;
+  int t = tpar;
+  // two tokens per iteration (this warp's tokens are tpar, tpar + 2, ...)
+  for (; t + 2 < ntok; t += 4, o += 2 * step) {
+    const uint32_t c0 = T.code[t * kQvgHeads + hh], c1 = T.code[(t + 2) * kQvgHeads + hh];  // stage s: bits 2s, 2s+1
+    decode4<OUT_DT, FAST>(out, o, T, p3, hh, d, c0);
+    decode4<OUT_DT, FAST>(out, o + step, T, p3, hh, d, c1);
   }
+  if (t < ntok) decode4<OUT_DT, FAST>(out, o, T, p3, hh, d, T.code[t * kQvgHeads + hh]);
 }
 
 }  // namespace
