@@ -349,34 +349,43 @@ def run_gpu(args) -> None:
             hk[i].copy_(sets[s][0][i])
             hv[i].copy_(sets[s][1][i])
         host.append((hk, hv))
-    if swap:
-        stage_k, stage_v = sets[0]
-    else:
-        stage_k = [torch.empty(shape, dtype=torch.bfloat16, device=dev) for _ in range(n_layers)]
-        stage_v = [torch.empty(shape, dtype=torch.bfloat16, device=dev) for _ in range(n_layers)]
+    # Pipelined turns: turn j+1's K/V cross PCIe on a copy stream (into the
+    # other resident input set, free again) while turn j commits; commit
+    # returns only after its kernels ran, so its buffer is free for turn j+2.
     flag_host = torch.empty(1, dtype=torch.int32, pin_memory=True)
     vlen_dev = torch.empty(1, dtype=torch.int32, device=dev)
+    copy_stream = torch.cuda.Stream(dev)
+    copied = [torch.cuda.Event(), torch.cuda.Event()]
 
-    def e2e_step():
-        hk, hv = host[seg % 2]
-        for i in range(n_layers):
-            stage_k[i].copy_(hk[i], non_blocking=True)
-            stage_v[i].copy_(hv[i], non_blocking=True)
-        step(stage_k, stage_v)
-        # device -> host read of the step's result: the working-set length
-        vlen_dev.fill_(bank.layer(0).valid_len())
-        flag_host.copy_(vlen_dev, non_blocking=True)
+    def enqueue_copy(j: int, b: int):
+        hk, hv = host[(seg + j) % 2]
+        copy_stream.wait_stream(stream)  # after the last reader of buffer b
+        with torch.cuda.stream(copy_stream):
+            for i in range(n_layers):
+                sets[b][0][i].copy_(hk[i], non_blocking=True)
+                sets[b][1][i].copy_(hv[i], non_blocking=True)
+        copied[b].record(copy_stream)
 
-    for _ in range(args.warmup):
-        e2e_step()
+    def e2e_turns(n_turns: int):
+        enqueue_copy(0, 0)
+        for j in range(n_turns):
+            b = j % 2
+            if j + 1 < n_turns:
+                enqueue_copy(j + 1, 1 - b)
+            stream.wait_event(copied[b])
+            step(*sets[b])
+            # device -> host read of the turn's result: the working-set length
+            vlen_dev.fill_(bank.layer(0).valid_len())
+            flag_host.copy_(vlen_dev, non_blocking=True)
+
+    e2e_turns(args.warmup)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for _ in range(e2e_steps):
-        e2e_step()
+    e2e_turns(e2e_steps)
     e1.record(stream)
     torch.cuda.synchronize()
     ems = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
