@@ -164,16 +164,21 @@ __global__ void __launch_bounds__(256) k_int8_quantize(const QuantJob* __restric
 //    every value of the row (x <= peak, s = peak * (1 + O(2^-23)) / 127), so
 //    the reference's clamp to [-127, 127] never binds.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ uint32_t max_u16x2(uint32_t a, uint32_t b) {
+// Lane-wise max(|a|, |b|) of two bf16 pairs (the sign bit is the XOR of the
+// operands' and is masked off by the caller); a NaN lane yields a NaN, so
+// one instruction per pair serves both the peak and the non-finite scan.
+__device__ __forceinline__ uint32_t maxabs_bf16x2(uint32_t a, uint32_t b) {
   uint32_t d;
-  asm("max.u16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  asm("max.NaN.xorsign.abs.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
   return d;
 }
 
-template <int G, int R>
+template <int G, int R, int V>
 __global__ void __launch_bounds__(256) k_int8_quantize_bf16(const QuantJob* __restrict__ jobs, uint64_t rows,
                                                             uint64_t in_row_offset, uint32_t* __restrict__ flag) {
-  constexpr int D = 16 * G;
+  // G threads per row, V bf16 values per thread (V = 16 or 32)
+  constexpr int D = V * G;
+  constexpr int NW = V / 8;  // 16-byte loads per thread and row
   const QuantJob J = jobs[blockIdx.y >> 1];
   const int side = blockIdx.y & 1;
   const uint4* in = reinterpret_cast<const uint4*>(side ? J.v : J.k);
@@ -182,30 +187,34 @@ __global__ void __launch_bounds__(256) k_int8_quantize_bf16(const QuantJob* __re
   const int sub = threadIdx.x % G;
   const uint64_t rows_per_pass = blockDim.x / G;
   const float inv127 = (float)(1.0 / 127.0);
-  const float M = 12582912.0f;  // 1.5 * 2^23
-  uint32_t worst = 0;           // max |bits| seen: >= 0x7F80 means inf / NaN
+  uint32_t worst = 0;  // max |bits| seen: >= 0x7F80 means inf / NaN
   for (uint64_t base = (uint64_t)blockIdx.x * rows_per_pass * R; base < rows;
        base += (uint64_t)gridDim.x * rows_per_pass * R) {
-    uint4 w[R][2];
+    uint4 w[R][NW];
 #pragma unroll
     for (int r = 0; r < R; ++r) {
       const uint64_t row = base + r * rows_per_pass + threadIdx.x / G;
       if (row < rows) {
-        const uint4* p = in + ((in_row_offset + row) * D + sub * 16) / 8;
-        w[r][0] = __ldg(p);
-        w[r][1] = __ldg(p + 1);
+        const uint4* p = in + ((in_row_offset + row) * D + sub * V) / 8;
+#pragma unroll
+        for (int k = 0; k < NW; ++k) w[r][k] = __ldg(p + k);
       } else {
-        w[r][0] = w[r][1] = make_uint4(0, 0, 0, 0);
+#pragma unroll
+        for (int k = 0; k < NW; ++k) w[r][k] = make_uint4(0, 0, 0, 0);
       }
     }
 #pragma unroll
     for (int r = 0; r < R; ++r) {
       const uint64_t row = base + r * rows_per_pass + threadIdx.x / G;
-      const uint32_t ws[8] = {w[r][0].x, w[r][0].y, w[r][0].z, w[r][0].w,
-                              w[r][1].x, w[r][1].y, w[r][1].z, w[r][1].w};
+      uint32_t ws[V / 2];
+#pragma unroll
+      for (int k = 0; k < NW; ++k) {
+        ws[4 * k] = w[r][k].x, ws[4 * k + 1] = w[r][k].y, ws[4 * k + 2] = w[r][k].z, ws[4 * k + 3] = w[r][k].w;
+      }
       uint32_t m2 = 0;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) m2 = max_u16x2(m2, ws[j] & 0x7FFF7FFFu);
+      for (int j = 0; j < V / 2; ++j) m2 = maxabs_bf16x2(m2, ws[j]);
+      m2 &= 0x7FFF7FFFu;
       uint32_t m = max(m2 & 0xFFFFu, m2 >> 16);
 #pragma unroll
       for (int o = G / 2; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
@@ -214,21 +223,24 @@ __global__ void __launch_bounds__(256) k_int8_quantize_bf16(const QuantJob* __re
       const float peak = __uint_as_float(m << 16);
       // scale = where(peak > 0, peak * (f32)(1/127) + 0, 1)   (int8.rs:72)
       const float s = peak > 0.0f ? __fadd_rn(__fmul_rn(peak, inv127), 0.0f) : 1.0f;
-      uint4 o;
+      uint4* qo = q + (row * D + sub * V) / 16;
       if (s >= FLT_MIN && s <= 1e37f) {
         const float rc = __frcp_rn(s);
-        uint32_t c[16];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          c[2 * j] = code_bits(__uint_as_float(ws[j] << 16), s, rc);
-          c[2 * j + 1] = code_bits(__uint_as_float(ws[j] & 0xFFFF0000u), s, rc);
+        for (int k = 0; k < V / 16; ++k) {
+          uint32_t c[16];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            c[2 * j] = code_bits(__uint_as_float(ws[8 * k + j] << 16), s, rc);
+            c[2 * j + 1] = code_bits(__uint_as_float(ws[8 * k + j] & 0xFFFF0000u), s, rc);
+          }
+          qo[k] = make_uint4(pack4(c[0], c[1], c[2], c[3]), pack4(c[4], c[5], c[6], c[7]),
+                             pack4(c[8], c[9], c[10], c[11]), pack4(c[12], c[13], c[14], c[15]));
         }
-        o = make_uint4(pack4(c[0], c[1], c[2], c[3]), pack4(c[4], c[5], c[6], c[7]),
-                       pack4(c[8], c[9], c[10], c[11]), pack4(c[12], c[13], c[14], c[15]));
       } else {
-        o = quant16_bf16_exact(w[r][0], w[r][1], s);
+#pragma unroll
+        for (int k = 0; k < V / 16; ++k) qo[k] = quant16_bf16_exact(w[r][2 * k], w[r][2 * k + 1], s);
       }
-      q[(row * D + sub * 16) / 16] = o;
       if (sub == 0) sc[row] = s;
     }
   }
@@ -287,11 +299,11 @@ static cudaError_t quantize_dispatch(const QuantJob* jobs, int n_jobs, uint64_t 
     constexpr int R2 = 2;
     if (vec_ok) {
       switch (D) {
-        case 16: k_int8_quantize_bf16<1, R2><<<grid_for(threads / 1 * R2), threads, 0, s>>>(jobs, rows, off, flag); return cudaGetLastError();
-        case 32: k_int8_quantize_bf16<2, R2><<<grid_for(threads / 2 * R2), threads, 0, s>>>(jobs, rows, off, flag); return cudaGetLastError();
-        case 64: k_int8_quantize_bf16<4, R2><<<grid_for(threads / 4 * R2), threads, 0, s>>>(jobs, rows, off, flag); return cudaGetLastError();
-        case 128: k_int8_quantize_bf16<8, R2><<<grid_for(threads / 8 * R2), threads, 0, s>>>(jobs, rows, off, flag); return cudaGetLastError();
-        case 256: k_int8_quantize_bf16<16, R2><<<grid_for(threads / 16 * R2), threads, 0, s>>>(jobs, rows, off, flag); return cudaGetLastError();
+        case 16: k_int8_quantize_bf16<1, R2, 16><<<grid_for(threads / 1 * R2), threads, 0, s>>>(jobs, rows, off, flag); return cudaGetLastError();
+        case 32: k_int8_quantize_bf16<2, R2, 16><<<grid_for(threads / 2 * R2), threads, 0, s>>>(jobs, rows, off, flag); return cudaGetLastError();
+        case 64: k_int8_quantize_bf16<2, R2, 32><<<grid_for(threads / 2 * R2), threads, 0, s>>>(jobs, rows, off, flag); return cudaGetLastError();
+        case 128: k_int8_quantize_bf16<4, R2, 32><<<grid_for(threads / 4 * R2), threads, 0, s>>>(jobs, rows, off, flag); return cudaGetLastError();
+        case 256: k_int8_quantize_bf16<8, R2, 32><<<grid_for(threads / 8 * R2), threads, 0, s>>>(jobs, rows, off, flag); return cudaGetLastError();
         default: break;
       }
     }
