@@ -145,6 +145,14 @@ int nkv_bank_kernel_stats(nkv_bank* bank, nkv_kernel_stat* out, int32_t reset) {
   });
 }
 
+int nkv_bank_save(nkv_bank* bank, const char* path) {
+  return guarded([&] { bank_of(bank).save(path); });
+}
+
+int nkv_bank_load(nkv_bank* bank, const char* path) {
+  return guarded([&] { bank_of(bank).load(path); });
+}
+
 int nkv_cache_working_set(const nkv_bank* bank, int32_t layer, const void** k_dev, const void** v_dev,
                           uint64_t* valid_len) {
   return guarded([&] {

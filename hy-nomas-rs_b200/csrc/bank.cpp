@@ -13,8 +13,9 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdio>
 #include <cstring>
-#include <thread>
+#include <memory>
 
 
 namespace nkv {
@@ -689,10 +690,12 @@ void Bank::commit(const nkv_segment_desc& s, int kv_dtype, const void* const* k,
       fresh = nullptr;
       fail(NKV_ERR_MSG, std::string("cannot quantize non-finite ") + (k_bad ? "k" : "v") + " values");
     }
+    if (parked_) changed_while_parked_ = true;
     if (!plan_ok) {
       // like the reference, the segment stays archived when rebuild fails
       if (fresh) cudaFree(fresh);
       fresh = nullptr;
+      ws_current_ = false;
       throw plan_err;
     }
     if (fresh) {
@@ -702,6 +705,7 @@ void Bank::commit(const nkv_segment_desc& s, int kv_dtype, const void* const* k,
     }
     layout_ = std::move(plan.layout);
     valid_ = plan.valid;
+    ws_current_ = true;
     m_.h2d_bytes += valid_ * B_ * H_ * D_ * dtype_size(dtype_) * 2;  // history.rs:438-439
     m_.rebuilds += 1;
   } catch (const Error& e) {
@@ -750,6 +754,7 @@ void Bank::rebuild_now() {
   }
   layout_ = std::move(plan.layout);
   valid_ = plan.valid;
+  ws_current_ = true;
   m_.h2d_bytes += valid_ * B_ * H_ * D_ * dtype_size(dtype_) * 2;
   m_.rebuilds += 1;
 }
@@ -767,6 +772,8 @@ void Bank::rollback() {
     fail(NKV_ERR_CACHE_STATE, "archive does not match the frame timeline");
   total_frames_ -= last.desc.frame_count;
   m_.archived_segments = m_.archived_segments > 0 ? m_.archived_segments - 1 : 0;
+  if (parked_) changed_while_parked_ = true;
+  ws_current_ = false;  // until the rebuild below succeeds
   rebuild_now();
   m_.rollbacks += 1;
 }
@@ -776,6 +783,8 @@ void Bank::rollback() {
 void Bank::park() {
   if (!cfg_.phase_swap || parked_) return;
   DeviceScope ds(device_);
+  p_ws_current_ = ws_current_;
+  changed_while_parked_ = false;
   const size_t plane = size_t(B_) * valid_ * H_ * D_ * dtype_size(dtype_);
   cudaEvent_t ready;
   NKV_CUDA(cudaEventCreateWithFlags(&ready, cudaEventDisableTiming));
@@ -842,6 +851,7 @@ void Bank::unpark() {
   }
   layout_ = p_layout_;
   valid_ = p_valid_;
+  ws_current_ = p_ws_current_ && !changed_while_parked_;
   m_.h2d_bytes += p_bytes_;
   parked_ = false;
 }
@@ -1051,6 +1061,203 @@ void Bank::kernel_stats(nkv_kernel_stat* out, bool reset) {
   for (int i = 0; i < NKV_KERNEL_COUNT; ++i) out[i] = stats_[i];
   if (reset)
     for (auto& s : stats_) s = nkv_kernel_stat{0, 0.0};
+}
+
+// ---------------------------------------------------------------------------
+// Archive persistence.  File layout (host byte order):
+//   "NKVBANK1"  u32 version (1)
+//   config: storage, qvg{stages, bits, block, text_as_int8, seed}, sampling,
+//           gamma (f64 bits), has_capacity, capacity, past_frames, phase_swap
+//   geometry: n_layers, layer_begin, batch, heads, head_dim, dtype
+//   u64 total_frames, u64 tokens_per_frame, the 8 counters
+//   u64 n_segments; per segment: the 6 descriptor fields, u64 bytes, the
+//       segment's device slab (every local layer's payload, as laid out here)
+//   QVG only: n_layers fitted flags (u8), then the codebooks (f32)
+//   "NKVEND01"
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr char kMagic[8] = {'N', 'K', 'V', 'B', 'A', 'N', 'K', '1'};
+constexpr char kEnd[8] = {'N', 'K', 'V', 'E', 'N', 'D', '0', '1'};
+constexpr size_t kIoChunk = size_t(64) << 20;
+
+struct File {
+  FILE* f = nullptr;
+  std::string path;
+  ~File() {
+    if (f) fclose(f);
+  }
+  void put(const void* p, size_t n) {
+    if (n && fwrite(p, 1, n, f) != n) fail(NKV_ERR_MSG, "write to " + path + " failed");
+  }
+  void get(void* p, size_t n) {
+    if (n && fread(p, 1, n, f) != n) fail(NKV_ERR_MSG, path + " is truncated or unreadable");
+  }
+  template <class T>
+  void put_v(T v) { put(&v, sizeof(T)); }
+  template <class T>
+  T get_v() {
+    T v;
+    get(&v, sizeof(T));
+    return v;
+  }
+};
+
+void put_config(File& f, const nkv_cache_config& c) {
+  f.put_v<int32_t>(c.storage);
+  f.put_v<int32_t>(c.qvg.stages), f.put_v<int32_t>(c.qvg.bits_per_stage), f.put_v<int32_t>(c.qvg.block_size);
+  f.put_v<int32_t>(c.qvg.text_as_int8), f.put_v<uint64_t>(c.qvg.codebook_seed);
+  f.put_v<int32_t>(c.sampling), f.put_v<double>(c.gamma);
+  f.put_v<int32_t>(c.has_capacity), f.put_v<uint64_t>(c.capacity), f.put_v<uint64_t>(c.past_frames);
+  f.put_v<int32_t>(c.phase_swap);
+}
+
+bool same_config(File& f, const nkv_cache_config& c) {
+  bool same = f.get_v<int32_t>() == c.storage;
+  same &= f.get_v<int32_t>() == c.qvg.stages;
+  same &= f.get_v<int32_t>() == c.qvg.bits_per_stage;
+  same &= f.get_v<int32_t>() == c.qvg.block_size;
+  same &= f.get_v<int32_t>() == c.qvg.text_as_int8;
+  same &= f.get_v<uint64_t>() == c.qvg.codebook_seed;
+  same &= f.get_v<int32_t>() == c.sampling;
+  const double g = f.get_v<double>();
+  same &= std::memcmp(&g, &c.gamma, sizeof(double)) == 0;
+  same &= f.get_v<int32_t>() == c.has_capacity;
+  same &= f.get_v<uint64_t>() == c.capacity;
+  same &= f.get_v<uint64_t>() == c.past_frames;
+  same &= f.get_v<int32_t>() == c.phase_swap;
+  return same;
+}
+
+}  // namespace
+
+void Bank::save(const char* path) {
+  if (!path) fail(NKV_ERR_ARGUMENT, "null path");
+  if (parked_) fail(NKV_ERR_CACHE_STATE, "cannot save a parked cache; unpark it first");
+  if (!ws_current_)
+    fail(NKV_ERR_CACHE_STATE,
+         "cannot save: the working set is not the rebuild of the archive (a rebuild failed, or a commit or "
+         "rollback happened while parked)");
+  DeviceScope ds(device_);
+  NKV_CUDA(cudaStreamSynchronize(stream_));
+  File f;
+  f.path = path;
+  f.f = std::fopen(path, "wb");
+  if (!f.f) fail(NKV_ERR_MSG, std::string("cannot open ") + path + " for writing");
+  f.put(kMagic, sizeof(kMagic));
+  f.put_v<uint32_t>(1);
+  put_config(f, cfg_);
+  f.put_v<int32_t>(n_layers_), f.put_v<int32_t>(layer_begin_);
+  f.put_v<int64_t>(B_), f.put_v<int64_t>(H_), f.put_v<int64_t>(D_), f.put_v<int32_t>(dtype_);
+  f.put_v<uint64_t>(total_frames_), f.put_v<uint64_t>(tpf_);
+  f.put(&m_, sizeof(m_));
+  f.put_v<uint64_t>(archive_.size());
+  std::vector<unsigned char> buf;
+  for (const Rec& r : archive_) {
+    f.put(&r.desc, sizeof(r.desc));
+    const uint64_t bytes = uint64_t(r.layer_stride) * n_layers_;
+    f.put_v<uint64_t>(bytes);
+    for (uint64_t o = 0; o < bytes; o += kIoChunk) {
+      const size_t n = size_t(std::min<uint64_t>(kIoChunk, bytes - o));
+      buf.resize(n);
+      NKV_CUDA(cudaMemcpy(buf.data(), r.slab + o, n, cudaMemcpyDeviceToHost));
+      f.put(buf.data(), n);
+    }
+  }
+  if (cfg_.storage == NKV_STORAGE_QVG) {
+    f.put(fitted_.data(), fitted_.size());
+    f.put(cb_host_.data(), cb_host_.size() * sizeof(float));
+  }
+  f.put(kEnd, sizeof(kEnd));
+  if (std::fflush(f.f) != 0) fail(NKV_ERR_MSG, std::string("write to ") + path + " failed");
+}
+
+void Bank::load(const char* path) {
+  if (!path) fail(NKV_ERR_ARGUMENT, "null path");
+  if (!archive_.empty() || total_frames_ != 0 || parked_)
+    fail(NKV_ERR_CACHE_STATE, "load needs a fresh cache (nothing committed yet)");
+  DeviceScope ds(device_);
+  File f;
+  f.path = path;
+  f.f = std::fopen(path, "rb");
+  if (!f.f) fail(NKV_ERR_MSG, std::string("cannot open ") + path);
+  char magic[8];
+  f.get(magic, sizeof(magic));
+  if (std::memcmp(magic, kMagic, sizeof(magic)) != 0 || f.get_v<uint32_t>() != 1)
+    fail(NKV_ERR_MSG, std::string(path) + " is not a saved cache archive");
+  bool same = same_config(f, cfg_);
+  same &= f.get_v<int32_t>() == n_layers_;
+  same &= f.get_v<int32_t>() == layer_begin_;
+  same &= f.get_v<int64_t>() == B_;
+  same &= f.get_v<int64_t>() == H_;
+  same &= f.get_v<int64_t>() == D_;
+  same &= f.get_v<int32_t>() == dtype_;
+  if (!same)
+    fail(NKV_ERR_INVALID_CONFIG, std::string(path) + " was saved by a cache with a different configuration or geometry");
+  const uint64_t total_frames = f.get_v<uint64_t>(), tpf = f.get_v<uint64_t>();
+  nkv_metrics m;
+  f.get(&m, sizeof(m));
+  const uint64_t n = f.get_v<uint64_t>();
+  std::vector<Rec> recs;
+  std::vector<unsigned char> buf;
+  try {
+    uint64_t frames = 0;
+    for (uint64_t i = 0; i < n; ++i) {
+      nkv_segment_desc d;
+      f.get(&d, sizeof(d));
+      if (d.frame_start != frames || d.frame_count == 0 || d.image_tokens == 0 ||
+          (tpf && d.image_tokens != d.frame_count * tpf) || (i > 0 && d.segment_index <= recs.back().desc.segment_index))
+        fail(NKV_ERR_MSG, std::string(path) + ": segment " + std::to_string(i) + " breaks the frame timeline");
+      frames += d.frame_count;
+      Rec r = make_rec(d);
+      const uint64_t bytes = f.get_v<uint64_t>();
+      if (bytes != uint64_t(r.layer_stride) * n_layers_)
+        fail(NKV_ERR_MSG, std::string(path) + ": segment " + std::to_string(i) + " has the wrong payload size");
+      r.slab = arena_.push(size_t(bytes));
+      recs.push_back(r);
+      for (uint64_t o = 0; o < bytes; o += kIoChunk) {
+        const size_t c = size_t(std::min<uint64_t>(kIoChunk, bytes - o));
+        buf.resize(c);
+        f.get(buf.data(), c);
+        NKV_CUDA(cudaMemcpy(r.slab + o, buf.data(), c, cudaMemcpyHostToDevice));
+      }
+    }
+    if (frames != total_frames) fail(NKV_ERR_MSG, std::string(path) + ": the segments do not cover the timeline");
+    std::vector<char> fitted(fitted_.size());
+    std::vector<float> cb(cb_host_.size());
+    if (cfg_.storage == NKV_STORAGE_QVG) {
+      f.get(fitted.data(), fitted.size());
+      f.get(cb.data(), cb.size() * sizeof(float));
+    }
+    char end[8];
+    f.get(end, sizeof(end));
+    if (std::memcmp(end, kEnd, sizeof(end)) != 0) fail(NKV_ERR_MSG, std::string(path) + " is corrupt (no end marker)");
+    // install
+    if (cfg_.storage == NKV_STORAGE_QVG) {
+      fitted_ = fitted;
+      cb_host_ = cb;
+      NKV_CUDA(cudaMemcpy(cb_dev_, cb_host_.data(), cb_host_.size() * sizeof(float), cudaMemcpyHostToDevice));
+    }
+    archive_ = recs;
+    total_frames_ = total_frames;
+    tpf_ = tpf;
+    if (!archive_.empty()) rebuild_now();
+    m_ = m;  // the counters as saved (the rebuild above is not a reference rebuild)
+    ws_current_ = true;
+  } catch (...) {
+    // back to a fresh cache
+    archive_.clear();
+    for (size_t i = 0; i < recs.size(); ++i) arena_.pop();
+    total_frames_ = 0, tpf_ = 0;
+    m_ = nkv_metrics{};
+    layout_.clear();
+    valid_ = 0;
+    if (cfg_.storage == NKV_STORAGE_QVG) {
+      std::fill(fitted_.begin(), fitted_.end(), 0);
+      std::fill(cb_host_.begin(), cb_host_.end(), 0.0f);
+    }
+    throw;
+  }
 }
 
 }  // namespace nkv

@@ -141,6 +141,12 @@ class Bank {
   void set_timing(bool on);
   void kernel_stats(nkv_kernel_stat* out, bool reset);
 
+  // Archive persistence (no counterpart in the reference, whose archive is
+  // in memory only): the timeline, counters, QVG codebooks and every archived
+  // payload; load rebuilds the working set.
+  void save(const char* path);
+  void load(const char* path);
+
   int n_layers() const { return n_layers_; }
 
  private:
@@ -175,6 +181,10 @@ class Bank {
   uint64_t valid_ = 0;
 
   bool parked_ = false;
+  // the working set is the rebuild of the current archive (false after a
+  // failed rebuild, or after unpark restored a set older than the archive)
+  bool ws_current_ = true;
+  bool p_ws_current_ = true, changed_while_parked_ = false;
   std::vector<nkv_segment_layout> p_layout_;
   uint64_t p_valid_ = 0, p_bytes_ = 0;
   std::vector<unsigned char*> p_host_;

@@ -479,6 +479,15 @@ class KvBank:
     def set_timing(self, on: bool) -> None:
         _check(lib().nkv_bank_set_timing(self._h, int(on)))
 
+    # -- archive persistence (no counterpart in the reference)
+    def save(self, path) -> None:
+        """Write the archive, timeline, counters and QVG codebooks to `path`."""
+        _check(lib().nkv_bank_save(self._h, str(path).encode()))
+
+    def load(self, path) -> None:
+        """Restore a saved archive into this fresh bank and rebuild the working set."""
+        _check(lib().nkv_bank_load(self._h, str(path).encode()))
+
     def kernel_stats(self, reset: bool = False) -> dict:
         arr = (_abi.nkv_kernel_stat * _abi.NKV_KERNEL_COUNT)()
         _check(lib().nkv_bank_kernel_stats(self._h, arr, int(reset)))

@@ -129,6 +129,8 @@ SIGNATURES = {
     "nkv_bank_decode_segment": (C.c_int, [P, U64, C.POINTER(P), C.POINTER(P)]),
     "nkv_bank_set_timing": (C.c_int, [P, I32]),
     "nkv_bank_kernel_stats": (C.c_int, [P, C.POINTER(nkv_kernel_stat), I32]),
+    "nkv_bank_save": (C.c_int, [P, C.c_char_p]),
+    "nkv_bank_load": (C.c_int, [P, C.c_char_p]),
     "nkv_cache_working_set": (C.c_int, [P, I32, C.POINTER(P), C.POINTER(P), C.POINTER(U64)]),
     "nkv_cache_layout": (C.c_int, [P, I32, C.POINTER(nkv_segment_layout), U64, C.POINTER(U64)]),
     "nkv_cache_info": (C.c_int, [P, I32, C.POINTER(nkv_cache_info_t)]),

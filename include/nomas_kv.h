@@ -219,6 +219,20 @@ int nkv_bank_decode_segment(nkv_bank* bank, uint64_t archive_pos, void* const* k
 int nkv_bank_set_timing(nkv_bank* bank, int32_t enable);
 int nkv_bank_kernel_stats(nkv_bank* bank, nkv_kernel_stat* out /* [NKV_KERNEL_COUNT] */, int32_t reset);
 
+/* Archive persistence.  No counterpart in the reference, whose archive lives
+ * in memory only.  nkv_bank_save writes the segment timeline, the counters,
+ * the QVG codebooks and every archived payload of the bank's local layers to
+ * `path`; it refuses (NKV_ERR_CACHE_STATE) while parked or while the working
+ * set is not the rebuild of the archive (after a failed rebuild, or a commit
+ * or rollback while parked).  nkv_bank_load restores such a file into a bank
+ * created with the same configuration and geometry that has committed
+ * nothing yet (else NKV_ERR_INVALID_CONFIG / NKV_ERR_CACHE_STATE), rebuilds
+ * the working set on the device and restores the counters as saved.  A file
+ * that is not a saved archive, or is truncated, is NKV_ERR_MSG and leaves the
+ * bank fresh.  Files use the host's byte order. */
+int nkv_bank_save(nkv_bank* bank, const char* path);
+int nkv_bank_load(nkv_bank* bank, const char* path);
+
 /* ----------------------------------------------------- one layer's cache -- */
 
 /* LifetimeKvCache::working_set (cache/mod.rs:168; history.rs:465-481):
