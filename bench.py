@@ -1,8 +1,8 @@
 #!/usr/bin/env python
 """Benchmark of the lifelong KV-cache hot path at 8B geometry.
 
-Workload ("Nomas-8B geometry INT8 commit+uniform
-rebuild"): 48 layers, 24 heads, head_dim 128, BF16 K/V (keys with a
+Workload (the headline configuration, "Nomas-8B geometry INT8 commit +
+uniform rebuild"): 48 layers, 24 heads, head_dim 128, BF16 K/V (keys with a
 per-channel scale exp(N(0,1))), segments of 4 latent frames x 1560 tokens +
 256 text tokens, INT8 storage, uniform history sampling of 16 past frames,
 32 archived segments.  One step is one interactive turn through the public
@@ -41,13 +41,13 @@ PAST = 16
 ARCHIVED = 32
 METRIC = "KV commit+rebuild GB/s (8B geometry, INT8, uniform rebuild)"
 METRIC_QVG = "KV commit+rebuild GB/s (8B geometry, QVG, uniform rebuild)"
-# BASELINE configs[4] (box run): the same turn with a phase-swapped cache,
+# The box-run configuration: the same turn with a phase-swapped cache,
 # park + unpark of the working set every turn, over a 64-segment archive.
 METRIC_SWAP = "KV turn GB/s incl. phase swap (8B geometry, {}, uniform rebuild, park + unpark)"
 ARCHIVED_SWAP = 64
 WORKLOADS = {"int8": "nomas-8B INT8 commit + uniform rebuild (16 past frames) + newest segment",
              "qvg": "nomas-8B QVG (frozen codebooks) commit + uniform decode-gather rebuild + newest segment"}
-# SURVEY 8(d) algorithmic bytes per token per layer: K+V BF16 read (12288) +
+# Algorithmic bytes per token per layer: K+V BF16 read (12288) +
 # u8 codes and f32 scales written (6336) for a commit; the reverse for a
 # gathered output token.
 BYTES_PER_TOKEN = 2 * HEADS * HEAD_DIM * 2 + 2 * (HEADS * HEAD_DIM + HEADS * 4)  # 18624
@@ -59,7 +59,7 @@ def rebuild_tokens() -> int:
     return PAST * TPF + PAST * TEXT  # 29056
 
 
-# QVG: per video token and layer 12,288 B read + 48 code
+# QVG configuration: per video token and layer 12,288 B read + 48 code
 # bytes + 12 scale bytes written = 12,348 B for an encode, the reverse for a
 # decode-gathered token (codebooks are cache-resident); text stays INT8.
 QVG_BYTES_PER_VIDEO_TOKEN = 2 * HEADS * HEAD_DIM * 2 + 2 * HEADS + 2 * HEADS * 4 * 4 // 64  # 12,348
@@ -86,7 +86,7 @@ def step_bytes(n_layers: int, workload: str = "int8", swap: bool = False) -> dic
 
 
 def qvg_codebooks(layer: int):
-    """Frozen synthetic codebooks of BASELINE configs[2]: per (layer, side,
+    """Frozen synthetic codebooks of the QVG configuration: per (layer, side,
     head, stage) 4 codewords x 128 dims ~ N(0, sigma_s), sigma = 1, .5, .25, .125."""
     import numpy as np
     rng = np.random.default_rng(1000 + layer)
@@ -502,9 +502,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--workload", default="int8", choices=["int8", "qvg"],
-                    help="int8 = BASELINE configs[1] (the headline); qvg = configs[2]")
+                    help="int8 = the headline configuration; qvg = the QVG configuration (frozen codebooks)")
     ap.add_argument("--swap", action="store_true",
-                    help="BASELINE configs[4]: phase-swapped cache, park + unpark every turn, 64-segment archive")
+                    help="box-run configuration: phase-swapped cache, park + unpark every turn, 64-segment archive")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="model layers (48 = the 8B geometry; fewer only for small profiling cases)")
     args = ap.parse_args()

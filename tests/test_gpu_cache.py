@@ -40,7 +40,7 @@ def test_inputs_bit_identical_on_both_sides(H):
 
 @pytest.mark.parametrize("model_dtype", ["f32", "bf16"])
 def test_config1_tiny_int8_uniform6(H, model_dtype):
-    """INT8, uniform history of 6 past frames."""
+    """The tiny configuration (config 1): INT8, uniform history of 6 past frames."""
     p = _pair(H, "int8", "uniform", past=6, model_dtype=model_dtype)
     for _ in range(4):
         assert p.commit() is None
@@ -50,7 +50,7 @@ def test_config1_tiny_int8_uniform6(H, model_dtype):
 
 @pytest.mark.parametrize("capacity", [192, 208])
 def test_config1_tiny_recent_swa(H, capacity):
-    """BASELINE config 1's SWA window of 3 frames as Recent capacity."""
+    """The tiny configuration's SWA window of 3 frames as Recent capacity."""
     p = _pair(H, "int8", "recent", capacity=capacity)
     for _ in range(4):
         assert p.commit() is None
@@ -137,7 +137,7 @@ def test_qvg_head_dim_128_fast_encoder_in_the_bank(H, input_dtype):
 
 
 def test_qvg_frozen_codebooks_and_partial_blocks(H):
-    """Frozen synthetic codebooks (BASELINE config 3 style), a last block of
+    """Frozen synthetic codebooks (as in the QVG benchmark), a last block of
     fewer than 64 tokens, and the sigma_s = 1, .5, .25, .125 stage scales."""
     p = _pair(H, "qvg", "uniform", past=6, model_dtype="bf16", input_dtype="bf16", tpf=50, text=7)
     rng = np.random.default_rng(7)
