@@ -175,10 +175,13 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------- CPU side
-def cpu_sample(threads: int, warmup: int = 1, steps: int = 1) -> dict:
+def cpu_sample(threads: int, warmup: int = 1, steps: int = 1, workload: str = "int8", swap: bool = False) -> dict:
     """The oracle (C++ restatement of the reference's CPU cache path, full
     segment decode before index_select) on `threads` layers in parallel, one
-    layer per host thread, 8B geometry, archive prefilled to 31 segments."""
+    layer per host thread, 8B geometry, archive prefilled like the GPU run
+    (32 segments, 64 with the phase swap); `workload` and `swap` select the
+    same turn as the GPU arm (QVG with the same frozen codebooks; park and
+    unpark every turn)."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import numpy as np
     import oracle as orc
@@ -186,14 +189,19 @@ def cpu_sample(threads: int, warmup: int = 1, steps: int = 1) -> dict:
 
     orc.build()
     n = threads
-    cfg = orc.Config(storage=orc.INT8, sampling=orc.UNIFORM, past_frames=PAST)
+    archived = ARCHIVED_SWAP if swap else ARCHIVED
+    cfg = orc.Config(storage=orc.QVG if workload == "qvg" else orc.INT8, sampling=orc.UNIFORM, past_frames=PAST,
+                     phase_swap=swap)
     bank = orc.Bank(cfg, n, 1, HEADS, HEAD_DIM, orc.BF16)
+    if workload == "qvg":
+        for l in range(n):
+            bank.set_codebooks(l, qvg_codebooks(l))
     ks = [synth.host_values(0, 1.0, 1, SEG_TOKENS, HEADS, HEAD_DIM, l, 0, 0, 1) for l in range(n)]
     vs = [synth.host_values(0, 1.0, 1, SEG_TOKENS, HEADS, HEAD_DIM, l, 0, 1, 1) for l in range(n)]
     seg = dict(segment_index=0, frame_start=0, frame_count=FRAMES, image_tokens=FRAMES * TPF, text_tokens=TEXT)
     bank.commit(seg, orc.BF16, ks, vs, nthreads=n)
-    bank.prefill_clone(ARCHIVED - 2 - warmup)
-    idx = ARCHIVED - 1 - warmup
+    bank.prefill_clone(archived - 2 - warmup)
+    idx = archived - 1 - warmup
     times = []
     for i in range(warmup + steps):
         s = dict(seg, segment_index=idx, frame_start=idx * FRAMES)
@@ -205,15 +213,19 @@ def cpu_sample(threads: int, warmup: int = 1, steps: int = 1) -> dict:
             t.start()
         for t in ths:
             t.join()
+        if swap:  # phase_swap.rs:42-92: the working set to host memory and back
+            bank.park()
+            bank.unpark()
         dt = time.perf_counter() - t0
         if i >= warmup:
             times.append(dt)
         idx += 1
     bank.close()
     sec = sum(times) / len(times)
-    return {"value": step_bytes(n)["total"] / sec / 1e9, "unit": "GB/s", "cores": n, "kind": "port",
-            "sample": f"{n} layer(s) x 1 turn (commit + uniform rebuild + newest-segment decode) at 8B geometry, "
-                      f"archive of {ARCHIVED} segments, one host thread per layer; "
+    what = "commit + uniform rebuild + newest-segment decode" + (" + park + unpark" if swap else "")
+    return {"value": step_bytes(n, workload, swap)["total"] / sec / 1e9, "unit": "GB/s", "cores": n, "kind": "port",
+            "sample": f"{n} layer(s) x {len(times)} turn(s) ({workload.upper()}: {what}) at 8B geometry, "
+                      f"archive of {archived} segments, one host thread per layer; "
                       f"{sec:.2f} s per turn"}
 
 
@@ -428,8 +440,8 @@ def run_gpu(args) -> None:
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         try:
-            cpu = cpu_sample(min(os.cpu_count() or 1, 8))
-            one = cpu_sample(1)
+            cpu = cpu_sample(min(os.cpu_count() or 1, 8), workload=wl, swap=swap)
+            one = cpu_sample(1, workload=wl, swap=swap)
             cpu["single_thread_value"] = one["value"]
             cpu["single_thread_sample"] = one["sample"]
         except Exception as e:  # noqa: BLE001
@@ -483,11 +495,14 @@ def run_reference(args) -> None:
     if rank != 0:
         return
     threads = min(os.cpu_count() or 1, LAYERS)
-    r = cpu_sample(threads, warmup=max(0, min(args.warmup, 1)), steps=max(1, min(args.steps, 2)))
-    out = {"impl": "reference", "metric": METRIC, "value": round(r["value"], 3), "unit": "GB/s", "n_gpus": args.gpus,
+    wl, swap = args.workload, args.swap
+    r = cpu_sample(threads, warmup=max(0, min(args.warmup, 1)), steps=max(1, min(args.steps, 2)), workload=wl,
+                   swap=swap)
+    metric = METRIC_SWAP.format(wl.upper()) if swap else METRIC if wl == "int8" else METRIC_QVG
+    out = {"impl": "reference", "metric": metric, "value": round(r["value"], 3), "unit": "GB/s", "n_gpus": args.gpus,
            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "strong",
            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-           "config": {"workload": "nomas-8B INT8 commit + uniform rebuild (16 past frames) + newest segment",
+           "config": {"workload": WORKLOADS[wl] + (" + park/unpark (phase swap) every turn" if swap else ""),
                       "layers_sampled": threads},
            "cpu_baseline": r, "e2e": {"value": round(r["value"], 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                                       "d2h_bytes_per_step": 0}}
