@@ -308,8 +308,11 @@ __device__ __forceinline__ void decode4(void* out, uint64_t o, const QvgTables& 
   const float4 x = *reinterpret_cast<const float4*>(&T.q01[hh][(code & 3u) * 4 + ((code >> 2) & 3u)][d]);
   const float4 y = *reinterpret_cast<const float4*>(&T.p2[hh][(code >> 4) & 3u][d]);
   const float4 z = pick4(p3, code >> 6);
-  store4<OUT_DT, FAST>(out, o, __fadd_rn(__fadd_rn(x.x, y.x), z.x), __fadd_rn(__fadd_rn(x.y, y.y), z.y),
-                       __fadd_rn(__fadd_rn(x.z, y.z), z.z), __fadd_rn(__fadd_rn(x.w, y.w), z.w));
+  // (Q01 + P2) + P3, each add rounded: packed adds of table values (no
+  // multiply anywhere in this data flow, so nothing can be contracted)
+  const float2 lo = __fadd2_rn(__fadd2_rn(make_float2(x.x, x.y), make_float2(y.x, y.y)), make_float2(z.x, z.y));
+  const float2 hi = __fadd2_rn(__fadd2_rn(make_float2(x.z, x.w), make_float2(y.z, y.w)), make_float2(z.z, z.w));
+  store4<OUT_DT, FAST>(out, o, lo.x, lo.y, hi.x, hi.y);
 }
 
 template <int OUT_DT, bool FAST>
