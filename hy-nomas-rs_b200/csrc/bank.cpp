@@ -199,6 +199,7 @@ Bank::Bank(const nkv_cache_config& cfg, int n_layers, int layer_begin, int64_t b
   // [0]: any layer saw a non-finite value (aborts the gather); [1 + i]: layer i
   NKV_CUDA(cudaMalloc(&d_flag_, sizeof(uint32_t) * (n_layers_ + 1)));
   NKV_CUDA(cudaHostAlloc(&h_flag_, sizeof(uint32_t) * (n_layers_ + 1), cudaHostAllocDefault));
+  NKV_CUDA(cudaEventCreateWithFlags(&flag_ev_, cudaEventDisableTiming));
   std::memset(h_flag_, 0, sizeof(uint32_t) * (n_layers_ + 1));
   if (cfg.storage == NKV_STORAGE_QVG) {
     cb_layer_ = size_t(2) * H_ * q_stages_ * q_E_ * D_;
@@ -227,6 +228,7 @@ Bank::~Bank() {
   if (cb_dev_) cudaFree(cb_dev_);
   if (d_flag_) cudaFree(d_flag_);
   if (h_flag_) cudaFreeHost(h_flag_);
+  if (flag_ev_) cudaEventDestroy(flag_ev_);
   for (auto p : p_host_)
     if (p) cudaFreeHost(p);
   stg_.release();
@@ -664,10 +666,15 @@ void Bank::commit(const nkv_segment_desc& s, int kv_dtype, const void* const* k,
         tend(NKV_KERNEL_QUANTIZE);
       }
     }
-    if (gt.n_tiles + gt.n_qtiles > 0) launch_gather_into(gt, outk_off, outv_off, plan.valid, gt.aligned, d_flag_);
+    // The non-finite flags are final once the archive kernels ran: read them
+    // back ahead of the rebuild gather (which aborts on them by itself), so
+    // the host waits only for the kernels that read the caller's K/V and the
+    // gather overlaps the caller's next calls (all stream-ordered).
     NKV_CUDA(cudaMemcpyAsync(h_flag_, d_flag_, sizeof(uint32_t) * (n_layers_ + 1), cudaMemcpyDeviceToHost,
                              stream_));
-    NKV_CUDA(cudaStreamSynchronize(stream_));
+    NKV_CUDA(cudaEventRecord(flag_ev_, stream_));
+    if (gt.n_tiles + gt.n_qtiles > 0) launch_gather_into(gt, outk_off, outv_off, plan.valid, gt.aligned, d_flag_);
+    NKV_CUDA(cudaEventSynchronize(flag_ev_));
     collect_timing(false);
 
     if (h_flag_[0] != 0) {

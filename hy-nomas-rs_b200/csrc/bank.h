@@ -201,6 +201,7 @@ class Bank {
 
   uint32_t* d_flag_ = nullptr;  // n_layers + 1 non-finite flags (see the constructor)
   uint32_t* h_flag_ = nullptr;
+  cudaEvent_t flag_ev_ = nullptr;  // the flags' read-back has landed
   Staging stg_;
 
   bool timing_ = false;
