@@ -200,13 +200,6 @@ Bank::Bank(const nkv_cache_config& cfg, int n_layers, int layer_begin, int64_t b
   NKV_CUDA(cudaMalloc(&d_flag_, sizeof(uint32_t) * (n_layers_ + 1)));
   NKV_CUDA(cudaHostAlloc(&h_flag_, sizeof(uint32_t) * (n_layers_ + 1), cudaHostAllocDefault));
   NKV_CUDA(cudaEventCreateWithFlags(&flag_ev_, cudaEventDisableTiming));
-  if (cfg_.storage == NKV_STORAGE_QVG) {
-    int least = 0, greatest = 0;
-    NKV_CUDA(cudaDeviceGetStreamPriorityRange(&least, &greatest));
-    NKV_CUDA(cudaStreamCreateWithPriority(&gstream_, cudaStreamNonBlocking, greatest));
-    NKV_CUDA(cudaEventCreateWithFlags(&ev_go_, cudaEventDisableTiming));
-    NKV_CUDA(cudaEventCreateWithFlags(&ev_gdone_, cudaEventDisableTiming));
-  }
   std::memset(h_flag_, 0, sizeof(uint32_t) * (n_layers_ + 1));
   if (cfg.storage == NKV_STORAGE_QVG) {
     cb_layer_ = size_t(2) * H_ * q_stages_ * q_E_ * D_;
@@ -236,12 +229,6 @@ Bank::~Bank() {
   if (d_flag_) cudaFree(d_flag_);
   if (h_flag_) cudaFreeHost(h_flag_);
   if (flag_ev_) cudaEventDestroy(flag_ev_);
-  if (gstream_) {
-    cudaStreamSynchronize(gstream_);
-    cudaStreamDestroy(gstream_);
-  }
-  if (ev_go_) cudaEventDestroy(ev_go_);
-  if (ev_gdone_) cudaEventDestroy(ev_gdone_);
   for (auto p : p_host_)
     if (p) cudaFreeHost(p);
   stg_.release();
@@ -463,8 +450,7 @@ GatherTables Bank::add_runs(const Plan& plan, bool outputs_aligned) {
 }
 
 void Bank::launch_gather_into(const GatherTables& t, size_t outk_off, size_t outv_off, uint64_t out_L,
-                              bool vector_ok, const uint32_t* abort_flag, int timing_id, cudaStream_t st) {
-  if (!st) st = stream_;
+                              bool vector_ok, const uint32_t* abort_flag, int timing_id) {
   if (t.n_tiles + t.n_qtiles == 0) return;
   GatherArgs a{};
   a.runs = static_cast<const GatherRun*>(stg_.dev(t.runs_off));
@@ -483,9 +469,9 @@ void Bank::launch_gather_into(const GatherTables& t, size_t outk_off, size_t out
   a.stages = q_stages_, a.bits = q_bits_, a.block = q_block_;
   a.abort_flag = abort_flag;
   const bool hd_ok = ((H_ * D_) % 16) == 0;
-  tbegin(timing_id, st);
-  NKV_CUDA(launch_gather(a, vector_ok && hd_ok, st));
-  tend(timing_id, st);
+  tbegin(timing_id);
+  NKV_CUDA(launch_gather(a, vector_ok && hd_ok, stream_));
+  tend(timing_id);
 }
 
 size_t Bank::ws_plane_bytes(uint64_t cap) const { return align_up(size_t(B_) * cap * H_ * D_ * dtype_size(dtype_)); }
@@ -643,20 +629,12 @@ void Bank::commit(const nkv_segment_desc& s, int kv_dtype, const void* const* k,
     }
 
     size_t outk_off = 0, outv_off = 0;
-    GatherTables gt, gt_old;  // QVG: gt = the new segment's runs, gt_old = older segments' runs
-    const bool split = cfg_.storage == NKV_STORAGE_QVG;
+    GatherTables gt;
     if (plan_ok && plan.valid > 0) {
       ensure_ws(plan.valid, &fresh, &fresh_cap);
       unsigned char* base = fresh ? fresh : ws_;
       const uint64_t cap = fresh ? fresh_cap : ws_cap_;
-      if (split) {
-        Plan p_new, p_old;
-        for (const auto& rs : plan.runs) (rs.rec + 1 == archive_.size() ? p_new : p_old).runs.push_back(rs);
-        gt = add_runs(p_new);
-        gt_old = add_runs(p_old);
-      } else {
-        gt = add_runs(plan);
-      }
+      gt = add_runs(plan);
       std::vector<void*> ok(n_layers_), ov(n_layers_);
       for (int i = 0; i < n_layers_; ++i) ok[i] = ws_plane(base, cap, i, 0), ov[i] = ws_plane(base, cap, i, 1);
       outk_off = stg_.add(ok.data(), ok.size() * sizeof(void*));
@@ -676,8 +654,10 @@ void Bank::commit(const nkv_segment_desc& s, int kv_dtype, const void* const* k,
                                     uint64_t(B_) * L * H_, 0, D_, kv_dtype, in_aligned, d_flag_, stream_));
       tend(NKV_KERNEL_QUANTIZE);
     } else {
-      // the text block first: it holds the segment's only non-finite check
-      // (history.rs:263-276), so its flags are final before the encoder runs
+      tbegin(NKV_KERNEL_QVG_ENCODE);
+      NKV_CUDA(launch_qvg_encode(static_cast<const QvgEncodeJob*>(stg_.dev(jobs_off)), 2 * n_layers_, kv_dtype, L,
+                                 int(H_), int(D_), s.image_tokens, q_stages_, q_bits_, q_block_, in_aligned, stream_));
+      tend(NKV_KERNEL_QVG_ENCODE);
       if (s.text_tokens > 0) {
         tbegin(NKV_KERNEL_QUANTIZE);
         NKV_CUDA(launch_int8_quantize(static_cast<const QuantJob*>(stg_.dev(text_jobs_off)), n_layers_,
@@ -685,20 +665,6 @@ void Bank::commit(const nkv_segment_desc& s, int kv_dtype, const void* const* k,
                                       stream_));
         tend(NKV_KERNEL_QUANTIZE);
       }
-      // the older segments' part of the rebuild does not depend on this
-      // segment's codes: it runs on the high-priority gather stream beside the
-      // (compute-bound) encoder and still aborts on the final flags
-      if (gt_old.n_tiles + gt_old.n_qtiles > 0) {
-        NKV_CUDA(cudaEventRecord(ev_go_, stream_));
-        NKV_CUDA(cudaStreamWaitEvent(gstream_, ev_go_, 0));
-        launch_gather_into(gt_old, outk_off, outv_off, plan.valid, gt_old.aligned, d_flag_, NKV_KERNEL_GATHER,
-                           gstream_);
-        NKV_CUDA(cudaEventRecord(ev_gdone_, gstream_));
-      }
-      tbegin(NKV_KERNEL_QVG_ENCODE);
-      NKV_CUDA(launch_qvg_encode(static_cast<const QvgEncodeJob*>(stg_.dev(jobs_off)), 2 * n_layers_, kv_dtype, L,
-                                 int(H_), int(D_), s.image_tokens, q_stages_, q_bits_, q_block_, in_aligned, stream_));
-      tend(NKV_KERNEL_QVG_ENCODE);
     }
     // The non-finite flags are final once the archive kernels ran: read them
     // back ahead of the rebuild gather (which aborts on them by itself), so
@@ -708,7 +674,6 @@ void Bank::commit(const nkv_segment_desc& s, int kv_dtype, const void* const* k,
                              stream_));
     NKV_CUDA(cudaEventRecord(flag_ev_, stream_));
     if (gt.n_tiles + gt.n_qtiles > 0) launch_gather_into(gt, outk_off, outv_off, plan.valid, gt.aligned, d_flag_);
-    if (gt_old.n_tiles + gt_old.n_qtiles > 0) NKV_CUDA(cudaStreamWaitEvent(stream_, ev_gdone_, 0));  // join
     NKV_CUDA(cudaEventSynchronize(flag_ev_));
     collect_timing(false);
 
@@ -1052,7 +1017,7 @@ uint64_t Bank::export_segment(int layer, uint64_t pos, void* host, uint64_t cap)
 // ------------------------------------------------------------------ timing --
 void Bank::set_timing(bool on) { timing_ = on; }
 
-void Bank::tbegin(int, cudaStream_t st) {
+void Bank::tbegin(int) {
   if (!timing_) return;
   if (ev_pool_.empty()) {
     cudaEvent_t e;
@@ -1061,10 +1026,10 @@ void Bank::tbegin(int, cudaStream_t st) {
   }
   cur_a_ = ev_pool_.back();
   ev_pool_.pop_back();
-  NKV_CUDA(cudaEventRecord(cur_a_, st ? st : stream_));
+  NKV_CUDA(cudaEventRecord(cur_a_, stream_));
 }
 
-void Bank::tend(int kind, cudaStream_t st) {
+void Bank::tend(int kind) {
   if (!timing_ || !cur_a_) return;
   cudaEvent_t b;
   if (ev_pool_.empty()) {
@@ -1073,7 +1038,7 @@ void Bank::tend(int kind, cudaStream_t st) {
     b = ev_pool_.back();
     ev_pool_.pop_back();
   }
-  NKV_CUDA(cudaEventRecord(b, st ? st : stream_));
+  NKV_CUDA(cudaEventRecord(b, stream_));
   pending_.push_back({kind, cur_a_, b});
   cur_a_ = nullptr;
 }

@@ -156,15 +156,15 @@ class Bank {
   GatherTables add_runs(const Plan& plan, bool outputs_aligned = true);
   std::vector<int> fit_qvg(const nkv_segment_desc& s, int kv_dtype, const void* const* k, const void* const* v);
   void launch_gather_into(const GatherTables& t, size_t outk_off, size_t outv_off, uint64_t out_L, bool vector_ok,
-                          const uint32_t* abort_flag, int timing_id = NKV_KERNEL_GATHER, cudaStream_t st = nullptr);
+                          const uint32_t* abort_flag, int timing_id = NKV_KERNEL_GATHER);
   void ensure_ws(uint64_t tokens, unsigned char** fresh, uint64_t* fresh_cap);
   unsigned char* ws_plane(unsigned char* base, uint64_t cap, int layer, int side) const;
   size_t ws_plane_bytes(uint64_t cap) const;
   void rebuild_now();  // plan + gather + install (rollback path)
   uint64_t capacity_or_max() const { return cfg_.has_capacity ? cfg_.capacity : UINT64_MAX; }
 
-  void tbegin(int kind, cudaStream_t st = nullptr);  // events on st (default: the bank's stream)
-  void tend(int kind, cudaStream_t st = nullptr);
+  void tbegin(int kind);
+  void tend(int kind);
   void collect_timing(bool wait);
 
   nkv_cache_config cfg_;
@@ -202,10 +202,6 @@ class Bank {
   uint32_t* d_flag_ = nullptr;  // n_layers + 1 non-finite flags (see the constructor)
   uint32_t* h_flag_ = nullptr;
   cudaEvent_t flag_ev_ = nullptr;  // the flags' read-back has landed
-  // QVG commit: the gather of older segments runs on gstream_ (high
-  // priority) beside the encoder; ev_go_ releases it, ev_gdone_ joins it
-  cudaStream_t gstream_ = nullptr;
-  cudaEvent_t ev_go_ = nullptr, ev_gdone_ = nullptr;
   Staging stg_;
 
   bool timing_ = false;
