@@ -24,9 +24,10 @@ BUILD = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "nomas_kv", "libnomas_kv.so")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
-SOURCES = ["kernels_commit.cu", "kernels_gather.cu", "kernels_qvg.cu", "kernels_qvg_fit.cu", "bank.cpp", "abi.cpp",
+SOURCES = ["kernels_commit.cu", "kernels_gather.cu", "kernels_qvg.cu", "kernels_qvg_fit.cu", "kernels_project.cu",
+           "bank.cpp", "abi.cpp",
            "noalloc.cu"]
-HEADERS = ["nkv_kernels.h", "nkv_device.cuh", "nkv_policy.h", "bank.h"]
+HEADERS = ["nkv_kernels.h", "nkv_device.cuh", "nkv_quant.cuh", "nkv_policy.h", "bank.h"]
 
 # -fmad=false / -ffp-contract=off: the reference rounds every multiply and
 # add separately; the kernels ask for fused operations explicitly where the

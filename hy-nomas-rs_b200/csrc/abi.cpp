@@ -153,6 +153,21 @@ int nkv_bank_load(nkv_bank* bank, const char* path) {
   return guarded([&] { bank_of(bank).load(path); });
 }
 
+int nkv_bank_stage_segment(nkv_bank* bank, const nkv_segment_desc* seg, nkv_staged_layer* out) {
+  return guarded([&] {
+    need(seg, "seg");
+    bank_of(bank).stage(*seg, out);
+  });
+}
+
+int nkv_bank_commit_staged(nkv_bank* bank) {
+  return guarded([&] { bank_of(bank).commit_staged(); });
+}
+
+int nkv_bank_discard_staged(nkv_bank* bank) {
+  return guarded([&] { bank_of(bank).discard_staged(); });
+}
+
 int nkv_cache_working_set(const nkv_bank* bank, int32_t layer, const void** k_dev, const void** v_dev,
                           uint64_t* valid_len) {
   return guarded([&] {
@@ -257,6 +272,50 @@ int nkv_plan_recent_trim(const uint64_t* records, uint64_t n, uint64_t capacity,
         kept[5 * i] = k[i].segment_index, kept[5 * i + 1] = k[i].frame_start, kept[5 * i + 2] = k[i].frame_count;
         kept[5 * i + 3] = k[i].image_tokens, kept[5 * i + 4] = k[i].text_tokens;
       }
+  });
+}
+
+int nkv_kv_project(const nkv_kv_project_args* a, void* stream) {
+  return guarded([&] {
+    need(a, "args");
+    if (a->head_dim != 128 || !nkv::kv_project_shape_ok(a->tokens, a->heads, a->head_dim))
+      nkv::fail(NKV_ERR_ARGUMENT, "nkv_kv_project needs head_dim 128, heads * 128 a multiple of 256 and tokens > 0");
+    need(a->x, "x"), need(a->wk, "wk"), need(a->wv, "wv"), need(a->status, "status");
+    const bool codes = a->k_codes || a->v_codes || a->k_scales || a->v_scales;
+    if (codes && !(a->k_codes && a->v_codes && a->k_scales && a->v_scales))
+      nkv::fail(NKV_ERR_ARGUMENT, "k_codes, v_codes, k_scales and v_scales go together");
+    if (a->rope_cos ? !a->rope_sin : a->rope_sin != nullptr)
+      nkv::fail(NKV_ERR_ARGUMENT, "rope_cos and rope_sin go together");
+    if (a->n_ranges < 0 || a->n_ranges > 2) nkv::fail(NKV_ERR_ARGUMENT, "n_ranges must be 0, 1 or 2");
+    for (int i = 0; i < a->n_ranges; ++i) {
+      const nkv_row_range& r = a->ranges[i];
+      if (r.lo < 0 || r.hi < r.lo || r.hi > a->tokens || r.dst < 0)
+        nkv::fail(NKV_ERR_ARGUMENT, "row range " + std::to_string(i) + " outside [0, tokens)");
+    }
+    const void* ptrs[] = {a->x, a->wk, a->wv, a->bk, a->bv, a->k_norm_gain, a->rope_cos, a->rope_sin, a->k_out,
+                          a->v_out, a->k_codes, a->k_scales, a->v_codes, a->v_scales, a->status};
+    for (const void* p : ptrs)
+      if (reinterpret_cast<uintptr_t>(p) & 15u) nkv::fail(NKV_ERR_ARGUMENT, "nkv_kv_project pointers must be 16-byte aligned");
+    nkv::KvProjectParams p{};
+    p.M = a->tokens;
+    p.H = a->heads;
+    p.qk_norm = a->qk_norm;
+    p.eps = a->eps;
+    p.bias_k = static_cast<const uint16_t*>(a->bk);
+    p.bias_v = static_cast<const uint16_t*>(a->bv);
+    p.k_gain = static_cast<const uint16_t*>(a->k_norm_gain);
+    p.rope_cos = a->rope_cos;
+    p.rope_sin = a->rope_sin;
+    p.k_out = static_cast<uint16_t*>(a->k_out);
+    p.v_out = static_cast<uint16_t*>(a->v_out);
+    p.k_codes = a->k_codes, p.k_scales = a->k_scales, p.v_codes = a->v_codes, p.v_scales = a->v_scales;
+    p.n_ranges = codes ? a->n_ranges : 0;
+    for (int i = 0; i < p.n_ranges; ++i)
+      p.range_lo[i] = a->ranges[i].lo, p.range_hi[i] = a->ranges[i].hi, p.range_dst[i] = a->ranges[i].dst;
+    p.flag = a->status;
+    p.err = a->status;
+    nkv::check_cuda(nkv::launch_kv_project(a->x, a->wk, a->wv, p, static_cast<cudaStream_t>(stream)),
+                    "kv projection launch");
   });
 }
 

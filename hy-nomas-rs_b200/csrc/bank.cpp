@@ -299,7 +299,9 @@ void Bank::validate(const nkv_segment_desc& s, int kv_dtype, const void* const* 
     fail(NKV_ERR_GEOMETRY, "action_start " + std::to_string(s.action_start) + " outside text block of " +
                                std::to_string(s.text_tokens));
   if (kv_dtype < NKV_F32 || kv_dtype > NKV_F16) fail(NKV_ERR_GEOMETRY, "segment k must be float");
-  // "segment KV must live on the cache device" (history.rs:232-236)
+  // "segment KV must live on the cache device" (history.rs:232-236); a
+  // staged segment has no input tensors
+  if (k && v)
   for (int i = 0; i < n_layers_; ++i)
     for (int side = 0; side < 2; ++side) {
       const void* p = side ? v[i] : k[i];
@@ -555,19 +557,76 @@ std::vector<int> Bank::fit_qvg(const nkv_segment_desc& s, int kv_dtype, const vo
 }
 
 // commit_segment (history.rs:458-463).
+void Bank::no_staged(const char* what) const {
+  if (staged_)
+    fail(NKV_ERR_CACHE_STATE, std::string(what) + " with a staged segment pending: commit or discard it first");
+}
+
 void Bank::commit(const nkv_segment_desc& s, int kv_dtype, const void* const* k, const void* const* v) {
   if (!k || !v) fail(NKV_ERR_ARGUMENT, "null K/V pointer array");
   for (int i = 0; i < n_layers_; ++i)
     if (!k[i] || !v[i]) fail(NKV_ERR_ARGUMENT, "null K/V pointer for layer " + std::to_string(i));
+  no_staged("commit");
   DeviceScope ds(device_);
   validate(s, kv_dtype, k, v);
 
   // ---- archive_segment: slab + device encode into it
   Rec r = make_rec(s);
   r.slab = arena_.push(r.layer_stride * n_layers_);
+  finish_commit(s, r, kv_dtype, k, v, false);
+}
+
+// validate_segment (history.rs:168-238) and the record's slab; the
+// producer then writes the INT8 rows (int8.rs:65-81 layout: codes (B, L, H, D)
+// u8, scales (B, L, H) f32) and ORs its non-finite bits into the layer's
+// status word, in work ordered before the bank's stream reaches commit_staged.
+void Bank::stage(const nkv_segment_desc& s, nkv_staged_layer* out) {
+  if (!out) fail(NKV_ERR_ARGUMENT, "null staged-layer array");
+  if (cfg_.storage != NKV_STORAGE_INT8) fail(NKV_ERR_INVALID_CONFIG, "staged commits need INT8 storage");
+  if (staged_) fail(NKV_ERR_CACHE_STATE, "a staged segment is already pending");
+  DeviceScope ds(device_);
+  validate(s, NKV_BF16, nullptr, nullptr);
+  Rec r = make_rec(s);
+  r.slab = arena_.push(r.layer_stride * n_layers_);
+  try {
+    NKV_CUDA(cudaMemsetAsync(d_flag_, 0, sizeof(uint32_t) * (n_layers_ + 1), stream_));
+  } catch (...) {
+    arena_.pop();
+    throw;
+  }
+  for (int i = 0; i < n_layers_; ++i) {
+    unsigned char* lb = r.slab + size_t(i) * r.layer_stride;
+    out[i].k_codes = lb + r.off[0];
+    out[i].v_codes = lb + r.off[1];
+    out[i].k_scales = reinterpret_cast<float*>(lb + r.off[2]);
+    out[i].v_scales = reinterpret_cast<float*>(lb + r.off[3]);
+    out[i].status = d_flag_ + 1 + i;
+  }
+  staged_rec_ = r;
+  staged_ = true;
+}
+
+void Bank::commit_staged() {
+  if (!staged_) fail(NKV_ERR_CACHE_STATE, "no staged segment");
+  DeviceScope ds(device_);
+  Rec r = staged_rec_;
+  staged_ = false;
+  finish_commit(r.desc, r, NKV_BF16, nullptr, nullptr, true);
+}
+
+void Bank::discard_staged() {
+  if (!staged_) fail(NKV_ERR_CACHE_STATE, "no staged segment");
+  DeviceScope ds(device_);
+  NKV_CUDA(cudaStreamSynchronize(stream_));  // a producer may still write into the slab
+  arena_.pop();
+  staged_ = false;
+}
+
+void Bank::finish_commit(const nkv_segment_desc& s, Rec r, int kv_dtype, const void* const* k, const void* const* v,
+                         bool staged) {
   const nkv_metrics saved = m_;
   const uint64_t L = s.image_tokens + s.text_tokens;
-  bool pushed = false;
+  bool pushed = false, popped = false;
   unsigned char* fresh = nullptr;
   uint64_t fresh_cap = 0;
   try {
@@ -595,9 +654,12 @@ void Bank::commit(const nkv_segment_desc& s, int kv_dtype, const void* const* k,
 
     stg_.begin();
     bool in_aligned = true;
-    for (int i = 0; i < n_layers_; ++i) in_aligned &= aligned16(k[i]) && aligned16(v[i]);
+    if (!staged)
+      for (int i = 0; i < n_layers_; ++i) in_aligned &= aligned16(k[i]) && aligned16(v[i]);
     size_t jobs_off = 0, text_jobs_off = 0;
-    if (cfg_.storage == NKV_STORAGE_FLOAT) {
+    if (staged) {
+      // the producer wrote the codes and the per-layer flags
+    } else if (cfg_.storage == NKV_STORAGE_FLOAT) {
       std::vector<ConvertJob> jobs;
       for (int i = 0; i < n_layers_; ++i) {
         unsigned char* lb = r.slab + size_t(i) * r.layer_stride;
@@ -642,8 +704,13 @@ void Bank::commit(const nkv_segment_desc& s, int kv_dtype, const void* const* k,
     }
     stg_.upload(stream_);
 
-    NKV_CUDA(cudaMemsetAsync(d_flag_, 0, sizeof(uint32_t) * (n_layers_ + 1), stream_));
-    if (cfg_.storage == NKV_STORAGE_FLOAT) {
+    if (staged) {
+      NKV_CUDA(launch_flag_reduce(d_flag_, n_layers_, stream_));  // the gather aborts on word 0
+    } else {
+      NKV_CUDA(cudaMemsetAsync(d_flag_, 0, sizeof(uint32_t) * (n_layers_ + 1), stream_));
+    }
+    if (staged) {
+    } else if (cfg_.storage == NKV_STORAGE_FLOAT) {
       tbegin(NKV_KERNEL_FLOAT_ARCHIVE);
       NKV_CUDA(launch_convert(static_cast<const ConvertJob*>(stg_.dev(jobs_off)), 2 * n_layers_,
                               uint64_t(B_) * L * H_ * D_, kv_dtype, dtype_, stream_));
@@ -693,8 +760,10 @@ void Bank::commit(const nkv_segment_desc& s, int kv_dtype, const void* const* k,
       total_frames_ -= s.frame_count;
       m_ = saved;
       arena_.pop();
+      popped = true;
       if (fresh) cudaFree(fresh);
       fresh = nullptr;
+      if (h_flag_[0] & kProjectTimeoutBit) fail(NKV_ERR_CUDA, "the K/V producer kernel timed out");
       fail(NKV_ERR_MSG, std::string("cannot quantize non-finite ") + (k_bad ? "k" : "v") + " values");
     }
     if (parked_) changed_while_parked_ = true;
@@ -722,7 +791,7 @@ void Bank::commit(const nkv_segment_desc& s, int kv_dtype, const void* const* k,
       total_frames_ -= s.frame_count;
       m_ = saved;
       arena_.pop();
-    } else if (!pushed && e.code != NKV_ERR_MSG) {
+    } else if (!pushed && !popped) {
       arena_.pop();
     }
     throw;
@@ -768,6 +837,7 @@ void Bank::rebuild_now() {
 
 // rollback_last_segment (history.rs:507-528).
 void Bank::rollback() {
+  no_staged("rollback");  // the staged slab sits above the archive's
   if (cfg_.sampling == NKV_SAMPLING_RECENT)
     fail(NKV_ERR_CACHE_STATE, "recent-mode SWA does not support streaming rollback (use an archived sampling)");
   if (archive_.empty()) fail(NKV_ERR_CACHE_STATE, "nothing to roll back");
@@ -1140,6 +1210,7 @@ bool same_config(File& f, const nkv_cache_config& c) {
 
 void Bank::save(const char* path) {
   if (!path) fail(NKV_ERR_ARGUMENT, "null path");
+  no_staged("save");
   if (parked_) fail(NKV_ERR_CACHE_STATE, "cannot save a parked cache; unpark it first");
   if (!ws_current_)
     fail(NKV_ERR_CACHE_STATE,
@@ -1181,6 +1252,7 @@ void Bank::save(const char* path) {
 
 void Bank::load(const char* path) {
   if (!path) fail(NKV_ERR_ARGUMENT, "null path");
+  no_staged("load");
   if (!archive_.empty() || total_frames_ != 0 || parked_)
     fail(NKV_ERR_CACHE_STATE, "load needs a fresh cache (nothing committed yet)");
   DeviceScope ds(device_);

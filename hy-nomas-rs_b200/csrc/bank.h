@@ -121,6 +121,13 @@ class Bank {
   ~Bank();
 
   void commit(const nkv_segment_desc& s, int kv_dtype, const void* const* k, const void* const* v);
+  // Two-phase INT8 commit for a producer that writes the archive rows itself
+  // (the fused K/V projection): stage validates the segment and reserves its
+  // record, commit_staged archives it and rebuilds, discard_staged drops it.
+  void stage(const nkv_segment_desc& s, nkv_staged_layer* out);
+  void commit_staged();
+  void discard_staged();
+  bool staged() const { return staged_; }
   void rollback();
   void park();
   void unpark();
@@ -152,6 +159,11 @@ class Bank {
  private:
   Rec make_rec(const nkv_segment_desc& s) const;
   void validate(const nkv_segment_desc& s, int kv_dtype, const void* const* k, const void* const* v);
+  // archive_segment + rebuild of a validated segment whose slab is pushed;
+  // `staged`: the codes are already in the slab and the per-layer flags set
+  void finish_commit(const nkv_segment_desc& s, Rec r, int kv_dtype, const void* const* k, const void* const* v,
+                     bool staged);
+  void no_staged(const char* what) const;
   Plan plan_rebuild();
   GatherTables add_runs(const Plan& plan, bool outputs_aligned = true);
   std::vector<int> fit_qvg(const nkv_segment_desc& s, int kv_dtype, const void* const* k, const void* const* v);
@@ -181,6 +193,8 @@ class Bank {
   uint64_t valid_ = 0;
 
   bool parked_ = false;
+  bool staged_ = false;  // a staged segment's slab is the arena's top
+  Rec staged_rec_;
   // the working set is the rebuild of the current archive (false after a
   // failed rebuild, or after unpark restored a set older than the archive)
   bool ws_current_ = true;

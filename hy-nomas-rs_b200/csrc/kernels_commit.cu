@@ -13,6 +13,7 @@
 
 #include "nkv_device.cuh"
 #include "nkv_kernels.h"
+#include "nkv_quant.cuh"
 
 namespace nkv {
 
@@ -32,14 +33,6 @@ namespace nkv {
 // the 1.5 * 2^23 magic constant, corrected on exact .5 ties by a select.
 // Rows whose scale is subnormal (or above 1e37) take the IEEE division.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ uint32_t quant_exact(float x, float s) {
-  float t = roundf(__fdiv_rn(x, s));
-  t = dev::cmin(dev::cmax(t, -127.0f), 127.0f);
-  t = __fadd_rn(__fmul_rn(t, 1.0f), 128.0f);
-  t = dev::cmin(dev::cmax(t, 0.0f), 255.0f);
-  return dev::as_u8(t);
-}
-
 // The exact per-value path kept out of line: inlined, the compiler turns the
 // rarely taken branch into predicated code that every thread issues.
 __device__ __noinline__ uint2 quant8_exact(float4 lo, float4 hi, float s) {
@@ -62,24 +55,6 @@ __device__ __noinline__ uint4 quant16_bf16_exact(uint4 w0, uint4 w1, float s) {
     out[k] = b[0] | (b[1] << 8) | (b[2] << 16) | (b[3] << 24);
   }
   return make_uint4(out[0], out[1], out[2], out[3]);
-}
-
-// Code of one value: (round_half_away(RN(x / s)) + 128) in the low byte of
-// the returned f32 bit pattern's 8 LSBs XOR 0x80 (see kernel notes); valid
-// for s in [FLT_MIN, 1e37] with r = RN(1/s).
-__device__ __forceinline__ uint32_t code_bits(float x, float s, float r) {
-  const float M = 12582912.0f;  // 1.5 * 2^23
-  const float q0 = __fmul_rn(x, r);
-  const float e = __fmaf_rn(-q0, s, x);
-  const float q1 = __fmaf_rn(e, r, q0);                  // RN(x / s)
-  const float t = __fadd_rn(__fadd_rn(q1, M), -M);       // round to nearest even
-  const float hv = __fadd_rn(q1, copysignf(0.5f, q1));   // exact on a .5 tie
-  const float f = fabsf(__fadd_rn(q1, -t)) == 0.5f ? hv : t;
-  return __float_as_uint(__fadd_rn(f, M));               // low byte: f mod 256
-}
-
-__device__ __forceinline__ uint32_t pack4(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
-  return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410) ^ 0x80808080u;
 }
 
 // 8 values of one row with scale s -> 8 packed code bytes.
@@ -361,6 +336,18 @@ static cudaError_t convert_out(const ConvertJob* jobs, int n_jobs, uint64_t n, i
     case BF16: k_convert<IN_DT, BF16><<<grid, 256, 0, s>>>(jobs, n); break;
     default: k_convert<IN_DT, F16><<<grid, 256, 0, s>>>(jobs, n); break;
   }
+  return cudaGetLastError();
+}
+
+__global__ void k_flag_reduce(uint32_t* flags, int n) {
+  uint32_t any = 0;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) any |= flags[1 + i];
+  for (int o = 16; o > 0; o >>= 1) any |= __shfl_xor_sync(0xFFFFFFFFu, any, o);
+  if (threadIdx.x == 0 && any) atomicOr(flags, any);
+}
+
+cudaError_t launch_flag_reduce(uint32_t* flags, int n, cudaStream_t s) {
+  k_flag_reduce<<<1, 32, 0, s>>>(flags, n);
   return cudaGetLastError();
 }
 

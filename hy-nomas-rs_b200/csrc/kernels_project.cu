@@ -1,0 +1,531 @@
+// kernels_project.cu — the commit producer fused into the K/V projection on
+// sm_100a: tcgen05 tensor cores fed by TMA, with the reference's whole
+// per-(token, head) chain from the projection to the INT8 archive codes in
+// the epilogue.
+//
+// Reference chain for one layer's captured K / V (batch 1):
+//   k = Lin_k(x)             modules/mod.rs:122-142 (bf16 GEMM, then + bias in bf16)
+//   k = RmsNorm_k(k)         modules/attention.rs:117-122, modules/norm.rs:55-65
+//   k = apply_rotary(k)      modules/attention.rs:144, rope.rs:257-306
+//   v = Lin_v(x)             modules/attention.rs:116
+//   quantize_kv_pair(k, v)   cache/int8.rs:85-134 (the commit's archive step)
+// The bf16 K / V are still written (the attention of the capturing pass
+// reads them, attention.rs:145-147), but the commit no longer reads them
+// back: the codes and scales come out of the same epilogue.
+//
+// Kernel shape (one persistent CTA per SM, 192 threads):
+//  * warp 0, one thread: TMA producer.  A 128-token x 64 slice of x and a
+//    256-row x 64 slice of W_k or W_v per stage, 128-byte swizzled, into a
+//    4-stage shared-memory ring (48 KB per stage);
+//  * warp 1: allocates 512 TMEM columns (two 128 x 256 f32 accumulators);
+//    one thread issues tcgen05.mma kind::f16 (bf16 x bf16 -> f32,
+//    M=128 N=256 K=16), frees each stage with tcgen05.commit and hands a
+//    finished accumulator to the epilogue with a second commit;
+//  * warps 2-5: the epilogue.  Warp w reads TMEM lanes 32*(w%4)..+31, so
+//    thread l owns token row 32*(w%4)+l of the tile, and each of the tile's
+//    two heads is 128 values in that thread's registers: bias, RMS norm,
+//    rotary pairs, |x| max and codes need no cross-thread exchange.  While
+//    it runs, the MMA warp fills the other accumulator with the next tile.
+//
+// Every wait is bounded (kWaitNs on %globaltimer); a wait that runs out sets
+// kProjectTimeoutBit in the status word and the CTA's abort flag, every role
+// leaves its loop, and the CTA frees its TMEM after a bounded drain.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <cfloat>
+#include <cstdint>
+
+#include "nkv_device.cuh"
+#include "nkv_kernels.h"
+#include "nkv_quant.cuh"
+
+namespace nkv {
+namespace {
+
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int A_BYTES = BM * BK * 2;  // 16 KB
+constexpr int B_BYTES = BN * BK * 2;  // 32 KB
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int TMEM_COLS = 2 * BN;
+constexpr int kThreads = 192;
+constexpr int kSmemBytes = STAGES * STAGE_BYTES + 1024 /* barriers */ + 1024 /* alignment */;
+constexpr uint64_t kWaitNs = 1000000000ull;  // 1 s per wait
+
+// tcgen05 instruction descriptor: f32 accumulate (bits 4-5 = 1), A and B
+// bf16 (bits 7-9, 10-12 = 1), both K-major (bits 15, 16 = 0), N >> 3 at
+// bit 17, M >> 4 at bit 24.
+constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(BN >> 3) << 17) | (uint32_t(BM >> 4) << 24);
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Wait for the phase of parity `parity` to complete; false when the CTA was
+// aborted or the wait ran out (which aborts the CTA and sets *err).
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile uint32_t* abort_flag,
+                                          uint32_t* err) {
+  if (mbar_try(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  for (;;) {
+    for (int i = 0; i < 32; ++i)
+      if (mbar_try(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer() - t0 > kWaitNs) {
+      *abort_flag = 1u;
+      atomicOr(err, kProjectTimeoutBit);
+      return false;
+    }
+  }
+}
+
+// 2-D tiled TMA load (no multicast) completing on `bar`.
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int32_t x, int32_t y,
+                                            uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+          "r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+// Shared-memory matrix descriptor of a K-major, 128-byte-swizzled tile whose
+// rows are 128 bytes (64 bf16): start address >> 4 in bits 0-13, leading
+// byte offset 1 (unused for swizzled K-major), stride byte offset 1024 >> 4
+// (eight rows) in bits 32-45, descriptor version 1 (bit 46), layout
+// SWIZZLE_128B = 2 in bits 61-63.  Tiles start on 1024-byte boundaries, so
+// the base offset field stays 0; stepping K by 16 elements adds 32 bytes to
+// the start address.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
+  return uint64_t((addr & 0x3FFFFu) >> 4) | (uint64_t(1) << 16) | (uint64_t(1024 >> 4) << 32) |
+         (uint64_t(1) << 46) | (uint64_t(2) << 61);
+}
+
+__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(kIdesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+
+// 32 consecutive f32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
+  uint32_t* r = reinterpret_cast<uint32_t*>(v);
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
+// tcgen05.wait::ld, with the 32 registers of one load threaded through it
+// so no use of them is scheduled ahead of the wait.
+__device__ __forceinline__ void tmem_wait32(float* v) {
+  uint32_t* r = reinterpret_cast<uint32_t*>(v);
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
+                 "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]),
+                 "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+               :
+               : "memory");
+}
+
+// f32 -> bf16 (round to nearest even) -> f32, two values at a time.  The
+// hardware conversion is the integer RNE for every non-NaN input; a NaN
+// stays a NaN (its payload is not the reference's, which only matters for
+// rows the non-finite check rejects).
+__device__ __forceinline__ void bf16_round2(float& a, float& b) {
+  const uint32_t w = dev::bf16x2_bits_nonnan(a, b);
+  a = __uint_as_float(w << 16);
+  b = __uint_as_float(w & 0xFFFF0000u);
+}
+
+__device__ __forceinline__ void load_bf16x8(const uint16_t* p, float* out) {
+  const uint4 w = __ldg(reinterpret_cast<const uint4*>(p));
+  const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    out[2 * i] = __uint_as_float(ws[i] << 16);
+    out[2 * i + 1] = __uint_as_float(ws[i] & 0xFFFF0000u);
+  }
+}
+
+// The epilogue of one (token row, head): y holds the 128 f32 accumulator
+// values of this row and head.
+__device__ __forceinline__ void epilogue_head(float (&y)[128], const KvProjectParams& p, int side, int64_t row,
+                                              int head, bool& bad) {
+  const int dim = p.H * 128;
+  const uint16_t* bias = side ? p.bias_v : p.bias_k;
+  // Lin::fwd (modules/mod.rs:135-138): the GEMM's bf16 result, then the
+  // bias added in bf16
+#pragma unroll
+  for (int d = 0; d < 128; d += 2) bf16_round2(y[d], y[d + 1]);
+  if (bias) {
+#pragma unroll
+    for (int d0 = 0; d0 < 128; d0 += 8) {
+      float b[8];
+      load_bf16x8(bias + head * 128 + d0, b);
+#pragma unroll
+      for (int j = 0; j < 8; j += 2) {
+        y[d0 + j] = __fadd_rn(y[d0 + j], b[j]);
+        y[d0 + j + 1] = __fadd_rn(y[d0 + j + 1], b[j + 1]);
+        bf16_round2(y[d0 + j], y[d0 + j + 1]);
+      }
+    }
+  }
+  if (side == 0 && p.qk_norm) {
+    // RmsNorm (norm.rs:55-65): f32 mean of squares over the head dim, four
+    // interleaved partial sums (d mod 4) added as (s0 + s1) + (s2 + s3);
+    // 1/sqrt(var + eps) as an IEEE square root and division
+    float s[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+    for (int d = 0; d < 128; ++d) s[d & 3] = __fadd_rn(s[d & 3], __fmul_rn(y[d], y[d]));
+    const float ss = __fadd_rn(__fadd_rn(s[0], s[1]), __fadd_rn(s[2], s[3]));
+    const float var = __fmul_rn(ss, 0.0078125f);  // / 128, exact
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, p.eps)));
+    if (p.k_gain) {
+#pragma unroll
+      for (int d0 = 0; d0 < 128; d0 += 8) {
+        float g[8];
+        load_bf16x8(p.k_gain + d0, g);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) y[d0 + j] = __fmul_rn(__fmul_rn(y[d0 + j], inv), g[j]);
+      }
+    } else {
+#pragma unroll
+      for (int d = 0; d < 128; ++d) y[d] = __fmul_rn(y[d], inv);
+    }
+#pragma unroll
+    for (int d = 0; d < 128; d += 2) bf16_round2(y[d], y[d + 1]);
+  }
+  if (side == 0 && p.rope_cos) {
+    // apply_rotary (rope.rs:269-305): interleaved (re, im) pairs, products
+    // and sums rounded separately in f32, then bf16
+    const float4* c4 = reinterpret_cast<const float4*>(p.rope_cos + row * 64);
+    const float4* s4 = reinterpret_cast<const float4*>(p.rope_sin + row * 64);
+#pragma unroll
+    for (int q = 0; q < 16; ++q) {
+      const float4 c = __ldg(c4 + q), sn = __ldg(s4 + q);
+      const float cs[4] = {c.x, c.y, c.z, c.w}, ss[4] = {sn.x, sn.y, sn.z, sn.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int d = 8 * q + 2 * j;
+        const float xr = y[d], xi = y[d + 1];
+        float o_r = __fsub_rn(__fmul_rn(xr, cs[j]), __fmul_rn(xi, ss[j]));
+        float o_i = __fadd_rn(__fmul_rn(xi, cs[j]), __fmul_rn(xr, ss[j]));
+        bf16_round2(o_r, o_i);
+        y[d] = o_r;
+        y[d + 1] = o_i;
+      }
+    }
+  }
+  // the bf16 K / V the attention reads
+  uint16_t* out = side ? p.v_out : p.k_out;
+  if (out) {
+    uint4* o = reinterpret_cast<uint4*>(out + row * dim + head * 128);
+#pragma unroll
+    for (int q = 0; q < 16; ++q) {
+      uint32_t w[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        w[j] = (__float_as_uint(y[8 * q + 2 * j]) >> 16) | (__float_as_uint(y[8 * q + 2 * j + 1]) & 0xFFFF0000u);
+      o[q] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  }
+  // the archive rows: quantize_one (int8.rs:65-81) of committed rows only
+  uint8_t* codes = side ? p.v_codes : p.k_codes;
+  if (!codes) return;
+  int64_t dst = -1;
+#pragma unroll
+  for (int i = 0; i < 2; ++i)
+    if (i < p.n_ranges && row >= p.range_lo[i] && row < p.range_hi[i]) dst = row - p.range_lo[i] + p.range_dst[i];
+  if (dst < 0) return;
+  float peak = 0.0f;
+#pragma unroll
+  for (int d = 0; d < 128; ++d) {
+    const float a = fabsf(y[d]);
+    bad |= !(a < FLT_MAX);  // x != x || |x| >= f32::MAX (int8.rs:99-117)
+    peak = fmaxf(peak, a);
+  }
+  const float inv127 = (float)(1.0 / 127.0);
+  const float s = peak > 0.0f ? __fadd_rn(__fmul_rn(peak, inv127), 0.0f) : 1.0f;
+  uint4* q = reinterpret_cast<uint4*>(codes + dst * dim + head * 128);
+  if (s >= FLT_MIN && s <= 1e37f) {
+    const float r = __frcp_rn(s);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      uint32_t w[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int d = 16 * k + 4 * j;
+        w[j] = pack4(code_bits(y[d], s, r), code_bits(y[d + 1], s, r), code_bits(y[d + 2], s, r),
+                     code_bits(y[d + 3], s, r));
+      }
+      q[k] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      uint32_t w[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int d = 16 * k + 4 * j;
+        w[j] = quant_exact(y[d], s) | (quant_exact(y[d + 1], s) << 8) | (quant_exact(y[d + 2], s) << 16) |
+               (quant_exact(y[d + 3], s) << 24);
+      }
+      q[k] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  }
+  (side ? p.v_scales : p.k_scales)[dst * p.H + head] = s;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    k_kv_project(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_wk,
+                 const __grid_constant__ CUtensorMap tm_wv, const KvProjectParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  // bars: full[STAGES], empty[STAGES], tfull[2], tempty[2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
+  volatile uint32_t* abort_flag = tmem_slot + 1;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int dim = p.H * 128;
+  const int n_half = dim / BN;  // N tiles per side
+  const int tiles_m = int((p.M + BM - 1) / BM);
+  const int n_tiles = tiles_m * 2 * n_half;
+  const int kb_count = dim / BK;
+
+  const uint32_t smem_base = smem_u32(smem);
+  auto full_bar = [&](int s) { return smem_u32(bars + s); };
+  auto empty_bar = [&](int s) { return smem_u32(bars + STAGES + s); };
+  auto tfull_bar = [&](int b) { return smem_u32(bars + 2 * STAGES + b); };
+  auto tempty_bar = [&](int b) { return smem_u32(bars + 2 * STAGES + 2 + b); };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(tfull_bar(b), 1);
+      mbar_init(tempty_bar(b), 4);  // one arrival per epilogue warp
+    }
+    *abort_flag = 0u;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------- TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int t = blockIdx.x; t < n_tiles && !*abort_flag; t += gridDim.x) {
+        const int tm = t % tiles_m, tn = t / tiles_m;
+        const int side = tn / n_half, n0 = (tn % n_half) * BN;
+        const CUtensorMap* wmap = side ? &tm_wv : &tm_wk;
+        for (int kb = 0; kb < kb_count; ++kb) {
+          if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag, p.err)) break;
+          const uint32_t a_dst = smem_base + stage * STAGE_BYTES;
+          mbar_expect_tx(full_bar(stage), STAGE_BYTES);
+          tma_load_2d(a_dst, &tm_x, kb * BK, tm * BM, full_bar(stage));
+          tma_load_2d(a_dst + A_BYTES, wmap, kb * BK, n0, full_bar(stage));
+          if (++stage == STAGES) stage = 0, phase ^= 1u;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int buf = 0;
+      uint32_t acc_phase = 0;
+      for (int t = blockIdx.x; t < n_tiles && !*abort_flag; t += gridDim.x) {
+        if (!mbar_wait(tempty_bar(buf), acc_phase ^ 1u, abort_flag, p.err)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + uint32_t(buf * BN);
+        bool ok = true;
+        for (int kb = 0; kb < kb_count; ++kb) {
+          if (!mbar_wait(full_bar(stage), phase, abort_flag, p.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_base + stage * STAGE_BYTES;
+          const uint64_t adesc = smem_desc(a_addr), bdesc = smem_desc(a_addr + A_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)  // +32 bytes per K step = +2 in the address field
+            umma_bf16(d_tmem, adesc + uint64_t(2 * k), bdesc + uint64_t(2 * k), (kb | k) != 0 ? 1u : 0u);
+          umma_commit(empty_bar(stage));
+          if (++stage == STAGES) stage = 0, phase ^= 1u;
+        }
+        if (!ok) break;
+        umma_commit(tfull_bar(buf));
+        if (++buf == 2) buf = 0, acc_phase ^= 1u;
+      }
+    }
+  } else {
+    // ---------------------------------------------------- epilogue
+    const int quad = warp & 3;
+    int buf = 0;
+    uint32_t acc_phase = 0;
+    bool bad = false;
+    for (int t = blockIdx.x; t < n_tiles; t += gridDim.x) {
+      if (!mbar_wait(tfull_bar(buf), acc_phase, abort_flag, p.err)) break;
+      tc_fence_after();
+      const int tm = t % tiles_m, tn = t / tiles_m;
+      const int side = tn / n_half, head0 = (tn % n_half) * (BN / 128);
+      const int64_t row = int64_t(tm) * BM + quad * 32 + lane;
+      const uint32_t taddr = tmem_base + (uint32_t(quad * 32) << 16) + uint32_t(buf * BN);
+#pragma unroll 1
+      for (int hh = 0; hh < BN / 128; ++hh) {
+        float y[128];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tmem_ld32(taddr + uint32_t(hh * 128 + c * 32), y + c * 32);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tmem_wait32(y + c * 32);
+        if (hh == BN / 128 - 1) {
+          // the accumulator is in registers: hand it back to the MMA warp
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(tempty_bar(buf));
+        }
+        if (row < p.M) epilogue_head(y, p, side, row, head0 + hh, bad);
+      }
+      if (__any_sync(0xFFFFFFFFu, bad)) {
+        if (lane == 0) atomicOr(p.flag, 1u << side);
+        bad = false;
+      }
+      if (++buf == 2) buf = 0, acc_phase ^= 1u;
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (*abort_flag && threadIdx.x == 0) {
+    // copies or MMAs of an aborted CTA may still be in flight: give them a
+    // bounded 1 ms to land before the memory they target is released
+    const uint64_t t0 = globaltimer();
+    while (globaltimer() - t0 < 1000000ull) {
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS) : "memory");
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+// Row-major bf16 matrix of `rows` x `cols` as a 2-D tensor map with a
+// (64 columns x box_rows) 128-byte-swizzled box.
+bool make_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return false;
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {cols * 2};
+  const cuuint32_t box[2] = {uint32_t(BK), box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+bool kv_project_shape_ok(int64_t M, int H, int D) { return M > 0 && D == 128 && H > 0 && (H * D) % BN == 0; }
+
+cudaError_t launch_kv_project(const void* x, const void* wk, const void* wv, const KvProjectParams& p,
+                              cudaStream_t stream) {
+  if (!kv_project_shape_ok(p.M, p.H, 128)) return cudaErrorInvalidValue;
+  const uint64_t dim = uint64_t(p.H) * 128;
+  CUtensorMap mx, mk, mv;
+  if (!make_map(&mx, x, uint64_t(p.M), dim, BM) || !make_map(&mk, wk, dim, dim, BN) ||
+      !make_map(&mv, wv, dim, dim, BN))
+    return cudaErrorInvalidValue;
+  static int configured_device = -1;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (configured_device != dev) {
+    e = cudaFuncSetAttribute(k_kv_project, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (e != cudaSuccess) return e;
+    configured_device = dev;
+  }
+  int sms = 0;
+  e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return e;
+  const int tiles = int((p.M + BM - 1) / BM) * int(2 * dim / BN);
+  const int grid = tiles < sms ? tiles : sms;
+  k_kv_project<<<grid, kThreads, kSmemBytes, stream>>>(mx, mk, mv, p);
+  return cudaGetLastError();
+}
+
+}  // namespace nkv

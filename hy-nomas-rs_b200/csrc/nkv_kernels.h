@@ -163,4 +163,37 @@ cudaError_t launch_qvg_decode(const float* cb_side, const uint8_t* codes, const 
 cudaError_t launch_synth_fill(void* dst, int dtype, uint64_t rows, int H, int D, uint64_t key,
                               uint64_t index_offset, const float* table, const float* chan_scale, cudaStream_t s);
 
+// Fused K/V projection + commit producer (kernels_project.cu).  x is the
+// (M, H*128) bf16 input of one layer, W_k / W_v the (H*128, H*128) bf16
+// nn.Linear weights ([out][in]); every other pointer may be null where the
+// comment says so.
+struct KvProjectParams {
+  int64_t M;                        // tokens
+  int32_t H;                        // heads (head_dim is 128; H*128 % 256 == 0)
+  int32_t qk_norm;                  // RmsNorm on K (attention.rs:120-122)
+  float eps;                        // RmsNorm eps as f32
+  const uint16_t* bias_k;           // (H*128) bf16 or null
+  const uint16_t* bias_v;
+  const uint16_t* k_gain;           // (128) bf16 RmsNorm gain or null (no gain)
+  const float* rope_cos;            // (M, 64) f32 or null (no rotation)
+  const float* rope_sin;
+  uint16_t* k_out;                  // (M, H*128) bf16 or null
+  uint16_t* v_out;
+  uint8_t* k_codes;                 // INT8 archive rows or null (no codes)
+  float* k_scales;
+  uint8_t* v_codes;
+  float* v_scales;
+  int32_t n_ranges;                 // rows [lo, hi) of x -> archive rows dst.. (at most 2)
+  int64_t range_lo[2], range_hi[2], range_dst[2];
+  uint32_t* flag;                   // bit 0: non-finite K, bit 1: V, in a committed row
+  uint32_t* err;                    // kProjectTimeoutBit is OR-ed in when a bounded wait ran out
+};
+constexpr uint32_t kProjectTimeoutBit = 0x80000000u;
+bool kv_project_shape_ok(int64_t M, int H, int D);
+// OR of flags[1..n] into flags[0] (a staged commit's per-layer status words
+// into the word the rebuild gather aborts on)
+cudaError_t launch_flag_reduce(uint32_t* flags, int n, cudaStream_t s);
+cudaError_t launch_kv_project(const void* x, const void* wk, const void* wv, const KvProjectParams& p,
+                              cudaStream_t stream);
+
 }  // namespace nkv

@@ -1,0 +1,42 @@
+// nkv_quant.cuh — per-value INT8 code arithmetic of quantize_one
+// (cache/int8.rs:65-81), shared by the commit kernels and the fused K/V
+// projection epilogue.  The derivation (Markstein quotient, half-away-from-
+// zero rounding by the 1.5 * 2^23 constant) is described where the commit
+// kernels use it (kernels_commit.cu).
+#pragma once
+#include <cfloat>
+#include <cstdint>
+
+#include "nkv_device.cuh"
+
+namespace nkv {
+
+// round_half_away(x / s) + 128 as a byte, with an IEEE division: the path
+// for scales outside [FLT_MIN, 1e37].
+__device__ __forceinline__ uint32_t quant_exact(float x, float s) {
+  float t = roundf(__fdiv_rn(x, s));
+  t = dev::cmin(dev::cmax(t, -127.0f), 127.0f);
+  t = __fadd_rn(__fmul_rn(t, 1.0f), 128.0f);
+  t = dev::cmin(dev::cmax(t, 0.0f), 255.0f);
+  return dev::as_u8(t);
+}
+
+// Code of one value: (round_half_away(RN(x / s)) + 128) in the low byte of
+// the returned f32 bit pattern's 8 LSBs XOR 0x80 (see kernel notes); valid
+// for s in [FLT_MIN, 1e37] with r = RN(1/s).
+__device__ __forceinline__ uint32_t code_bits(float x, float s, float r) {
+  const float M = 12582912.0f;  // 1.5 * 2^23
+  const float q0 = __fmul_rn(x, r);
+  const float e = __fmaf_rn(-q0, s, x);
+  const float q1 = __fmaf_rn(e, r, q0);                  // RN(x / s)
+  const float t = __fadd_rn(__fadd_rn(q1, M), -M);       // round to nearest even
+  const float hv = __fadd_rn(q1, copysignf(0.5f, q1));   // exact on a .5 tie
+  const float f = fabsf(__fadd_rn(q1, -t)) == 0.5f ? hv : t;
+  return __float_as_uint(__fadd_rn(f, M));               // low byte: f mod 256
+}
+
+__device__ __forceinline__ uint32_t pack4(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410) ^ 0x80808080u;
+}
+
+}  // namespace nkv

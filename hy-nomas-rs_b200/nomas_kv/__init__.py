@@ -488,10 +488,97 @@ class KvBank:
         """Restore a saved archive into this fresh bank and rebuild the working set."""
         _check(lib().nkv_bank_load(self._h, str(path).encode()))
 
+    # -- two-phase INT8 commit for a producer that writes the archive rows
+    def stage_segment(self, desc: _abi.nkv_segment_desc) -> list[dict]:
+        """Validate `desc` and reserve its INT8 record; per local layer the
+        device addresses of k_codes / v_codes (B, L, H, D) u8, k_scales /
+        v_scales (B, L, H) f32 and the layer's status word."""
+        arr = (_abi.nkv_staged_layer * self.n_layers)()
+        _check(lib().nkv_bank_stage_segment(self._h, C.byref(desc), arr))
+        return [{f: int(getattr(a, f) or 0) for f, _ in _abi.nkv_staged_layer._fields_} for a in arr]
+
+    def commit_staged(self) -> None:
+        _check(lib().nkv_bank_commit_staged(self._h))
+
+    def discard_staged(self) -> None:
+        _check(lib().nkv_bank_discard_staged(self._h))
+
+    def commit_projected(self, desc: _abi.nkv_segment_desc, xs, weights, rope=None, k_outs=None, v_outs=None,
+                         qk_norm: bool = True, eps: float = 1e-6) -> None:
+        """Commit a segment whose K / V are the projections of xs[i] (layer
+        i's (L, H*D) bf16 attention input) by weights[i] = dict(wk, wv, bk,
+        bv, k_gain): nkv_kv_project writes the archive rows (and the bf16
+        K / V into k_outs / v_outs when given), then the staged commit
+        archives and rebuilds.  Batch 1, head_dim 128."""
+        staged = self.stage_segment(desc)
+        L = desc.image_tokens + desc.text_tokens
+        try:
+            for i in range(self.n_layers):
+                w = weights[i]
+                kv_project(xs[i], w["wk"], w["wv"], bk=w.get("bk"), bv=w.get("bv"), k_gain=w.get("k_gain"),
+                           qk_norm=qk_norm, eps=eps, rope=rope,
+                           k_out=None if k_outs is None else k_outs[i], v_out=None if v_outs is None else v_outs[i],
+                           codes=staged[i], ranges=[(0, L, 0)], status_ptr=staged[i]["status"],
+                           stream=self.stream)
+        except Exception:
+            self.discard_staged()
+            raise
+        self.commit_staged()
+
     def kernel_stats(self, reset: bool = False) -> dict:
         arr = (_abi.nkv_kernel_stat * _abi.NKV_KERNEL_COUNT)()
         _check(lib().nkv_bank_kernel_stats(self._h, arr, int(reset)))
         return {n: (int(arr[i].launches), float(arr[i].total_ms)) for i, n in enumerate(_abi.KERNEL_NAMES)}
+
+
+def kv_project(x, wk, wv, bk=None, bv=None, k_gain=None, qk_norm: bool = True, eps: float = 1e-6, rope=None,
+               k_out=None, v_out=None, codes=None, ranges=None, status=None, status_ptr: int = 0, stream=None):
+    """nkv_kv_project on torch tensors (one layer, batch 1): the captured
+    K / V of modules/attention.rs:107-124, 143-144 with the INT8 archive rows
+    of the committed ranges.  x (tokens, H*128) bf16; wk / wv (H*128, H*128)
+    bf16; bk / bv / k_gain bf16 or None; rope = (cos, sin) f32 (tokens, 64)
+    or None; k_out / v_out bf16 (tokens, H*128) or None; codes = dict with
+    k_codes / v_codes / k_scales / v_scales (tensors or device addresses) or
+    None; ranges = [(lo, hi, dst), ...]; status = a 1-element int32/uint32
+    device tensor (or status_ptr an address) that receives the non-finite
+    bits."""
+    torch = _torch()
+    if x.dim() != 2 or x.dtype != torch.bfloat16:
+        raise ArgumentError("x must be a (tokens, H*128) bf16 tensor")
+    tokens, dim = x.shape
+    addr = lambda t: 0 if t is None else (t if isinstance(t, int) else t.data_ptr())  # noqa: E731
+    for name, t in (("x", x), ("wk", wk), ("wv", wv), ("bk", bk), ("bv", bv), ("k_gain", k_gain),
+                    ("k_out", k_out), ("v_out", v_out)):
+        if t is not None and not isinstance(t, int):
+            if t.dtype != torch.bfloat16 or not t.is_contiguous() or t.device != x.device:
+                raise ArgumentError(f"{name} must be a contiguous bf16 tensor on {x.device}")
+    if wk.shape != (dim, dim) or wv.shape != (dim, dim):
+        raise GeometryError(f"weights must be ({dim}, {dim})")
+    a = _abi.nkv_kv_project_args()
+    a.tokens, a.heads, a.head_dim = tokens, dim // 128, 128
+    a.x, a.wk, a.wv, a.bk, a.bv = addr(x), addr(wk), addr(wv), addr(bk), addr(bv)
+    a.qk_norm, a.eps, a.k_norm_gain = int(bool(qk_norm)), float(eps), addr(k_gain)
+    if rope is not None:
+        cos, sin = rope
+        for t in (cos, sin):
+            if t.dtype != torch.float32 or tuple(t.shape) != (tokens, 64) or not t.is_contiguous():
+                raise GeometryError("rope tables must be contiguous f32 (tokens, 64)")
+        a.rope_cos, a.rope_sin = addr(cos), addr(sin)
+    a.k_out, a.v_out = addr(k_out), addr(v_out)
+    if codes is not None:
+        a.k_codes, a.k_scales = addr(codes["k_codes"]), addr(codes["k_scales"])
+        a.v_codes, a.v_scales = addr(codes["v_codes"]), addr(codes["v_scales"])
+        rs = list(ranges) if ranges is not None else [(0, tokens, 0)]
+        if len(rs) > 2:
+            raise ArgumentError("at most two row ranges")
+        a.n_ranges = len(rs)
+        for i, (lo, hi, dst) in enumerate(rs):
+            a.ranges[i].lo, a.ranges[i].hi, a.ranges[i].dst = lo, hi, dst
+    a.status = status_ptr if status is None else status.data_ptr()
+    if stream is None:
+        stream = torch.cuda.current_stream(x.device)
+    with torch.cuda.device(x.device):
+        _check(lib().nkv_kv_project(C.byref(a), C.c_void_p(stream.cuda_stream)))
 
 
 def build_cache(cfg: CacheConfig, batch: int, heads: int, head_dim: int, dtype, device=None) -> KvBank:

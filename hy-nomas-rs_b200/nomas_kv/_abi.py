@@ -107,6 +107,28 @@ class nkv_kernel_stat(C.Structure):
     _fields_ = [("launches", C.c_uint64), ("total_ms", C.c_double)]
 
 
+class nkv_staged_layer(C.Structure):
+    _fields_ = [("k_codes", C.c_void_p), ("v_codes", C.c_void_p), ("k_scales", C.c_void_p),
+                ("v_scales", C.c_void_p), ("status", C.c_void_p)]
+
+
+class nkv_row_range(C.Structure):
+    _fields_ = [("lo", C.c_int64), ("hi", C.c_int64), ("dst", C.c_int64)]
+
+
+class nkv_kv_project_args(C.Structure):
+    _fields_ = [
+        ("tokens", C.c_int64), ("heads", C.c_int32), ("head_dim", C.c_int32),
+        ("x", C.c_void_p), ("wk", C.c_void_p), ("bk", C.c_void_p), ("wv", C.c_void_p), ("bv", C.c_void_p),
+        ("qk_norm", C.c_int32), ("eps", C.c_float), ("k_norm_gain", C.c_void_p),
+        ("rope_cos", C.c_void_p), ("rope_sin", C.c_void_p),
+        ("k_out", C.c_void_p), ("v_out", C.c_void_p),
+        ("k_codes", C.c_void_p), ("k_scales", C.c_void_p), ("v_codes", C.c_void_p), ("v_scales", C.c_void_p),
+        ("n_ranges", C.c_int32), ("ranges", nkv_row_range * 2),
+        ("status", C.c_void_p),
+    ]
+
+
 P = C.c_void_p
 U64 = C.c_uint64
 I64 = C.c_int64
@@ -131,6 +153,9 @@ SIGNATURES = {
     "nkv_bank_kernel_stats": (C.c_int, [P, C.POINTER(nkv_kernel_stat), I32]),
     "nkv_bank_save": (C.c_int, [P, C.c_char_p]),
     "nkv_bank_load": (C.c_int, [P, C.c_char_p]),
+    "nkv_bank_stage_segment": (C.c_int, [P, C.POINTER(nkv_segment_desc), C.POINTER(nkv_staged_layer)]),
+    "nkv_bank_commit_staged": (C.c_int, [P]),
+    "nkv_bank_discard_staged": (C.c_int, [P]),
     "nkv_cache_working_set": (C.c_int, [P, I32, C.POINTER(P), C.POINTER(P), C.POINTER(U64)]),
     "nkv_cache_layout": (C.c_int, [P, I32, C.POINTER(nkv_segment_layout), U64, C.POINTER(U64)]),
     "nkv_cache_info": (C.c_int, [P, I32, C.POINTER(nkv_cache_info_t)]),
@@ -146,6 +171,7 @@ SIGNATURES = {
     "nkv_qvg_encode": (C.c_int, [P, I32, P, I32, U64, I64, I64, U64, I32, I32, I32, P, P, P]),
     "nkv_qvg_decode": (C.c_int, [P, I32, P, P, U64, I64, I64, I32, I32, I32, P, P]),
     "nkv_synth_fill": (C.c_int, [P, I32, U64, I64, I64, U64, U64, P, P, P]),
+    "nkv_kv_project": (C.c_int, [C.POINTER(nkv_kv_project_args), P]),
     "nkv_int8_quantize_layers_noalloc": (C.c_int, [C.POINTER(P), C.POINTER(P), I32, I32, U64, I64, C.POINTER(P),
                                                    C.POINTER(P), C.POINTER(P), C.POINTER(P),
                                                    C.POINTER(C.c_uint32), P]),

@@ -219,6 +219,33 @@ int nkv_bank_decode_segment(nkv_bank* bank, uint64_t archive_pos, void* const* k
 int nkv_bank_set_timing(nkv_bank* bank, int32_t enable);
 int nkv_bank_kernel_stats(nkv_bank* bank, nkv_kernel_stat* out /* [NKV_KERNEL_COUNT] */, int32_t reset);
 
+/* Two-phase INT8 commit for a producer that writes the archive rows itself,
+ * such as nkv_kv_project below (no reference counterpart: it splits
+ * KvBank::commit, cache/mod.rs:257-268, around archive_segment's quantize,
+ * history.rs:248-253, so the K/V need not be read back).
+ *  - nkv_bank_stage_segment: validate_segment (history.rs:168-238) without
+ *    the input-tensor checks, then reserve the segment's record; out[i] gets
+ *    local layer i's INT8 planes — k_codes / v_codes (B, L, H, D) u8
+ *    (int8 + 128), k_scales / v_scales (B, L, H) f32 — and its status word,
+ *    into which the producer ORs bit 0 (non-finite K) / bit 1 (V).  INT8
+ *    storage only (else NKV_ERR_INVALID_CONFIG); one staged segment at a
+ *    time; commit, rollback, save and load are refused while one is pending.
+ *  - nkv_bank_commit_staged: archive the staged record and rebuild, with
+ *    nkv_bank_commit's semantics from the non-finite check on (a set status
+ *    bit rejects the segment, NKV_ERR_MSG, and nothing changes).  The
+ *    producer's work must be ordered before the bank's stream.
+ *  - nkv_bank_discard_staged: drop it (waits for the bank's stream). */
+typedef struct {
+  uint8_t* k_codes;
+  uint8_t* v_codes;
+  float* k_scales;
+  float* v_scales;
+  uint32_t* status;
+} nkv_staged_layer;
+int nkv_bank_stage_segment(nkv_bank* bank, const nkv_segment_desc* seg, nkv_staged_layer* out /* [n_layers] */);
+int nkv_bank_commit_staged(nkv_bank* bank);
+int nkv_bank_discard_staged(nkv_bank* bank);
+
 /* Archive persistence.  No counterpart in the reference, whose archive lives
  * in memory only.  nkv_bank_save writes the segment timeline, the counters,
  * the QVG codebooks and every archived payload of the bank's local layers to
@@ -319,6 +346,57 @@ int nkv_qvg_encode(const float* cb_dev, int32_t side, const void* x, int32_t in_
 int nkv_qvg_decode(const float* cb_dev, int32_t side, const uint8_t* codes, const float* scales, uint64_t tokens,
                    int64_t heads, int64_t head_dim, int32_t stages, int32_t bits, int32_t block, float* out,
                    void* stream);
+
+/* The captured K / V of one layer with the commit's quantize in the same
+ * kernel (tcgen05 GEMM, TMA, sm_100a), batch 1:
+ *   K = apply_rotary(RmsNorm_k(Lin_k(x)))   modules/attention.rs:107-124, 143-144;
+ *                                           modules/mod.rs:122-142; norm.rs:55-65;
+ *                                           rope.rs:257-306
+ *   V = Lin_v(x)
+ * with every intermediate rounded to bf16 where the reference rounds it, and
+ * for each row of x inside `ranges`, quantize_one (cache/int8.rs:65-81) of
+ * that K / V row per head into the INT8 planes (row lo + i of x -> plane row
+ * dst + i).  x is (tokens, H*D) bf16; wk / wv the (H*D, H*D) nn.Linear
+ * weights ([out][in]) bf16; bk / bv (H*D) bf16 or NULL (no bias);
+ * k_norm_gain (D) bf16 or NULL (no gain); qk_norm = 0 skips the norm;
+ * rope_cos / rope_sin (tokens, D/2) f32 or NULL (no rotation); k_out / v_out
+ * (tokens, H*D) bf16 or NULL; k_codes.. NULL for no codes.  Requirements:
+ * D = 128, H*D a multiple of 256, every pointer 16-byte aligned (else
+ * NKV_ERR_ARGUMENT).  *status (device word) gets bit 0 / bit 1 for a
+ * non-finite K / V value in a range row, bit 31 if a bounded wait inside the
+ * kernel ran out.  Stream-ordered on `stream` on the current device; no
+ * synchronisation.  Differences from the reference: the sum of squares is
+ * taken as four interleaved f32 partial sums and (var + eps)^-1/2 as
+ * 1 / sqrt with IEEE operations (candle: its own reduction order and powf);
+ * the GEMM accumulates in f32 on the tensor cores (candle: cuBLAS). */
+typedef struct {
+  int64_t lo, hi, dst;
+} nkv_row_range;
+typedef struct {
+  int64_t tokens;
+  int32_t heads;
+  int32_t head_dim;
+  const void* x;
+  const void* wk;
+  const void* bk;
+  const void* wv;
+  const void* bv;
+  int32_t qk_norm;
+  float eps;
+  const void* k_norm_gain;
+  const float* rope_cos;
+  const float* rope_sin;
+  void* k_out;
+  void* v_out;
+  uint8_t* k_codes;
+  float* k_scales;
+  uint8_t* v_codes;
+  float* v_scales;
+  int32_t n_ranges;
+  nkv_row_range ranges[2];
+  uint32_t* status;
+} nkv_kv_project_args;
+int nkv_kv_project(const nkv_kv_project_args* args, void* stream);
 
 /* Deterministic synthetic K/V for tests and benchmarks (no reference
  * counterpart): element (t, h, d) of a (rows = B*L, H, D) tensor is

@@ -1401,4 +1401,73 @@ uint64_t orc_splitmix_next(uint64_t* state) {
 uint16_t orc_bf16_bits(float x) { return bf16_bits(x); }
 uint16_t orc_f16_bits(float x) { return f16_bits(x); }
 
+// The captured K / V of one layer (batch 1), the producer side of a commit:
+//   Lin (modules/mod.rs:122-142): bf16 result of x W^T, then + bias in bf16;
+//   RmsNorm on K (modules/attention.rs:117-122, modules/norm.rs:55-65) when
+//     qk_norm: f32 mean of squares over the head dim, (var + eps)^-1/2, times
+//     the optional gain, to bf16;
+//   apply_rotary on K (attention.rs:144, rope.rs:257-306) when cos/sin are
+//     given: interleaved pairs, r*c - i*s and i*c + r*s in f32, to bf16.
+// The matrix product is accumulated in f64 and rounded to f32 before the
+// bf16 rounding (exact whenever every partial sum is, which the bit-exact
+// tests arrange); squares are summed as four interleaved partial sums
+// (d mod 4) added as (s0 + s1) + (s2 + s3), and (var + eps)^-1/2 is
+// 1 / sqrt(var + eps) with IEEE square root and division — the order and the
+// operations the device epilogue uses (the reference leaves the reduction
+// order to candle and uses powf).
+int orc_kv_project(const uint16_t* x, const uint16_t* wk, const uint16_t* bk, const uint16_t* wv,
+                   const uint16_t* bv, const uint16_t* k_gain, int32_t qk_norm, float eps, const float* cos_t,
+                   const float* sin_t, uint64_t M, uint64_t H, uint64_t D, uint16_t* k_out, uint16_t* v_out) {
+  const uint64_t dim = H * D;
+  std::vector<float> xf(M * dim), wf(dim * dim), row(dim);
+  for (uint64_t i = 0; i < M * dim; ++i) xf[i] = bf16_value(x[i]);
+  for (int side = 0; side < 2; ++side) {
+    const uint16_t* w = side ? wv : wk;
+    const uint16_t* b = side ? bv : bk;
+    uint16_t* out = side ? v_out : k_out;
+    for (uint64_t i = 0; i < dim * dim; ++i) wf[i] = bf16_value(w[i]);
+    for (uint64_t t = 0; t < M; ++t) {
+      for (uint64_t n = 0; n < dim; ++n) {
+        double acc = 0.0;
+        const float* xr = &xf[t * dim];
+        const float* wr = &wf[n * dim];
+        for (uint64_t k = 0; k < dim; ++k) acc += double(xr[k]) * double(wr[k]);
+        float y = bf16_value(bf16_bits(float(acc)));
+        if (b) y = bf16_value(bf16_bits(y + bf16_value(b[n])));
+        row[n] = y;
+      }
+      for (uint64_t h = 0; h < H; ++h) {
+        float* y = &row[h * D];
+        if (side == 0 && qk_norm) {
+          float s[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+          for (uint64_t d = 0; d < D; ++d) {
+            const float sq = y[d] * y[d];
+            s[d & 3] = s[d & 3] + sq;
+          }
+          const float ss = (s[0] + s[1]) + (s[2] + s[3]);
+          const float var = ss * (1.0f / float(D));
+          const float root = std::sqrt(var + eps);
+          const float inv = 1.0f / root;
+          for (uint64_t d = 0; d < D; ++d) {
+            float o = y[d] * inv;
+            if (k_gain) o = o * bf16_value(k_gain[d]);
+            y[d] = bf16_value(bf16_bits(o));
+          }
+        }
+        if (side == 0 && cos_t) {
+          for (uint64_t j = 0; j < D / 2; ++j) {
+            const float c = cos_t[t * (D / 2) + j], sn = sin_t[t * (D / 2) + j];
+            const float xr = y[2 * j], xi = y[2 * j + 1];
+            const float a = xr * c, bb = xi * sn, e = xi * c, f = xr * sn;
+            y[2 * j] = bf16_value(bf16_bits(a - bb));
+            y[2 * j + 1] = bf16_value(bf16_bits(e + f));
+          }
+        }
+      }
+      for (uint64_t n = 0; n < dim; ++n) out[t * dim + n] = bf16_bits(row[n]);
+    }
+  }
+  return OK;
+}
+
 }  // extern "C"

@@ -149,6 +149,8 @@ def lib():
         _lib.orc_qvg_payload_bytes.argtypes = [C.c_uint64] * 5
         _lib.orc_plan_recent_trim.argtypes = [C.c_void_p, C.c_uint64, C.c_uint64, C.c_uint64] + [C.c_void_p] * 7
         _lib.orc_splitmix_next.argtypes = [C.POINTER(C.c_uint64)]
+        _lib.orc_kv_project.argtypes = [C.c_void_p] * 6 + [C.c_int32, C.c_float, C.c_void_p, C.c_void_p] + [
+            C.c_uint64] * 3 + [C.c_void_p] * 2
     return _lib
 
 
@@ -244,6 +246,26 @@ def dequantize(q: np.ndarray, s: np.ndarray, valid: int, dtype: int) -> np.ndarr
     s = np.ascontiguousarray(s, np.float32)
     _check(lib().orc_dequantize(_ptr(q), _ptr(s), B, L, H, D, valid, dtype, _ptr(out)))
     return out
+
+
+def kv_project(x, wk, wv, bk=None, bv=None, k_gain=None, qk_norm=False, eps=1e-6, cos=None, sin=None,
+               head_dim: int = 128):
+    """Captured K / V of one layer (modules/attention.rs:107-124, 143-144):
+    bf16 bit arrays in (x: (M, H*D), w*: (H*D, H*D), b*: (H*D,), k_gain:
+    (D,)), f32 rope tables (M, D/2); returns the bf16 bits of K and V,
+    (M, H*D) each."""
+    x = np.ascontiguousarray(x, dtype=np.uint16)
+    M, dim = x.shape
+    H = dim // head_dim
+    arrs = [np.ascontiguousarray(a, dtype=np.uint16) if a is not None else None for a in (wk, bk, wv, bv, k_gain)]
+    tabs = [np.ascontiguousarray(a, dtype=np.float32) if a is not None else None for a in (cos, sin)]
+    k = np.empty((M, dim), np.uint16)
+    v = np.empty((M, dim), np.uint16)
+    p = lambda a: None if a is None else a.ctypes.data  # noqa: E731
+    _check(lib().orc_kv_project(x.ctypes.data, p(arrs[0]), p(arrs[1]), p(arrs[2]), p(arrs[3]), p(arrs[4]),
+                                int(bool(qk_norm)), float(np.float32(eps)), p(tabs[0]), p(tabs[1]), M, H, head_dim,
+                                k.ctypes.data, v.ctypes.data))
+    return k, v
 
 
 def qvg_fit(k: np.ndarray, v: np.ndarray, stages: int = 4, bits: int = 2, seed: int = 0x5EED0002) -> np.ndarray:
