@@ -100,8 +100,10 @@ def load_peaks() -> dict:
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
         d = json.load(open(p))
-        return {"hbm_gbs": float(d["hbm_gbs"]), "src": "measured"}
-    return {"hbm_gbs": 6650.0, "src": "fallback"}
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d.get("bf16_tflops", 1590.0)),
+                "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", d.get("bf16_tflops", 1400.0))),
+                "src": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "src": "fallback"}
 
 
 # ------------------------------------------------------------------ clocks
@@ -227,6 +229,46 @@ def cpu_sample(threads: int, warmup: int = 1, steps: int = 1, workload: str = "i
             "sample": f"{n} layer(s) x {len(times)} turn(s) ({workload.upper()}: {what}) at 8B geometry, "
                       f"archive of {archived} segments, one host thread per layer; "
                       f"{sec:.2f} s per turn"}
+
+
+def cpu_sample_project(threads: int, rows: int = 96) -> dict:
+    """The oracle's restatement of the producer chain (Lin + bias, RmsNorm,
+    RoPE; modules/attention.rs:107-124, 143-144) plus quantize_kv_pair for
+    `rows` tokens of one layer at the 8B geometry, one layer per host
+    thread; scaled to segment tokens/s over all 48 layers.  The archive /
+    rebuild part of the turn is left out: it is under 0.1 % of the
+    projection's CPU time."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import numpy as np
+    import oracle as orc
+
+    orc.build()
+    rng = np.random.default_rng(0)
+    b = lambda a: orc.bf16_bits(np.asarray(a, np.float32))  # noqa: E731
+    dim = HEADS * HEAD_DIM
+    w = [dict(wk=b(rng.standard_normal((dim, dim)) / np.sqrt(dim)), wv=b(rng.standard_normal((dim, dim)) / np.sqrt(dim)),
+              bk=b(0.1 * rng.standard_normal(dim)), bv=b(0.1 * rng.standard_normal(dim)),
+              gain=b(1 + 0.1 * rng.standard_normal(HEAD_DIM))) for _ in range(threads)]
+    x = b(rng.standard_normal((rows, dim)))
+    ang = rng.uniform(0, 6.3, (rows, HEAD_DIM // 2)).astype(np.float32)
+    cos, sin = np.cos(ang), np.sin(ang)
+
+    def one(i):
+        k, v = orc.kv_project(x, w[i]["wk"], w[i]["wv"], bk=w[i]["bk"], bv=w[i]["bv"], k_gain=w[i]["gain"],
+                              qk_norm=True, eps=1e-6, cos=cos, sin=sin)
+        orc.quantize_kv_pair(k.reshape(1, rows, HEADS, HEAD_DIM), v.reshape(1, rows, HEADS, HEAD_DIM), orc.BF16)
+
+    t0 = time.perf_counter()
+    ths = [threading.Thread(target=one, args=(i,)) for i in range(threads)]
+    for t in ths:
+        t.start()
+    for t in ths:
+        t.join()
+    sec = time.perf_counter() - t0
+    value = rows * threads / sec / LAYERS  # tokens/s through all 48 layers
+    return {"value": value, "unit": "segment tokens/s (all layers)", "cores": threads, "kind": "port",
+            "sample": f"{rows} tokens x {threads} layer(s) of the producer chain + quantize at the 8B geometry "
+                      f"(f64-accumulated GEMM, one host thread per layer), {sec:.2f} s; scaled to 48 layers"}
 
 
 # ------------------------------------------------------------ GPU side
@@ -490,12 +532,230 @@ def run_gpu(args) -> None:
         dist.destroy_process_group()
 
 
+# ------------------------------------------------- producer (projection)
+METRIC_PROJECT = "captured-K/V commit tokens/s (8B geometry, INT8, fused K/V projection producer)"
+DIM = HEADS * HEAD_DIM  # 3072
+PROJECT_FLOPS = 2 * SEG_TOKENS * (2 * DIM) * DIM  # one layer's K and V projection of a segment
+
+
+def run_project(args) -> None:
+    """The commit with its producer: per layer, the K / V projection of the
+    segment's attention input (Lin + bias, RmsNorm and RoPE on K) with the
+    INT8 archive rows written by the same tcgen05 kernel (nkv_kv_project),
+    then the staged commit (archive + uniform rebuild) and the newest-segment
+    gather.  Beside it, the same turn unfused (cuBLAS projection, the bias /
+    RmsNorm / RoPE chain in eager PyTorch, then commit_tensors, which
+    quantizes) and cuBLAS alone on the same GEMM shape."""
+    import torch
+    import torch.distributed as dist
+    import nomas_kv as nk
+    from nomas_kv import synth
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    begin, n_layers = nk.partition_layers(args.layers, world, rank)
+    stream = torch.cuda.current_stream(dev)
+    cfg = nk.CacheConfig(storage=nk.CacheStorage.int8(), sampling=nk.HistorySampling.uniform(), past_frames=PAST)
+    bank = nk.KvBank(cfg, n_layers, 1, HEADS, HEAD_DIM, torch.bfloat16, device=dev, layer_begin=begin)
+    desc = lambda i: nk._abi.nkv_segment_desc(i, i * FRAMES, FRAMES, FRAMES * TPF, TEXT, 0)  # noqa: E731
+    L = SEG_TOKENS
+    e2e_steps = 2
+    prefill = ARCHIVED - 1 - args.warmup
+    total = prefill + 2 * (args.warmup + args.steps) + e2e_steps + 2
+    bank.reserve(bank.segment_bytes(desc(0)) * n_layers * total, rebuild_tokens())
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(1234 + begin)
+    def randn(*shape, scale=1.0):  # noqa: E306
+        return (torch.randn(*shape, device=dev, generator=g) * scale).to(torch.bfloat16)
+    wk = [randn(DIM, DIM, scale=DIM ** -0.5) for _ in range(n_layers)]
+    wv = [randn(DIM, DIM, scale=DIM ** -0.5) for _ in range(n_layers)]
+    bk = [randn(DIM, scale=0.1) for _ in range(n_layers)]
+    bv = [randn(DIM, scale=0.1) for _ in range(n_layers)]
+    gain = [(1 + randn(HEAD_DIM, scale=0.1).float()).to(torch.bfloat16) for _ in range(n_layers)]
+    wkv = [torch.cat([wk[i], wv[i]], 0) for i in range(n_layers)]  # the unfused arm's one GEMM per layer
+    xs = [[randn(L, DIM) for _ in range(n_layers)] for _ in range(2)]  # two input sets (each > L2)
+    # the segment's 3D RoPE table (rope.rs:115-150 layout: one angle per pair)
+    pos = torch.arange(L, device=dev, dtype=torch.float32)[:, None]
+    freq = torch.pow(torch.tensor(256.0, device=dev), -torch.arange(0, HEAD_DIM, 2, device=dev) / HEAD_DIM)
+    ang = pos * freq[None, :]
+    rope = (torch.cos(ang).contiguous(), torch.sin(ang).contiguous())
+    k_out = [torch.empty((1, L, HEADS, HEAD_DIM), dtype=torch.bfloat16, device=dev) for _ in range(n_layers)]
+    v_out = [torch.empty_like(t) for t in k_out]
+    recent_k = [torch.empty_like(t) for t in k_out]
+    recent_v = [torch.empty_like(t) for t in k_out]
+    weights = [dict(wk=wk[i], wv=wv[i], bk=bk[i], bv=bv[i], k_gain=gain[i]) for i in range(n_layers)]
+    seg = 0
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(n_layers)]
+    proj_ms = [0.0, 0]
+
+    def fused(xset, time_launches=False):
+        nonlocal seg
+        staged = bank.stage_segment(desc(seg))
+        for i in range(n_layers):
+            if time_launches:
+                ev[i][0].record(stream)
+            nk.kv_project(xs[xset][i], wk[i], wv[i], bk=bk[i], bv=bv[i], k_gain=gain[i], qk_norm=True, eps=1e-6,
+                          rope=rope, k_out=k_out[i].view(L, DIM), v_out=v_out[i].view(L, DIM), codes=staged[i],
+                          ranges=[(0, L, 0)], status_ptr=staged[i]["status"], stream=stream)
+            if time_launches:
+                ev[i][1].record(stream)
+        bank.commit_staged()
+        bank.decode_segment(seg, recent_k, recent_v)
+        seg += 1
+        if time_launches:
+            torch.cuda.synchronize()
+            proj_ms[0] += sum(e[0].elapsed_time(e[1]) for e in ev)
+            proj_ms[1] += n_layers
+
+    def unfused(xset):
+        nonlocal seg
+        for i in range(n_layers):
+            kv = torch.matmul(xs[xset][i], wkv[i].T)  # cuBLAS, bf16 out
+            k = (kv[:, :DIM] + bk[i]).view(L, HEADS, HEAD_DIM).float()
+            v = kv[:, DIM:] + bv[i]
+            k = (k * torch.rsqrt((k * k).mean(-1, keepdim=True) + 1e-6) * gain[i].float()).to(torch.bfloat16).float()
+            kr, ki = k[..., 0::2], k[..., 1::2]
+            c, sn = rope[0][:, None, :], rope[1][:, None, :]
+            k = torch.stack([kr * c - ki * sn, ki * c + kr * sn], -1)
+            k_out[i].view(L, HEADS, HEAD_DIM).copy_(k.view(L, HEADS, HEAD_DIM))
+            v_out[i].view(L, DIM).copy_(v)
+        bank.commit_tensors(desc(seg), k_out, v_out)
+        bank.decode_segment(seg, recent_k, recent_v)
+        seg += 1
+
+    # prefill: the archive through the plain commit of synthetic K / V
+    gen = synth.DeviceGen(dev, seed=0, key_sigma=1.0)
+    for i in range(n_layers):
+        gen.fill(k_out[i], begin + i, 0, 0, nk.NKV_BF16)
+        gen.fill(v_out[i], begin + i, 0, 1, nk.NKV_BF16)
+    for _ in range(prefill):
+        bank.commit_tensors(desc(seg), k_out, v_out)
+        seg += 1
+
+    def timed(fn, steps):
+        for _ in range(args.warmup):
+            fn(seg % 2)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(steps):
+            fn(seg % 2)
+        b.record(stream)
+        torch.cuda.synchronize()
+        t = torch.tensor([a.elapsed_time(b)], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    clocks = ClockSampler(local)
+    clocks.start()
+    ms_fused = timed(fused, args.steps)
+    clk = clocks.stop()
+    # per-launch device time of the producer kernel (separate, event-bracketed turns)
+    for _ in range(2):
+        fused(seg % 2, time_launches=True)
+    launch_ms = proj_ms[0] / proj_ms[1]
+    ms_unfused = timed(unfused, args.steps)
+    # cuBLAS alone on the same GEMM (x [L, 3072] x [3072, 6144])
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for i in range(n_layers):
+        torch.matmul(xs[0][i], wkv[i].T)
+    a.record(stream)
+    reps = 3
+    for r in range(reps):
+        for i in range(n_layers):
+            torch.matmul(xs[r % 2][i], wkv[i].T)
+    b.record(stream)
+    torch.cuda.synchronize()
+    cublas_ms = a.elapsed_time(b) / (reps * n_layers)
+
+    # e2e: the attention inputs come from pinned host memory every turn
+    host_x = [[t.cpu().pin_memory() for t in xs[s]] for s in range(2)]
+    torch.cuda.synchronize()
+    ea, eb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ea.record(stream)
+    for st in range(e2e_steps):
+        for i in range(n_layers):
+            xs[st % 2][i].copy_(host_x[st % 2][i], non_blocking=True)
+        fused(st % 2)  # returns after reading the layers' non-finite flags back
+    eb.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = torch.tensor([ea.elapsed_time(eb)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+    e2e_ms = float(e2e_ms.item())
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        try:
+            cpu = cpu_sample_project(min(os.cpu_count() or 1, 8))
+        except Exception as e:  # noqa: BLE001
+            cpu = {"value": None, "unit": "segment tokens/s (all layers)", "cores": 0, "kind": "port",
+                   "sample": f"failed: {e}"}
+    peaks = load_peaks()
+    tflops = PROJECT_FLOPS / (launch_ms / 1e3) / 1e12
+    cublas_tflops = PROJECT_FLOPS / (cublas_ms / 1e3) / 1e12
+    value = SEG_TOKENS * args.steps / (ms_fused / 1e3)
+    if rank == 0:
+        out = {
+            "metric": METRIC_PROJECT, "value": round(value, 1), "unit": "segment tokens/s (all layers)",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms_fused / args.steps, 4), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "nomas-8B commit with its producer: per layer the K / V projection of a "
+                                   "6,496-token segment (Lin + bias, RmsNorm + RoPE on K) with INT8 archive rows "
+                                   "in the epilogue, staged commit, uniform rebuild (16 past frames), newest "
+                                   "segment", "layers": args.layers, "heads": HEADS, "head_dim": HEAD_DIM,
+                       "model_dim": DIM, "segment_tokens": SEG_TOKENS, "parallelism": f"layer-sharded x{world}",
+                       "l2": "attention inputs 1.9 GB per step > 126 MB L2"},
+            "unfused": {"ms_per_step": round(ms_unfused / args.steps, 4),
+                        "what": "cuBLAS projection (torch.matmul) + eager bias / RmsNorm / RoPE + commit_tensors",
+                        "speedup_fused": round(ms_unfused / ms_fused, 3)},
+            "roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": peaks["bf16_tflops"],
+                         "unit": "TFLOP/s", "frac": round(tflops / peaks["bf16_tflops"], 4), "traffic": None,
+                         "kernel": "k_kv_project (one launch per layer)", "flops_per_launch": PROJECT_FLOPS,
+                         "launch_ms": round(launch_ms, 4), "peak_src": peaks["src"] + " (burst cuBLAS bf16)",
+                         "cublas_same_gemm_ms": round(cublas_ms, 4), "cublas_same_gemm_tflops": round(cublas_tflops, 1)},
+            "e2e": {"value": round(SEG_TOKENS * e2e_steps / (e2e_ms / 1e3), 1), "unit": "segment tokens/s (all layers)",
+                    "h2d_bytes_per_step": SEG_TOKENS * DIM * 2 * args.layers,
+                    "d2h_bytes_per_step": 4 * (n_layers + 1) * world,
+                    "steps": e2e_steps},
+            "gpu_launches": args.steps * (n_layers + 3),
+            "clocks": clk, "cpu_baseline": cpu,
+        }
+        print(json.dumps(out), flush=True)
+    bank.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     threads = min(os.cpu_count() or 1, LAYERS)
     wl, swap = args.workload, args.swap
+    if wl == "project":
+        r = cpu_sample_project(threads)
+        out = {"impl": "reference", "metric": METRIC_PROJECT, "value": round(r["value"], 3), "unit": r["unit"],
+               "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+               "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+               "config": {"workload": "producer chain + quantize (oracle restatement)", "layers_sampled": threads},
+               "cpu_baseline": r, "e2e": {"value": round(r["value"], 3), "unit": r["unit"], "h2d_bytes_per_step": 0,
+                                          "d2h_bytes_per_step": 0}}
+        print(json.dumps(out), flush=True)
+        return
     r = cpu_sample(threads, warmup=max(0, min(args.warmup, 1)), steps=max(1, min(args.steps, 2)), workload=wl,
                    swap=swap)
     metric = METRIC_SWAP.format(wl.upper()) if swap else METRIC if wl == "int8" else METRIC_QVG
@@ -516,8 +776,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
-    ap.add_argument("--workload", default="int8", choices=["int8", "qvg"],
-                    help="int8 = the headline configuration; qvg = the QVG configuration (frozen codebooks)")
+    ap.add_argument("--workload", default="int8", choices=["int8", "qvg", "project"],
+                    help="int8 = the headline configuration; qvg = the QVG configuration (frozen codebooks); "
+                         "project = the commit with its fused K/V projection producer")
     ap.add_argument("--swap", action="store_true",
                     help="box-run configuration: phase-swapped cache, park + unpark every turn, 64-segment archive")
     ap.add_argument("--layers", type=int, default=LAYERS,
@@ -527,6 +788,8 @@ def main():
         raise SystemExit("--warmup must be >= 3")
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "project":
+        run_project(args)
     else:
         run_gpu(args)
 

@@ -125,12 +125,13 @@ def test_random_inputs(nkv, orc, M, H):
     k, v = oracle_kv(orc, a)
     assert got["status"] == 0
     # f32 accumulation on the tensor cores vs the oracle's f64: bf16 results
-    # equal or within a few bf16 units (a flipped rounding moves the RMS
-    # norm of its row a little)
+    # mostly equal; where a rounding flips, the difference is about one bf16
+    # unit of the row's O(1) values (a flipped RoPE input moves a nearly
+    # cancelling output by that much in absolute terms)
     for g, o in ((got["k"], k), (got["v"], v)):
         gf, of = orc.bf16_to_f32(g), orc.bf16_to_f32(o)
         assert np.mean(g == o) > 0.98
-        assert np.max(np.abs(gf - of) / np.maximum(np.abs(of), 1e-2)) < 2 ** -5
+        assert np.max(np.abs(gf - of) / np.maximum(np.abs(of), 1.0)) < 2 ** -5
     # the codes are the quantize of the K / V the kernel wrote: bit-exact
     kq, vq, ks, vs = oracle_codes(orc, got["k"], got["v"], H)
     assert np.array_equal(got["k_codes"], kq) and np.array_equal(got["v_codes"], vq)
