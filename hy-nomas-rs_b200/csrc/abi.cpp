@@ -292,10 +292,17 @@ int nkv_kv_project(const nkv_kv_project_args* a, void* stream) {
       if (r.lo < 0 || r.hi < r.lo || r.hi > a->tokens || r.dst < 0)
         nkv::fail(NKV_ERR_ARGUMENT, "row range " + std::to_string(i) + " outside [0, tokens)");
     }
-    const void* ptrs[] = {a->x, a->wk, a->wv, a->bk, a->bv, a->k_norm_gain, a->rope_cos, a->rope_sin, a->k_out,
-                          a->v_out, a->k_codes, a->k_scales, a->v_codes, a->v_scales, a->status};
-    for (const void* p : ptrs)
-      if (reinterpret_cast<uintptr_t>(p) & 15u) nkv::fail(NKV_ERR_ARGUMENT, "nkv_kv_project pointers must be 16-byte aligned");
+    // vector loads / stores and TMA need 16 bytes; scales and the status
+    // word are single 4-byte stores / atomics
+    const void* vec[] = {a->x, a->wk, a->wv, a->bk, a->bv, a->k_norm_gain, a->rope_cos, a->rope_sin, a->k_out,
+                         a->v_out, a->k_codes, a->v_codes};
+    for (const void* p : vec)
+      if (reinterpret_cast<uintptr_t>(p) & 15u)
+        nkv::fail(NKV_ERR_ARGUMENT, "nkv_kv_project tensor pointers must be 16-byte aligned");
+    for (const void* p : {static_cast<const void*>(a->k_scales), static_cast<const void*>(a->v_scales),
+                          static_cast<const void*>(a->status)})
+      if (reinterpret_cast<uintptr_t>(p) & 3u)
+        nkv::fail(NKV_ERR_ARGUMENT, "nkv_kv_project scales and status must be 4-byte aligned");
     nkv::KvProjectParams p{};
     p.M = a->tokens;
     p.H = a->heads;

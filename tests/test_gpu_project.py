@@ -181,7 +181,9 @@ def test_argument_checks(nkv):
     x = torch.zeros((64, 256), dtype=torch.bfloat16, device="cuda")
     w = torch.zeros((256, 256), dtype=torch.bfloat16, device="cuda")
     with pytest.raises(nkv.ArgumentError):  # misaligned status word
-        nkv.kv_project(x, w, w, status_ptr=st.data_ptr() + 4)
+        nkv.kv_project(x, w, w, status_ptr=st.data_ptr() + 2)
+    with pytest.raises(nkv.ArgumentError):  # misaligned input
+        nkv.kv_project(x.view(-1)[4:4 + 62 * 256].view(62, 256), w, w, status=st)  # 8-byte offset
 
 
 def test_8b_geometry_codes_match_commit_quantizer(nkv, orc):
