@@ -263,7 +263,7 @@ def test_staged_commit_equals_tensor_commit(nkv, orc):
             assert torch.equal(pv.view(torch.int16), fv.view(torch.int16))
             assert [s.as_tuple() for s in produced.layer(i).working_layout()] == \
                 [s.as_tuple() for s in fed.layer(i).working_layout()]
-            assert produced.layer(i).export_segment(seg) == fed.layer(i).export_segment(seg)
+            assert np.array_equal(produced.layer(i).export_segment(seg), fed.layer(i).export_segment(seg))
         assert produced.metrics().as_dict() == fed.metrics().as_dict()
 
 
