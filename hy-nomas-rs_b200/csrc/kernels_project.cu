@@ -43,13 +43,22 @@
 namespace nkv {
 namespace {
 
-constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 3;
 constexpr int A_BYTES = BM * BK * 2;  // 16 KB
 constexpr int B_BYTES = BN * BK * 2;  // 32 KB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int TMEM_COLS = 2 * BN;
 constexpr int kThreads = 192;
-constexpr int kSmemBytes = STAGES * STAGE_BYTES + 1024 /* barriers */ + 1024 /* alignment */;
+// Epilogue constants staged in shared memory ahead of each tile (cp.async,
+// overlapping the tile's main loop): each thread's own token row of the
+// rotary cos / sin tables, rows padded to 68 floats so the 32 lanes' 16-byte
+// reads of one column fall in distinct bank groups; and per epilogue warp
+// the tile's 256 bias values and the 128 gain values (bf16).
+constexpr int ROPE_PITCH = 68;
+constexpr int ROPE_BYTES = BM * ROPE_PITCH * 4;  // one table
+constexpr int WARP_CONST_BYTES = (BN + 128) * 2;
+constexpr int kSmemBytes = STAGES * STAGE_BYTES + 2 * ROPE_BYTES + 4 * WARP_CONST_BYTES + 1024 /* barriers */ +
+                           1024 /* alignment */;
 constexpr uint64_t kWaitNs = 1000000000ull;  // 1 s per wait
 
 // tcgen05 instruction descriptor: f32 accumulate (bits 4-5 = 1), A and B
@@ -119,6 +128,12 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
 // Shared-memory matrix descriptor of a K-major, 128-byte-swizzled tile whose
 // rows are 128 bytes (64 bf16): start address >> 4 in bits 0-13, leading
 // byte offset 1 (unused for swizzled K-major), stride byte offset 1024 >> 4
@@ -185,7 +200,7 @@ __device__ __forceinline__ void bf16_round2(float& a, float& b) {
 }
 
 __device__ __forceinline__ void load_bf16x8(const uint16_t* p, float* out) {
-  const uint4 w = __ldg(reinterpret_cast<const uint4*>(p));
+  const uint4 w = *reinterpret_cast<const uint4*>(p);
   const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
@@ -196,10 +211,13 @@ __device__ __forceinline__ void load_bf16x8(const uint16_t* p, float* out) {
 
 // The epilogue of one (token row, head): y holds the 128 f32 accumulator
 // values of this row and head.
+// bias: this head's 128 bias values or null; gain: the 128 RMS-norm gains
+// or null; rope_c / rope_s: this row's 64 cos / sin values or null (all in
+// shared memory).
 __device__ __forceinline__ void epilogue_head(float (&y)[128], const KvProjectParams& p, int side, int64_t row,
-                                              int head, bool& bad) {
+                                              int head, const uint16_t* bias, const uint16_t* gain,
+                                              const float* rope_c, const float* rope_s, bool& bad) {
   const int dim = p.H * 128;
-  const uint16_t* bias = side ? p.bias_v : p.bias_k;
   // Lin::fwd (modules/mod.rs:135-138): the GEMM's bf16 result, then the
   // bias added in bf16
 #pragma unroll
@@ -208,7 +226,7 @@ __device__ __forceinline__ void epilogue_head(float (&y)[128], const KvProjectPa
 #pragma unroll
     for (int d0 = 0; d0 < 128; d0 += 8) {
       float b[8];
-      load_bf16x8(bias + head * 128 + d0, b);
+      load_bf16x8(bias + d0, b);
 #pragma unroll
       for (int j = 0; j < 8; j += 2) {
         y[d0 + j] = __fadd_rn(y[d0 + j], b[j]);
@@ -227,11 +245,11 @@ __device__ __forceinline__ void epilogue_head(float (&y)[128], const KvProjectPa
     const float ss = __fadd_rn(__fadd_rn(s[0], s[1]), __fadd_rn(s[2], s[3]));
     const float var = __fmul_rn(ss, 0.0078125f);  // / 128, exact
     const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, p.eps)));
-    if (p.k_gain) {
+    if (gain) {
 #pragma unroll
       for (int d0 = 0; d0 < 128; d0 += 8) {
         float g[8];
-        load_bf16x8(p.k_gain + d0, g);
+        load_bf16x8(gain + d0, g);
 #pragma unroll
         for (int j = 0; j < 8; ++j) y[d0 + j] = __fmul_rn(__fmul_rn(y[d0 + j], inv), g[j]);
       }
@@ -242,14 +260,14 @@ __device__ __forceinline__ void epilogue_head(float (&y)[128], const KvProjectPa
 #pragma unroll
     for (int d = 0; d < 128; d += 2) bf16_round2(y[d], y[d + 1]);
   }
-  if (side == 0 && p.rope_cos) {
+  if (side == 0 && rope_c) {
     // apply_rotary (rope.rs:269-305): interleaved (re, im) pairs, products
     // and sums rounded separately in f32, then bf16
-    const float4* c4 = reinterpret_cast<const float4*>(p.rope_cos + row * 64);
-    const float4* s4 = reinterpret_cast<const float4*>(p.rope_sin + row * 64);
+    const float4* c4 = reinterpret_cast<const float4*>(rope_c);
+    const float4* s4 = reinterpret_cast<const float4*>(rope_s);
 #pragma unroll
     for (int q = 0; q < 16; ++q) {
-      const float4 c = __ldg(c4 + q), sn = __ldg(s4 + q);
+      const float4 c = c4[q], sn = s4[q];
       const float cs[4] = {c.x, c.y, c.z, c.w}, ss[4] = {sn.x, sn.y, sn.z, sn.w};
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
@@ -328,7 +346,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                  const __grid_constant__ CUtensorMap tm_wv, const KvProjectParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  float* rope_cos_s = reinterpret_cast<float*>(smem + STAGES * STAGE_BYTES);
+  float* rope_sin_s = rope_cos_s + BM * ROPE_PITCH;
+  uint16_t* warp_consts = reinterpret_cast<uint16_t*>(smem + STAGES * STAGE_BYTES + 2 * ROPE_BYTES);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES + 2 * ROPE_BYTES + 4 * WARP_CONST_BYTES);
   // bars: full[STAGES], empty[STAGES], tfull[2], tempty[2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
   volatile uint32_t* abort_flag = tmem_slot + 1;
@@ -425,12 +446,32 @@ __global__ void __launch_bounds__(kThreads, 1)
     int buf = 0;
     uint32_t acc_phase = 0;
     bool bad = false;
+    const int rit = quad * 32 + lane;  // row in the tile
+    float* my_cos = rope_cos_s + rit * ROPE_PITCH;
+    float* my_sin = rope_sin_s + rit * ROPE_PITCH;
+    uint16_t* wc = warp_consts + (warp - 2) * (WARP_CONST_BYTES / 2);  // [bias 256][gain 128]
     for (int t = blockIdx.x; t < n_tiles; t += gridDim.x) {
-      if (!mbar_wait(tfull_bar(buf), acc_phase, abort_flag, p.err)) break;
-      tc_fence_after();
       const int tm = t % tiles_m, tn = t / tiles_m;
       const int side = tn / n_half, head0 = (tn % n_half) * (BN / 128);
-      const int64_t row = int64_t(tm) * BM + quad * 32 + lane;
+      const int64_t row = int64_t(tm) * BM + rit;
+      // stage this tile's constants while its main loop runs
+      const uint16_t* bias_g = side ? p.bias_v : p.bias_k;
+      const bool rope = side == 0 && p.rope_cos != nullptr;
+      const bool gain = side == 0 && p.qk_norm && p.k_gain != nullptr;
+      if (bias_g) cp_async16(wc + lane * 8, bias_g + head0 * 128 + lane * 8);
+      if (gain && lane < 16) cp_async16(wc + BN + lane * 8, p.k_gain + lane * 8);
+      if (rope && row < p.M) {
+#pragma unroll
+        for (int q = 0; q < 16; ++q) {
+          cp_async16(my_cos + 4 * q, p.rope_cos + row * 64 + 4 * q);
+          cp_async16(my_sin + 4 * q, p.rope_sin + row * 64 + 4 * q);
+        }
+      }
+      cp_async_commit();
+      if (!mbar_wait(tfull_bar(buf), acc_phase, abort_flag, p.err)) break;
+      tc_fence_after();
+      cp_async_wait_all();
+      __syncwarp();
       const uint32_t taddr = tmem_base + (uint32_t(quad * 32) << 16) + uint32_t(buf * BN);
 #pragma unroll 1
       for (int hh = 0; hh < BN / 128; ++hh) {
@@ -445,8 +486,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(tempty_bar(buf));
         }
-        if (row < p.M) epilogue_head(y, p, side, row, head0 + hh, bad);
+        if (row < p.M)
+          epilogue_head(y, p, side, row, head0 + hh, bias_g ? wc + hh * 128 : nullptr, gain ? wc + BN : nullptr,
+                        rope ? my_cos : nullptr, my_sin, bad);
       }
+      __syncwarp();  // every lane is done with the warp's constants
       if (__any_sync(0xFFFFFFFFu, bad)) {
         if (lane == 0) atomicOr(p.flag, 1u << side);
         bad = false;
@@ -455,6 +499,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
+  cp_async_wait_all();  // an aborted epilogue may have copies in flight
   __syncwarp();
   tc_fence_before();
   __syncthreads();
