@@ -139,15 +139,6 @@ __global__ void __launch_bounds__(256) k_int8_quantize(const QuantJob* __restric
 //    every value of the row (x <= peak, s = peak * (1 + O(2^-23)) / 127), so
 //    the reference's clamp to [-127, 127] never binds.
 // ---------------------------------------------------------------------------
-// Lane-wise max(|a|, |b|) of two bf16 pairs (the sign bit is the XOR of the
-// operands' and is masked off by the caller); a NaN lane yields a NaN, so
-// one instruction per pair serves both the peak and the non-finite scan.
-__device__ __forceinline__ uint32_t maxabs_bf16x2(uint32_t a, uint32_t b) {
-  uint32_t d;
-  asm("max.NaN.xorsign.abs.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-  return d;
-}
-
 template <int G, int R, int V>
 __global__ void __launch_bounds__(256) k_int8_quantize_bf16(const QuantJob* __restrict__ jobs, uint64_t rows,
                                                             uint64_t in_row_offset, uint32_t* __restrict__ flag) {

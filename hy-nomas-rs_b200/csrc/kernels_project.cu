@@ -13,7 +13,7 @@
 // reads them, attention.rs:145-147), but the commit no longer reads them
 // back: the codes and scales come out of the same epilogue.
 //
-// Kernel shape (one persistent CTA per SM, 192 threads):
+// Kernel shape (one persistent CTA per SM, 320 threads):
 //  * warp 0, one thread: TMA producer.  A 128-token x 64 slice of x and a
 //    256-row x 64 slice of W_k or W_v per stage, 128-byte swizzled, into a
 //    4-stage shared-memory ring (48 KB per stage);
@@ -21,11 +21,12 @@
 //    one thread issues tcgen05.mma kind::f16 (bf16 x bf16 -> f32,
 //    M=128 N=256 K=16), frees each stage with tcgen05.commit and hands a
 //    finished accumulator to the epilogue with a second commit;
-//  * warps 2-5: the epilogue.  Warp w reads TMEM lanes 32*(w%4)..+31, so
-//    thread l owns token row 32*(w%4)+l of the tile, and each of the tile's
-//    two heads is 128 values in that thread's registers: bias, RMS norm,
-//    rotary pairs, |x| max and codes need no cross-thread exchange.  While
-//    it runs, the MMA warp fills the other accumulator with the next tile.
+//  * warps 2-9: the epilogue.  Warp w reads TMEM lanes 32*(w%4)..+31 of
+//    head (w-2)/4's 128 columns, so thread l owns token row 32*(w%4)+l of
+//    the tile for one head, 128 values in its registers: bias, RMS norm,
+//    rotary pairs, |x| max and codes need no cross-thread exchange.  Two
+//    epilogue warps per SM sub-partition hide each other's latency; while
+//    they run, the MMA warp fills the other accumulator with the next tile.
 //
 // Every wait is bounded (kWaitNs on %globaltimer); a wait that runs out sets
 // kProjectTimeoutBit in the status word and the CTA's abort flag, every role
@@ -48,17 +49,19 @@ constexpr int A_BYTES = BM * BK * 2;  // 16 KB
 constexpr int B_BYTES = BN * BK * 2;  // 32 KB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int TMEM_COLS = 2 * BN;
-constexpr int kThreads = 192;
+constexpr int kEpiWarps = 8;  // two per SM sub-partition: warps 2-5 head 0, 6-9 head 1 of a tile
+constexpr int kThreads = 32 * (2 + kEpiWarps);
 // Epilogue constants staged in shared memory ahead of each tile (cp.async,
-// overlapping the tile's main loop): each thread's own token row of the
-// rotary cos / sin tables, rows padded to 68 floats so the 32 lanes' 16-byte
-// reads of one column fall in distinct bank groups; and per epilogue warp
-// the tile's 256 bias values and the 128 gain values (bf16).
+// overlapping the tile's main loop): the tile's 128 token rows of the rotary
+// cos / sin tables (the head-0 warp of a lane quadrant copies cos, the head-1
+// warp sin, for the quadrant's 32 rows), rows padded to 68 floats so the 32
+// lanes' 16-byte reads of one column fall in distinct bank groups; and per
+// epilogue warp its head's 128 bias values and the 128 gain values (bf16).
 constexpr int ROPE_PITCH = 68;
 constexpr int ROPE_BYTES = BM * ROPE_PITCH * 4;  // one table
-constexpr int WARP_CONST_BYTES = (BN + 128) * 2;
-constexpr int kSmemBytes = STAGES * STAGE_BYTES + 2 * ROPE_BYTES + 4 * WARP_CONST_BYTES + 1024 /* barriers */ +
-                           1024 /* alignment */;
+constexpr int WARP_CONST_BYTES = (128 + 128) * 2;
+constexpr int kSmemBytes = STAGES * STAGE_BYTES + 2 * ROPE_BYTES + kEpiWarps * WARP_CONST_BYTES +
+                           1024 /* barriers */ + 1024 /* alignment */;
 constexpr uint64_t kWaitNs = 1000000000ull;  // 1 s per wait
 
 // tcgen05 instruction descriptor: f32 accumulate (bits 4-5 = 1), A and B
@@ -189,49 +192,35 @@ __device__ __forceinline__ void tmem_wait32(float* v) {
                : "memory");
 }
 
-// f32 -> bf16 (round to nearest even) -> f32, two values at a time.  The
-// hardware conversion is the integer RNE for every non-NaN input; a NaN
-// stays a NaN (its payload is not the reference's, which only matters for
-// rows the non-finite check rejects).
-__device__ __forceinline__ void bf16_round2(float& a, float& b) {
-  const uint32_t w = dev::bf16x2_bits_nonnan(a, b);
-  a = __uint_as_float(w << 16);
-  b = __uint_as_float(w & 0xFFFF0000u);
-}
+// Values travel through the epilogue as packed bf16 pairs (element 2j in the
+// low half of word j): every stage of the chain ends in a bf16 rounding, a
+// rotary (re, im) pair is exactly one word, and 128 values take 64 registers.
+// The hardware pair conversion is the integer round-to-nearest-even for
+// every non-NaN input; a NaN stays a NaN (its payload is not the
+// reference's, which only matters for rows the non-finite check rejects).
+__device__ __forceinline__ float lo_f(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float hi_f(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+__device__ __forceinline__ uint32_t pack_rn(float lo, float hi) { return dev::bf16x2_bits_nonnan(lo, hi); }
 
-__device__ __forceinline__ void load_bf16x8(const uint16_t* p, float* out) {
-  const uint4 w = *reinterpret_cast<const uint4*>(p);
-  const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    out[2 * i] = __uint_as_float(ws[i] << 16);
-    out[2 * i + 1] = __uint_as_float(ws[i] & 0xFFFF0000u);
-  }
-}
-
-// The epilogue of one (token row, head): y holds the 128 f32 accumulator
-// values of this row and head.
-// bias: this head's 128 bias values or null; gain: the 128 RMS-norm gains
-// or null; rope_c / rope_s: this row's 64 cos / sin values or null (all in
-// shared memory).
-__device__ __forceinline__ void epilogue_head(float (&y)[128], const KvProjectParams& p, int side, int64_t row,
+// The epilogue of one (token row, head): w holds bf16(accumulator) of the
+// row's 128 values.  bias: this head's 128 bias values or null; gain: the
+// 128 RMS-norm gains or null; rope_c / rope_s: this row's 64 cos / sin
+// values or null (all in shared memory).
+__device__ __forceinline__ void epilogue_head(uint32_t (&w)[64], const KvProjectParams& p, int side, int64_t row,
                                               int head, const uint16_t* bias, const uint16_t* gain,
                                               const float* rope_c, const float* rope_s, bool& bad) {
   const int dim = p.H * 128;
-  // Lin::fwd (modules/mod.rs:135-138): the GEMM's bf16 result, then the
-  // bias added in bf16
-#pragma unroll
-  for (int d = 0; d < 128; d += 2) bf16_round2(y[d], y[d + 1]);
+  // Lin::fwd (modules/mod.rs:135-138): the GEMM's bf16 result plus the bias,
+  // added in bf16
   if (bias) {
 #pragma unroll
-    for (int d0 = 0; d0 < 128; d0 += 8) {
-      float b[8];
-      load_bf16x8(bias + d0, b);
+    for (int q = 0; q < 16; ++q) {
+      const uint4 bw = *reinterpret_cast<const uint4*>(bias + 8 * q);
+      const uint32_t bs[4] = {bw.x, bw.y, bw.z, bw.w};
 #pragma unroll
-      for (int j = 0; j < 8; j += 2) {
-        y[d0 + j] = __fadd_rn(y[d0 + j], b[j]);
-        y[d0 + j + 1] = __fadd_rn(y[d0 + j + 1], b[j + 1]);
-        bf16_round2(y[d0 + j], y[d0 + j + 1]);
+      for (int j = 0; j < 4; ++j) {
+        uint32_t& x = w[4 * q + j];
+        x = pack_rn(__fadd_rn(lo_f(x), lo_f(bs[j])), __fadd_rn(hi_f(x), hi_f(bs[j])));
       }
     }
   }
@@ -241,24 +230,30 @@ __device__ __forceinline__ void epilogue_head(float (&y)[128], const KvProjectPa
     // 1/sqrt(var + eps) as an IEEE square root and division
     float s[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-    for (int d = 0; d < 128; ++d) s[d & 3] = __fadd_rn(s[d & 3], __fmul_rn(y[d], y[d]));
+    for (int j = 0; j < 64; ++j) {
+      const float a = lo_f(w[j]), b = hi_f(w[j]);
+      s[(2 * j) & 3] = __fadd_rn(s[(2 * j) & 3], __fmul_rn(a, a));
+      s[(2 * j + 1) & 3] = __fadd_rn(s[(2 * j + 1) & 3], __fmul_rn(b, b));
+    }
     const float ss = __fadd_rn(__fadd_rn(s[0], s[1]), __fadd_rn(s[2], s[3]));
     const float var = __fmul_rn(ss, 0.0078125f);  // / 128, exact
     const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, p.eps)));
     if (gain) {
 #pragma unroll
-      for (int d0 = 0; d0 < 128; d0 += 8) {
-        float g[8];
-        load_bf16x8(gain + d0, g);
+      for (int q = 0; q < 16; ++q) {
+        const uint4 gw = *reinterpret_cast<const uint4*>(gain + 8 * q);
+        const uint32_t gs[4] = {gw.x, gw.y, gw.z, gw.w};
 #pragma unroll
-        for (int j = 0; j < 8; ++j) y[d0 + j] = __fmul_rn(__fmul_rn(y[d0 + j], inv), g[j]);
+        for (int j = 0; j < 4; ++j) {
+          uint32_t& x = w[4 * q + j];
+          x = pack_rn(__fmul_rn(__fmul_rn(lo_f(x), inv), lo_f(gs[j])),
+                      __fmul_rn(__fmul_rn(hi_f(x), inv), hi_f(gs[j])));
+        }
       }
     } else {
 #pragma unroll
-      for (int d = 0; d < 128; ++d) y[d] = __fmul_rn(y[d], inv);
+      for (int j = 0; j < 64; ++j) w[j] = pack_rn(__fmul_rn(lo_f(w[j]), inv), __fmul_rn(hi_f(w[j]), inv));
     }
-#pragma unroll
-    for (int d = 0; d < 128; d += 2) bf16_round2(y[d], y[d + 1]);
   }
   if (side == 0 && rope_c) {
     // apply_rotary (rope.rs:269-305): interleaved (re, im) pairs, products
@@ -271,13 +266,10 @@ __device__ __forceinline__ void epilogue_head(float (&y)[128], const KvProjectPa
       const float cs[4] = {c.x, c.y, c.z, c.w}, ss[4] = {sn.x, sn.y, sn.z, sn.w};
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const int d = 8 * q + 2 * j;
-        const float xr = y[d], xi = y[d + 1];
-        float o_r = __fsub_rn(__fmul_rn(xr, cs[j]), __fmul_rn(xi, ss[j]));
-        float o_i = __fadd_rn(__fmul_rn(xi, cs[j]), __fmul_rn(xr, ss[j]));
-        bf16_round2(o_r, o_i);
-        y[d] = o_r;
-        y[d + 1] = o_i;
+        uint32_t& x = w[4 * q + j];
+        const float xr = lo_f(x), xi = hi_f(x);
+        x = pack_rn(__fsub_rn(__fmul_rn(xr, cs[j]), __fmul_rn(xi, ss[j])),
+                    __fadd_rn(__fmul_rn(xi, cs[j]), __fmul_rn(xr, ss[j])));
       }
     }
   }
@@ -286,13 +278,7 @@ __device__ __forceinline__ void epilogue_head(float (&y)[128], const KvProjectPa
   if (out) {
     uint4* o = reinterpret_cast<uint4*>(out + row * dim + head * 128);
 #pragma unroll
-    for (int q = 0; q < 16; ++q) {
-      uint32_t w[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j)
-        w[j] = (__float_as_uint(y[8 * q + 2 * j]) >> 16) | (__float_as_uint(y[8 * q + 2 * j + 1]) & 0xFFFF0000u);
-      o[q] = make_uint4(w[0], w[1], w[2], w[3]);
-    }
+    for (int q = 0; q < 16; ++q) o[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
   }
   // the archive rows: quantize_one (int8.rs:65-81) of committed rows only
   uint8_t* codes = side ? p.v_codes : p.k_codes;
@@ -302,40 +288,43 @@ __device__ __forceinline__ void epilogue_head(float (&y)[128], const KvProjectPa
   for (int i = 0; i < 2; ++i)
     if (i < p.n_ranges && row >= p.range_lo[i] && row < p.range_hi[i]) dst = row - p.range_lo[i] + p.range_dst[i];
   if (dst < 0) return;
-  float peak = 0.0f;
+  // |x| max on the bf16 patterns: NaN-propagating, and inf / NaN patterns
+  // (>= 0x7F80) sort above every finite one, so the same max answers the
+  // non-finite scan (x != x || |x| >= f32::MAX, int8.rs:99-117; no finite
+  // bf16 reaches f32::MAX)
+  uint32_t m = w[0] & 0x7FFF7FFFu;
 #pragma unroll
-  for (int d = 0; d < 128; ++d) {
-    const float a = fabsf(y[d]);
-    bad |= !(a < FLT_MAX);  // x != x || |x| >= f32::MAX (int8.rs:99-117)
-    peak = fmaxf(peak, a);
-  }
+  for (int j = 1; j < 64; ++j) m = maxabs_bf16x2(m, w[j]) & 0x7FFF7FFFu;
+  const uint32_t pk = max(m & 0xFFFFu, m >> 16);
+  bad |= pk >= 0x7F80u;
+  const float peak = __uint_as_float(pk << 16);
   const float inv127 = (float)(1.0 / 127.0);
   const float s = peak > 0.0f ? __fadd_rn(__fmul_rn(peak, inv127), 0.0f) : 1.0f;
-  uint4* q = reinterpret_cast<uint4*>(codes + dst * dim + head * 128);
+  uint4* qo = reinterpret_cast<uint4*>(codes + dst * dim + head * 128);
   if (s >= FLT_MIN && s <= 1e37f) {
     const float r = __frcp_rn(s);
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
-      uint32_t w[4];
+      uint32_t c[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const int d = 16 * k + 4 * j;
-        w[j] = pack4(code_bits(y[d], s, r), code_bits(y[d + 1], s, r), code_bits(y[d + 2], s, r),
-                     code_bits(y[d + 3], s, r));
+        const uint32_t a = w[8 * k + 2 * j], b = w[8 * k + 2 * j + 1];
+        c[j] = pack4(code_bits(lo_f(a), s, r), code_bits(hi_f(a), s, r), code_bits(lo_f(b), s, r),
+                     code_bits(hi_f(b), s, r));
       }
-      q[k] = make_uint4(w[0], w[1], w[2], w[3]);
+      qo[k] = make_uint4(c[0], c[1], c[2], c[3]);
     }
   } else {
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
-      uint32_t w[4];
+      uint32_t c[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const int d = 16 * k + 4 * j;
-        w[j] = quant_exact(y[d], s) | (quant_exact(y[d + 1], s) << 8) | (quant_exact(y[d + 2], s) << 16) |
-               (quant_exact(y[d + 3], s) << 24);
+        const uint32_t a = w[8 * k + 2 * j], b = w[8 * k + 2 * j + 1];
+        c[j] = quant_exact(lo_f(a), s) | (quant_exact(hi_f(a), s) << 8) | (quant_exact(lo_f(b), s) << 16) |
+               (quant_exact(hi_f(b), s) << 24);
       }
-      q[k] = make_uint4(w[0], w[1], w[2], w[3]);
+      qo[k] = make_uint4(c[0], c[1], c[2], c[3]);
     }
   }
   (side ? p.v_scales : p.k_scales)[dst * p.H + head] = s;
@@ -349,7 +338,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   float* rope_cos_s = reinterpret_cast<float*>(smem + STAGES * STAGE_BYTES);
   float* rope_sin_s = rope_cos_s + BM * ROPE_PITCH;
   uint16_t* warp_consts = reinterpret_cast<uint16_t*>(smem + STAGES * STAGE_BYTES + 2 * ROPE_BYTES);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES + 2 * ROPE_BYTES + 4 * WARP_CONST_BYTES);
+  uint64_t* bars =
+      reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES + 2 * ROPE_BYTES + kEpiWarps * WARP_CONST_BYTES);
   // bars: full[STAGES], empty[STAGES], tfull[2], tempty[2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
   volatile uint32_t* abort_flag = tmem_slot + 1;
@@ -374,7 +364,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(tfull_bar(b), 1);
-      mbar_init(tempty_bar(b), 4);  // one arrival per epilogue warp
+      mbar_init(tempty_bar(b), kEpiWarps);  // one arrival per epilogue warp
     }
     *abort_flag = 0u;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -442,59 +432,62 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ---------------------------------------------------- epilogue
-    const int quad = warp & 3;
+    const int quad = warp & 3, hh = (warp - 2) >> 2;  // lane quadrant, head of the tile
+    const int rit = quad * 32 + lane;                 // row in the tile
+    const float* my_cos = rope_cos_s + rit * ROPE_PITCH;
+    const float* my_sin = rope_sin_s + rit * ROPE_PITCH;
+    float* my_table = (hh == 0 ? rope_cos_s : rope_sin_s) + rit * ROPE_PITCH;
+    uint16_t* wc = warp_consts + (warp - 2) * (WARP_CONST_BYTES / 2);  // [bias 128][gain 128]
+    const uint32_t pair_bar = 1 + quad;  // named barrier of the two warps of a quadrant
     int buf = 0;
     uint32_t acc_phase = 0;
     bool bad = false;
-    const int rit = quad * 32 + lane;  // row in the tile
-    float* my_cos = rope_cos_s + rit * ROPE_PITCH;
-    float* my_sin = rope_sin_s + rit * ROPE_PITCH;
-    uint16_t* wc = warp_consts + (warp - 2) * (WARP_CONST_BYTES / 2);  // [bias 256][gain 128]
     for (int t = blockIdx.x; t < n_tiles; t += gridDim.x) {
       const int tm = t % tiles_m, tn = t / tiles_m;
-      const int side = tn / n_half, head0 = (tn % n_half) * (BN / 128);
+      const int side = tn / n_half, head = (tn % n_half) * (BN / 128) + hh;
       const int64_t row = int64_t(tm) * BM + rit;
       // stage this tile's constants while its main loop runs
       const uint16_t* bias_g = side ? p.bias_v : p.bias_k;
       const bool rope = side == 0 && p.rope_cos != nullptr;
       const bool gain = side == 0 && p.qk_norm && p.k_gain != nullptr;
-      if (bias_g) cp_async16(wc + lane * 8, bias_g + head0 * 128 + lane * 8);
-      if (gain && lane < 16) cp_async16(wc + BN + lane * 8, p.k_gain + lane * 8);
+      if (bias_g && lane < 16) cp_async16(wc + lane * 8, bias_g + head * 128 + lane * 8);
+      if (gain && lane >= 16) cp_async16(wc + 128 + (lane - 16) * 8, p.k_gain + (lane - 16) * 8);
       if (rope && row < p.M) {
+        const float* src = (hh == 0 ? p.rope_cos : p.rope_sin) + row * 64;
 #pragma unroll
-        for (int q = 0; q < 16; ++q) {
-          cp_async16(my_cos + 4 * q, p.rope_cos + row * 64 + 4 * q);
-          cp_async16(my_sin + 4 * q, p.rope_sin + row * 64 + 4 * q);
-        }
+        for (int q = 0; q < 16; ++q) cp_async16(my_table + 4 * q, src + 4 * q);
       }
       cp_async_commit();
-      if (!mbar_wait(tfull_bar(buf), acc_phase, abort_flag, p.err)) break;
-      tc_fence_after();
+      const bool ok = mbar_wait(tfull_bar(buf), acc_phase, abort_flag, p.err);
       cp_async_wait_all();
-      __syncwarp();
-      const uint32_t taddr = tmem_base + (uint32_t(quad * 32) << 16) + uint32_t(buf * BN);
-#pragma unroll 1
-      for (int hh = 0; hh < BN / 128; ++hh) {
-        float y[128];
+      // both tables of the quadrant's rows are in place (a barrier even on
+      // abort, so the partner warp is never left waiting)
+      asm volatile("bar.sync %0, 64;" ::"r"(pair_bar) : "memory");
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + (uint32_t(quad * 32) << 16) + uint32_t(buf * BN + hh * 128);
+      uint32_t w[64];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) tmem_ld32(taddr + uint32_t(hh * 128 + c * 32), y + c * 32);
+      for (int c = 0; c < 4; ++c) {
+        float acc[32];
+        tmem_ld32(taddr + uint32_t(c * 32), acc);
+        tmem_wait32(acc);
 #pragma unroll
-        for (int c = 0; c < 4; ++c) tmem_wait32(y + c * 32);
-        if (hh == BN / 128 - 1) {
-          // the accumulator is in registers: hand it back to the MMA warp
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(tempty_bar(buf));
-        }
-        if (row < p.M)
-          epilogue_head(y, p, side, row, head0 + hh, bias_g ? wc + hh * 128 : nullptr, gain ? wc + BN : nullptr,
-                        rope ? my_cos : nullptr, my_sin, bad);
+        for (int j = 0; j < 16; ++j) w[c * 16 + j] = pack_rn(acc[2 * j], acc[2 * j + 1]);
       }
-      __syncwarp();  // every lane is done with the warp's constants
+      // the accumulator is in registers: hand it back to the MMA warp
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tempty_bar(buf));
+      if (row < p.M)
+        epilogue_head(w, p, side, row, head, bias_g ? wc : nullptr, gain ? wc + 128 : nullptr,
+                      rope ? my_cos : nullptr, my_sin, bad);
       if (__any_sync(0xFFFFFFFFu, bad)) {
         if (lane == 0) atomicOr(p.flag, 1u << side);
         bad = false;
       }
+      // the quadrant's rotary rows and the warp's constants are free again
+      asm volatile("bar.sync %0, 64;" ::"r"(pair_bar) : "memory");
       if (++buf == 2) buf = 0, acc_phase ^= 1u;
     }
   }

@@ -39,4 +39,13 @@ __device__ __forceinline__ uint32_t pack4(uint32_t a, uint32_t b, uint32_t c, ui
   return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410) ^ 0x80808080u;
 }
 
+// Lane-wise max(|a|, |b|) of two bf16 pairs (the sign bit is the XOR of the
+// operands' and is masked off by the caller); a NaN lane yields a NaN, so
+// one instruction per pair serves both the peak and the non-finite scan.
+__device__ __forceinline__ uint32_t maxabs_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("max.NaN.xorsign.abs.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
 }  // namespace nkv
