@@ -13,14 +13,20 @@
 // reads them, attention.rs:145-147), but the commit no longer reads them
 // back: the codes and scales come out of the same epilogue.
 //
-// Kernel shape (one persistent CTA per SM, 320 threads):
-//  * warp 0, one thread: TMA producer.  A 128-token x 64 slice of x and a
-//    256-row x 64 slice of W_k or W_v per stage, 128-byte swizzled, into a
-//    4-stage shared-memory ring (48 KB per stage);
-//  * warp 1: allocates 512 TMEM columns (two 128 x 256 f32 accumulators);
-//    one thread issues tcgen05.mma kind::f16 (bf16 x bf16 -> f32,
-//    M=128 N=256 K=16), frees each stage with tcgen05.commit and hands a
-//    finished accumulator to the epilogue with a second commit;
+// Kernel shape: persistent CTA pairs (clusters of 2, one CTA per SM, 320
+// threads each) computing 256-token x 256-column tiles with the two-SM form
+// of the tensor-core MMA (tcgen05.mma.cta_group::2, M=256 N=256 K=16): CTA r
+// of a pair holds token rows 128r..128r+127 of A and rows 128r..128r+127 of
+// the tile's 256 weight rows, so each SM streams a third less operand data
+// from L2 than a 128 x 256 single-SM tile would;
+//  * warp 0, one thread per CTA: TMA producer.  Its CTA's 128 x 64 slices of
+//    x and of W_k or W_v per stage, 128-byte swizzled, into a 4-stage ring
+//    (32 KB per stage); the loads complete on the pair leader's barrier
+//    (plain loads, no multicast);
+//  * warp 1: allocates 512 TMEM columns per CTA (two 128 x 256 f32
+//    accumulators, the CTA's half of a tile); in the leader, one thread
+//    issues the MMAs, frees each stage of both CTAs with tcgen05.commit and
+//    hands a finished accumulator to both CTAs' epilogues;
 //  * warps 2-9: the epilogue.  Warp w reads TMEM lanes 32*(w%4)..+31 of
 //    head (w-2)/4's 128 columns, so thread l owns token row 32*(w%4)+l of
 //    the tile for one head, 128 values in its registers: bias, RMS norm,
@@ -44,9 +50,11 @@
 namespace nkv {
 namespace {
 
-constexpr int BM = 128, BN = 256, BK = 64, STAGES = 3;
-constexpr int A_BYTES = BM * BK * 2;  // 16 KB
-constexpr int B_BYTES = BN * BK * 2;  // 32 KB
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int PAIR_M = 2 * BM;          // tokens per pair tile
+constexpr int B_ROWS = BN / 2;          // weight rows each CTA of a pair loads
+constexpr int A_BYTES = BM * BK * 2;      // 16 KB
+constexpr int B_BYTES = B_ROWS * BK * 2;  // 16 KB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int TMEM_COLS = 2 * BN;
 constexpr int kEpiWarps = 8;  // two per SM sub-partition: warps 2-5 head 0, 6-9 head 1 of a tile
@@ -66,8 +74,9 @@ constexpr uint64_t kWaitNs = 1000000000ull;  // 1 s per wait
 
 // tcgen05 instruction descriptor: f32 accumulate (bits 4-5 = 1), A and B
 // bf16 (bits 7-9, 10-12 = 1), both K-major (bits 15, 16 = 0), N >> 3 at
-// bit 17, M >> 4 at bit 24.
-constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(BN >> 3) << 17) | (uint32_t(BM >> 4) << 24);
+// bit 17, M >> 4 at bit 24 (M = 256: the CTA pair's rows).
+constexpr uint32_t kIdesc =
+    (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(BN >> 3) << 17) | (uint32_t(PAIR_M >> 4) << 24);
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -87,8 +96,26 @@ __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
 }
 
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+// Arrive on a barrier given by its shared::cluster address (own or peer CTA).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+// The shared::cluster address of the same shared variable in CTA `rank`.
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
 __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
@@ -121,12 +148,14 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
   }
 }
 
-// 2-D tiled TMA load (no multicast) completing on `bar`.
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int32_t x, int32_t y,
-                                            uint32_t bar) {
+// 2-D tiled TMA load (no multicast) into this CTA's shared memory,
+// completing on `bar`, a shared::cluster barrier address of the CTA pair
+// (the leader's full barrier).
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, int32_t x, int32_t y,
+                                                 uint32_t bar) {
   asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
-          "r"(dst),
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
       : "memory");
 }
@@ -149,16 +178,20 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
          (uint64_t(1) << 46) | (uint64_t(2) << 61);
 }
 
-__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t accumulate) {
+// One M=256 N=256 K=16 MMA of the CTA pair, issued by the leader: A and B
+// descriptors address the same offsets in both CTAs' shared memory.
+__device__ __forceinline__ void umma_bf16_pair(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(a), "l"(b), "r"(kIdesc), "r"(accumulate));
 }
 
-__device__ __forceinline__ void umma_commit(uint32_t bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+// Arrive on `bar` (shared::cluster address, own or peer CTA) once the pair's
+// MMAs issued so far have completed.
+__device__ __forceinline__ void umma_commit_pair(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
 
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
@@ -340,14 +373,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint16_t* warp_consts = reinterpret_cast<uint16_t*>(smem + STAGES * STAGE_BYTES + 2 * ROPE_BYTES);
   uint64_t* bars =
       reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES + 2 * ROPE_BYTES + kEpiWarps * WARP_CONST_BYTES);
-  // bars: full[STAGES], empty[STAGES], tfull[2], tempty[2]
+  // bars: full[STAGES] (leader), empty[STAGES], tfull[2], tempty[2] (leader)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
   volatile uint32_t* abort_flag = tmem_slot + 1;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();  // 0 = the pair's leader
+  const int pair = blockIdx.x >> 1, n_pairs = gridDim.x >> 1;
   const int dim = p.H * 128;
   const int n_half = dim / BN;  // N tiles per side
-  const int tiles_m = int((p.M + BM - 1) / BM);
+  const int tiles_m = int((p.M + PAIR_M - 1) / PAIR_M);
   const int n_tiles = tiles_m * 2 * n_half;
   const int kb_count = dim / BK;
 
@@ -359,24 +394,24 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(full_bar(s), 1);
-      mbar_init(empty_bar(s), 1);
+      mbar_init(full_bar(s), 1);   // the leader's producer arms it for both CTAs' bytes
+      mbar_init(empty_bar(s), 1);  // one commit from the leader's MMA thread
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(tfull_bar(b), 1);
-      mbar_init(tempty_bar(b), kEpiWarps);  // one arrival per epilogue warp
+      mbar_init(tempty_bar(b), 2 * kEpiWarps);  // every epilogue warp of both CTAs
     }
     *abort_flag = 0u;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"(TMEM_COLS)
                  : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
   }
   tc_fence_before();
-  __syncthreads();
+  cluster_sync();  // both CTAs' barriers initialised and TMEM allocated
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -385,28 +420,30 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      for (int t = blockIdx.x; t < n_tiles && !*abort_flag; t += gridDim.x) {
+      for (int t = pair; t < n_tiles && !*abort_flag; t += n_pairs) {
         const int tm = t % tiles_m, tn = t / tiles_m;
-        const int side = tn / n_half, n0 = (tn % n_half) * BN;
+        const int side = tn / n_half, n0 = (tn % n_half) * BN + int(rank) * B_ROWS;
+        const int m0 = tm * PAIR_M + int(rank) * BM;
         const CUtensorMap* wmap = side ? &tm_wv : &tm_wk;
         for (int kb = 0; kb < kb_count; ++kb) {
           if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag, p.err)) break;
           const uint32_t a_dst = smem_base + stage * STAGE_BYTES;
-          mbar_expect_tx(full_bar(stage), STAGE_BYTES);
-          tma_load_2d(a_dst, &tm_x, kb * BK, tm * BM, full_bar(stage));
-          tma_load_2d(a_dst + A_BYTES, wmap, kb * BK, n0, full_bar(stage));
+          const uint32_t leader_full = map_to_rank(full_bar(stage), 0);
+          if (rank == 0) mbar_expect_tx(full_bar(stage), 2 * STAGE_BYTES);
+          tma_load_2d_pair(a_dst, &tm_x, kb * BK, m0, leader_full);
+          tma_load_2d_pair(a_dst + A_BYTES, wmap, kb * BK, n0, leader_full);
           if (++stage == STAGES) stage = 0, phase ^= 1u;
         }
       }
     }
   } else if (warp == 1) {
-    // ---------------------------------------------------- MMA issuer
-    if (lane == 0) {
+    // ---------------------------------------------------- MMA issuer (leader)
+    if (lane == 0 && rank == 0) {
       int stage = 0;
       uint32_t phase = 0;
       int buf = 0;
       uint32_t acc_phase = 0;
-      for (int t = blockIdx.x; t < n_tiles && !*abort_flag; t += gridDim.x) {
+      for (int t = pair; t < n_tiles && !*abort_flag; t += n_pairs) {
         if (!mbar_wait(tempty_bar(buf), acc_phase ^ 1u, abort_flag, p.err)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + uint32_t(buf * BN);
@@ -421,12 +458,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint64_t adesc = smem_desc(a_addr), bdesc = smem_desc(a_addr + A_BYTES);
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k)  // +32 bytes per K step = +2 in the address field
-            umma_bf16(d_tmem, adesc + uint64_t(2 * k), bdesc + uint64_t(2 * k), (kb | k) != 0 ? 1u : 0u);
-          umma_commit(empty_bar(stage));
+            umma_bf16_pair(d_tmem, adesc + uint64_t(2 * k), bdesc + uint64_t(2 * k), (kb | k) != 0 ? 1u : 0u);
+          umma_commit_pair(map_to_rank(empty_bar(stage), 0));
+          umma_commit_pair(map_to_rank(empty_bar(stage), 1));
           if (++stage == STAGES) stage = 0, phase ^= 1u;
         }
         if (!ok) break;
-        umma_commit(tfull_bar(buf));
+        umma_commit_pair(map_to_rank(tfull_bar(buf), 0));
+        umma_commit_pair(map_to_rank(tfull_bar(buf), 1));
         if (++buf == 2) buf = 0, acc_phase ^= 1u;
       }
     }
@@ -442,10 +481,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     int buf = 0;
     uint32_t acc_phase = 0;
     bool bad = false;
-    for (int t = blockIdx.x; t < n_tiles; t += gridDim.x) {
+    for (int t = pair; t < n_tiles; t += n_pairs) {
       const int tm = t % tiles_m, tn = t / tiles_m;
       const int side = tn / n_half, head = (tn % n_half) * (BN / 128) + hh;
-      const int64_t row = int64_t(tm) * BM + rit;
+      const int64_t row = int64_t(tm) * PAIR_M + int64_t(rank) * BM + rit;
       // stage this tile's constants while its main loop runs
       const uint16_t* bias_g = side ? p.bias_v : p.bias_k;
       const bool rope = side == 0 && p.rope_cos != nullptr;
@@ -478,7 +517,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // the accumulator is in registers: hand it back to the MMA warp
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(tempty_bar(buf));
+      if (lane == 0) mbar_arrive_cluster(map_to_rank(tempty_bar(buf), 0));  // the leader's barrier
       if (row < p.M)
         epilogue_head(w, p, side, row, head, bias_g ? wc : nullptr, gain ? wc + 128 : nullptr,
                       rope ? my_cos : nullptr, my_sin, bad);
@@ -497,16 +536,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   if (*abort_flag && threadIdx.x == 0) {
-    // copies or MMAs of an aborted CTA may still be in flight: give them a
+    // copies or MMAs of an aborted pair may still be in flight: give them a
     // bounded 1 ms to land before the memory they target is released
     const uint64_t t0 = globaltimer();
     while (globaltimer() - t0 < 1000000ull) {
     }
   }
-  __syncthreads();
+  cluster_sync();  // no MMA or arrival of the pair targets this CTA any more
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS) : "memory");
   }
 }
 
@@ -545,25 +584,41 @@ cudaError_t launch_kv_project(const void* x, const void* wk, const void* wv, con
   if (!kv_project_shape_ok(p.M, p.H, 128)) return cudaErrorInvalidValue;
   const uint64_t dim = uint64_t(p.H) * 128;
   CUtensorMap mx, mk, mv;
-  if (!make_map(&mx, x, uint64_t(p.M), dim, BM) || !make_map(&mk, wk, dim, dim, BN) ||
-      !make_map(&mv, wv, dim, dim, BN))
+  if (!make_map(&mx, x, uint64_t(p.M), dim, BM) || !make_map(&mk, wk, dim, dim, B_ROWS) ||
+      !make_map(&mv, wv, dim, dim, B_ROWS))
     return cudaErrorInvalidValue;
-  static int configured_device = -1;
+  static int configured_device = -1, max_pairs = 0;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg{};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2, attr[0].val.clusterDim.y = 1, attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
   if (configured_device != dev) {
     e = cudaFuncSetAttribute(k_kv_project, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     if (e != cudaSuccess) return e;
+    // CTA pairs that can be resident at once: the persistent grid
+    int sms = 0;
+    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
+    cfg.gridDim = dim3(2 * (sms / 2));
+    int clusters = 0;
+    e = cudaOccupancyMaxActiveClusters(&clusters, k_kv_project, &cfg);
+    if (e != cudaSuccess) return e;
+    if (clusters < 1) return cudaErrorInvalidConfiguration;
+    max_pairs = clusters;
     configured_device = dev;
   }
-  int sms = 0;
-  e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  if (e != cudaSuccess) return e;
-  const int tiles = int((p.M + BM - 1) / BM) * int(2 * dim / BN);
-  const int grid = tiles < sms ? tiles : sms;
-  k_kv_project<<<grid, kThreads, kSmemBytes, stream>>>(mx, mk, mv, p);
-  return cudaGetLastError();
+  const int tiles = int((p.M + PAIR_M - 1) / PAIR_M) * int(2 * dim / BN);
+  const int pairs = tiles < max_pairs ? tiles : max_pairs;
+  cfg.gridDim = dim3(2 * pairs);
+  return cudaLaunchKernelEx(&cfg, k_kv_project, mx, mk, mv, p);
 }
 
 }  // namespace nkv
