@@ -235,14 +235,14 @@ __device__ __forceinline__ float lo_f(uint32_t w) { return __uint_as_float(w << 
 __device__ __forceinline__ float hi_f(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
 __device__ __forceinline__ uint32_t pack_rn(float lo, float hi) { return dev::bf16x2_bits_nonnan(lo, hi); }
 
-// The epilogue of one (token row, head): w holds bf16(accumulator) of the
-// row's 128 values.  bias: this head's 128 bias values or null; gain: the
-// 128 RMS-norm gains or null; rope_c / rope_s: this row's 64 cos / sin
-// values or null (all in shared memory).
-__device__ __forceinline__ void epilogue_head(uint32_t (&w)[64], const KvProjectParams& p, int side, int64_t row,
-                                              int head, const uint16_t* bias, const uint16_t* gain,
-                                              const float* rope_c, const float* rope_s, bool& bad) {
-  const int dim = p.H * 128;
+// The values of one (token row, head): w holds bf16(accumulator) of the
+// row's 128 values and leaves with the K / V the reference commits.  bias:
+// this head's 128 bias values or null; gain: the 128 RMS-norm gains or null;
+// rope_c / rope_s: this row's 64 cos / sin values or null (all in shared
+// memory).
+__device__ __forceinline__ void finish_values(uint32_t (&w)[64], const KvProjectParams& p, int side,
+                                              const uint16_t* bias, const uint16_t* gain, const float* rope_c,
+                                              const float* rope_s) {
   // Lin::fwd (modules/mod.rs:135-138): the GEMM's bf16 result plus the bias,
   // added in bf16
   if (bias) {
@@ -306,21 +306,12 @@ __device__ __forceinline__ void epilogue_head(uint32_t (&w)[64], const KvProject
       }
     }
   }
-  // the bf16 K / V the attention reads
-  uint16_t* out = side ? p.v_out : p.k_out;
-  if (out) {
-    uint4* o = reinterpret_cast<uint4*>(out + row * dim + head * 128);
-#pragma unroll
-    for (int q = 0; q < 16; ++q) o[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
-  }
-  // the archive rows: quantize_one (int8.rs:65-81) of committed rows only
-  uint8_t* codes = side ? p.v_codes : p.k_codes;
-  if (!codes) return;
-  int64_t dst = -1;
-#pragma unroll
-  for (int i = 0; i < 2; ++i)
-    if (i < p.n_ranges && row >= p.range_lo[i] && row < p.range_hi[i]) dst = row - p.range_lo[i] + p.range_dst[i];
-  if (dst < 0) return;
+}
+
+// The archive row of one (token row, head): quantize_one (int8.rs:65-81) of
+// the 128 values in w, codes written as 128 bytes to `stage` (shared
+// memory), the scale returned; `bad` gets the non-finite check.
+__device__ __forceinline__ float quantize_row(const uint32_t (&w)[64], uint8_t* stage, bool& bad) {
   // |x| max on the bf16 patterns: NaN-propagating, and inf / NaN patterns
   // (>= 0x7F80) sort above every finite one, so the same max answers the
   // non-finite scan (x != x || |x| >= f32::MAX, int8.rs:99-117; no finite
@@ -333,7 +324,7 @@ __device__ __forceinline__ void epilogue_head(uint32_t (&w)[64], const KvProject
   const float peak = __uint_as_float(pk << 16);
   const float inv127 = (float)(1.0 / 127.0);
   const float s = peak > 0.0f ? __fadd_rn(__fmul_rn(peak, inv127), 0.0f) : 1.0f;
-  uint4* qo = reinterpret_cast<uint4*>(codes + dst * dim + head * 128);
+  uint4* qo = reinterpret_cast<uint4*>(stage);
   if (s >= FLT_MIN && s <= 1e37f) {
     const float r = __frcp_rn(s);
 #pragma unroll
@@ -360,7 +351,17 @@ __device__ __forceinline__ void epilogue_head(uint32_t (&w)[64], const KvProject
       qo[k] = make_uint4(c[0], c[1], c[2], c[3]);
     }
   }
-  (side ? p.v_scales : p.k_scales)[dst * p.H + head] = s;
+  return s;
+}
+
+// The archive row of token row `row` (rows [lo, hi) of x go to archive rows
+// dst..), or -1 when the row is not committed.
+__device__ __forceinline__ int64_t archive_row(const KvProjectParams& p, int64_t row) {
+  int64_t dst = -1;
+#pragma unroll
+  for (int i = 0; i < 2; ++i)
+    if (i < p.n_ranges && row >= p.range_lo[i] && row < p.range_hi[i]) dst = row - p.range_lo[i] + p.range_dst[i];
+  return row < p.M ? dst : -1;
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -519,13 +520,57 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(map_to_rank(tempty_bar(buf), 0));  // the leader's barrier
       if (row < p.M)
-        epilogue_head(w, p, side, row, head, bias_g ? wc : nullptr, gain ? wc + 128 : nullptr,
-                      rope ? my_cos : nullptr, my_sin, bad);
+        finish_values(w, p, side, bias_g ? wc : nullptr, gain ? wc + 128 : nullptr, rope ? my_cos : nullptr,
+                      my_sin);
+      // Stores go out as whole 128-byte lines: each thread parks its row in
+      // the quadrant's rotary rows (free once both warps of the quadrant are
+      // past the rotation; this warp takes the table it copied), then the
+      // warp writes 2 rows x 256 bytes (K / V) or 4 rows x 128 bytes (codes)
+      // per instruction.
+      asm volatile("bar.sync %0, 64;" ::"r"(pair_bar) : "memory");
+      const int64_t row0 = row - lane;  // the warp's first token row
+      uint8_t* stage_base = reinterpret_cast<uint8_t*>((hh == 0 ? rope_cos_s : rope_sin_s) + quad * 32 * ROPE_PITCH);
+      uint8_t* my_stage = stage_base + lane * ROPE_PITCH * 4;
+      uint16_t* out = side ? p.v_out : p.k_out;
+      if (out) {
+        if (row < p.M) {
+          uint4* st = reinterpret_cast<uint4*>(my_stage);
+#pragma unroll
+          for (int q = 0; q < 16; ++q) st[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+        }
+        __syncwarp();
+#pragma unroll 4
+        for (int i = 0; i < 16; ++i) {
+          const int u = i * 32 + lane, r = u >> 4, cu = u & 15;
+          if (row0 + r < p.M)
+            *reinterpret_cast<uint4*>(out + (row0 + r) * dim + head * 128 + cu * 8) =
+                *reinterpret_cast<const uint4*>(stage_base + r * ROPE_PITCH * 4 + cu * 16);
+        }
+        __syncwarp();
+      }
+      uint8_t* codes = side ? p.v_codes : p.k_codes;
+      if (codes) {
+        const int64_t dst = archive_row(p, row);
+        if (dst >= 0) {
+          const float sc = quantize_row(w, my_stage, bad);
+          (side ? p.v_scales : p.k_scales)[dst * p.H + head] = sc;
+        }
+        __syncwarp();
+#pragma unroll 4
+        for (int i = 0; i < 8; ++i) {
+          const int u = i * 32 + lane, r = u >> 3, cu = u & 7;
+          const int64_t d = archive_row(p, row0 + r);
+          if (d >= 0)
+            *reinterpret_cast<uint4*>(codes + d * dim + head * 128 + cu * 16) =
+                *reinterpret_cast<const uint4*>(stage_base + r * ROPE_PITCH * 4 + cu * 16);
+        }
+      }
       if (__any_sync(0xFFFFFFFFu, bad)) {
         if (lane == 0) atomicOr(p.flag, 1u << side);
         bad = false;
       }
-      // the quadrant's rotary rows and the warp's constants are free again
+      // the quadrant's rotary / staging rows and the warp's constants are
+      // free again
       asm volatile("bar.sync %0, 64;" ::"r"(pair_bar) : "memory");
       if (++buf == 2) buf = 0, acc_phase ^= 1u;
     }
