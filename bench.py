@@ -704,6 +704,12 @@ def run_project(args) -> None:
                    "sample": f"failed: {e}"}
     peaks = load_peaks()
     tflops = PROJECT_FLOPS / (launch_ms / 1e3) / 1e12
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tp):
+        t = json.load(open(tp)).get("project_kv_project")
+        if t:
+            traffic = int(t["dram_bytes"] / t["layers"])
     cublas_tflops = PROJECT_FLOPS / (cublas_ms / 1e3) / 1e12
     value = SEG_TOKENS * args.steps / (ms_fused / 1e3)
     if rank == 0:
@@ -722,7 +728,7 @@ def run_project(args) -> None:
                         "what": "cuBLAS projection (torch.matmul) + eager bias / RmsNorm / RoPE + commit_tensors",
                         "speedup_fused": round(ms_unfused / ms_fused, 3)},
             "roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": peaks["bf16_tflops"],
-                         "unit": "TFLOP/s", "frac": round(tflops / peaks["bf16_tflops"], 4), "traffic": None,
+                         "unit": "TFLOP/s", "frac": round(tflops / peaks["bf16_tflops"], 4), "traffic": traffic,
                          "kernel": "k_kv_project (one launch per layer)", "flops_per_launch": PROJECT_FLOPS,
                          "launch_ms": round(launch_ms, 4), "peak_src": peaks["src"] + " (burst cuBLAS bf16)",
                          "cublas_same_gemm_ms": round(cublas_ms, 4), "cublas_same_gemm_tflops": round(cublas_tflops, 1)},
