@@ -22,7 +22,7 @@
 //  * warp 0, one thread per CTA: TMA producer.  Its CTA's 128 x 64 slices of
 //    x and of W_k or W_v per stage, 128-byte swizzled, into a 4-stage ring
 //    (32 KB per stage); the loads complete on the pair leader's barrier
-//    (plain loads, no multicast);
+//    (plain per-CTA loads);
 //  * warp 1: allocates 512 TMEM columns per CTA (two 128 x 256 f32
 //    accumulators, the CTA's half of a tile); in the leader, one thread
 //    issues the MMAs, frees each stage of both CTAs with tcgen05.commit and
@@ -148,7 +148,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
   }
 }
 
-// 2-D tiled TMA load (no multicast) into this CTA's shared memory,
+// 2-D tiled TMA load (a plain per-CTA load) into this CTA's shared memory,
 // completing on `bar`, a shared::cluster barrier address of the CTA pair
 // (the leader's full barrier).
 __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, int32_t x, int32_t y,
