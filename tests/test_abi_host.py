@@ -118,3 +118,37 @@ def test_synth_generator_is_deterministic():
     assert a.shape == (1, 7, 4, 32) and (a == b).all() and not (a == c).all()
     t = synth.quantile_table()
     assert t.shape == (65536,) and abs(float(t.mean())) < 1e-6 and abs(float(t.std()) - 1.0) < 1e-3
+
+
+def test_ctypes_structs_match_the_header(nkv, tmp_path):
+    """Every struct the ctypes mirror passes across the ABI has the header's
+    size and field offsets (compiled with gcc against include/nomas_kv.h)."""
+    import ctypes as C
+    import shutil
+    import subprocess
+
+    from nomas_kv import _abi
+
+    if shutil.which("gcc") is None:
+        pytest.skip("gcc not available")
+    structs = {n: getattr(_abi, n) for n in ("nkv_qvg_config", "nkv_cache_config", "nkv_segment_desc",
+                                             "nkv_segment_layout", "nkv_metrics", "nkv_cache_info_t",
+                                             "nkv_kernel_stat", "nkv_staged_layer", "nkv_row_range",
+                                             "nkv_kv_project_args")}
+    lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "nomas_kv.h"', "int main(void) {"]
+    for name, st in structs.items():
+        lines.append(f'  printf("{name} %zu\\n", sizeof({name}));')
+        for f, _ in st._fields_:
+            lines.append(f'  printf("{name}.{f} %zu\\n", offsetof({name}, {f}));')
+    lines += ["  return 0;", "}"]
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    inc = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include")
+    subprocess.run(["gcc", "-std=c11", "-I", inc, str(src), "-o", str(exe)], check=True)
+    out = dict(line.rsplit(" ", 1) for line in subprocess.run([str(exe)], capture_output=True, text=True,
+                                                               check=True).stdout.splitlines())
+    for name, st in structs.items():
+        assert int(out[name]) == C.sizeof(st), name
+        for f, _ in st._fields_:
+            assert int(out[f"{name}.{f}"]) == getattr(st, f).offset, f"{name}.{f}"
