@@ -307,3 +307,59 @@ def test_stage_needs_int8(nkv):
     bank = nkv.KvBank(cfg, 1, 1, 2, D, BF16)
     with pytest.raises(nkv.InvalidConfigError):
         bank.stage_segment(_desc(nkv, 0, 64, 2, 16))
+
+
+def test_chunked_capture_equals_concatenated_commit(nkv, orc):
+    """The pipeline's capture (causal_ar.rs:381-420): a segment's video rows
+    come from several chunks, its text rows from the last chunk.  Two
+    projection calls with row ranges write one staged record; the bank equals
+    one fed the concatenated K / V through nkv_bank_commit."""
+    torch = _torch()
+    H, tpf, text = 2, 64, 16
+    dim = H * D
+    frames_a, frames_b = 2, 1  # chunk A: 2 frames; chunk B: 1 frame + the text block
+    La, Lb = frames_a * tpf + text, frames_b * tpf + text  # every chunk carries its text rows
+    L = (frames_a + frames_b) * tpf + text
+    produced, fed = _bank(nkv, 1, H), _bank(nkv, 1, H)
+    rng = np.random.default_rng(12)
+    b = lambda arr: dev_bf16(orc.bf16_bits(np.asarray(arr, np.float32)))  # noqa: E731
+    w = dict(wk=b(rng.standard_normal((dim, dim)) / 16), wv=b(rng.standard_normal((dim, dim)) / 16),
+             bk=b(0.1 * rng.standard_normal(dim)), bv=b(0.1 * rng.standard_normal(dim)),
+             k_gain=b(1 + 0.1 * rng.standard_normal(D)))
+    for seg in range(3):
+        xa, xb = b(rng.standard_normal((La, dim))), b(rng.standard_normal((Lb, dim)))
+        ang = rng.uniform(0, 6.3, (La + Lb, D // 2)).astype(np.float32)
+        cos = torch.from_numpy(np.cos(ang)).cuda()
+        sin = torch.from_numpy(np.sin(ang)).cuda()
+        ka, va = (torch.empty((La, dim), dtype=torch.bfloat16, device="cuda") for _ in range(2))
+        kb, vb = (torch.empty((Lb, dim), dtype=torch.bfloat16, device="cuda") for _ in range(2))
+        d = _abi_desc(seg, tpf, frames_a + frames_b, text)
+        staged = produced.stage_segment(d)[0]
+        # chunk A: its video rows -> segment rows [0, 2 tpf)
+        nkv.kv_project(xa, w["wk"], w["wv"], bk=w["bk"], bv=w["bv"], k_gain=w["k_gain"],
+                       rope=(cos[:La].contiguous(), sin[:La].contiguous()), k_out=ka, v_out=va, codes=staged,
+                       ranges=[(0, frames_a * tpf, 0)], status_ptr=staged["status"], stream=produced.stream)
+        # chunk B: video rows -> [2 tpf, 3 tpf), text rows -> [3 tpf, L)
+        nkv.kv_project(xb, w["wk"], w["wv"], bk=w["bk"], bv=w["bv"], k_gain=w["k_gain"],
+                       rope=(cos[La:].contiguous(), sin[La:].contiguous()), k_out=kb, v_out=vb, codes=staged,
+                       ranges=[(0, frames_b * tpf, frames_a * tpf), (frames_b * tpf, Lb, (frames_a + frames_b) * tpf)],
+                       status_ptr=staged["status"], stream=produced.stream)
+        produced.commit_staged()
+        k_cat = torch.cat([ka[:frames_a * tpf], kb]).view(1, L, H, D).contiguous()
+        v_cat = torch.cat([va[:frames_a * tpf], vb]).view(1, L, H, D).contiguous()
+        fed.commit_tensors(d, [k_cat], [v_cat])
+        torch.cuda.synchronize()
+        assert np.array_equal(produced.layer(0).export_segment(seg), fed.layer(0).export_segment(seg))
+        pk, pv = produced.layer(0).working_set()
+        fk, fv = fed.layer(0).working_set()
+        assert torch.equal(pk.view(torch.int16), fk.view(torch.int16))
+        assert torch.equal(pv.view(torch.int16), fv.view(torch.int16))
+    assert produced.metrics().as_dict() == fed.metrics().as_dict()
+
+
+def _abi_desc(i, tpf, frames, text):
+    from nomas_kv import _abi
+    d = _abi.nkv_segment_desc()
+    d.segment_index, d.frame_start, d.frame_count = i, i * frames, frames
+    d.image_tokens, d.text_tokens, d.action_start = tpf * frames, text, -1
+    return d
