@@ -363,3 +363,50 @@ def _abi_desc(i, tpf, frames, text):
     d.segment_index, d.frame_start, d.frame_count = i, i * frames, frames
     d.image_tokens, d.text_tokens, d.action_start = tpf * frames, text, -1
     return d
+
+
+@pytest.mark.parametrize("mode", ["recent_capacity", "parked"])
+def test_staged_commit_other_modes(nkv, orc, mode):
+    """Staged commits keep the plain commit's semantics in Recent mode with SWA
+    eviction (history.rs:345-360, swa.rs:52-130) and while parked (a commit
+    while parked is overwritten by the stale set on unpark,
+    phase_swap.rs:42-92): a producer-fed bank and a tensor-fed twin stay equal."""
+    torch = _torch()
+    H, tpf, frames, text = 2, 64, 2, 16
+    L = tpf * frames + text
+    dim = H * D
+    if mode == "recent_capacity":
+        cfg = nkv.CacheConfig(storage=nkv.CacheStorage.int8(), sampling=nkv.HistorySampling.recent(),
+                              capacity=3 * L - 40)
+    else:
+        cfg = nkv.CacheConfig(storage=nkv.CacheStorage.int8(), sampling=nkv.HistorySampling.uniform(),
+                              past_frames=3, phase_swap=True)
+    produced, fed = (nkv.KvBank(cfg, 1, 1, H, D, BF16) for _ in range(2))
+    rng = np.random.default_rng(31)
+    b = lambda arr: dev_bf16(orc.bf16_bits(np.asarray(arr, np.float32)))  # noqa: E731
+    w = [dict(wk=b(rng.standard_normal((dim, dim)) / 16), wv=b(rng.standard_normal((dim, dim)) / 16),
+              bk=b(0.1 * rng.standard_normal(dim)), k_gain=b(1 + 0.1 * rng.standard_normal(D)))]
+    for seg in range(6):
+        x = [b(rng.standard_normal((L, dim)))]
+        ks = [torch.empty((1, L, H, D), dtype=torch.bfloat16, device="cuda")]
+        vs = [torch.empty_like(ks[0])]
+        d = _abi_desc(seg, tpf, frames, text)
+        park = mode == "parked" and seg in (2, 4)
+        if park:
+            produced.park_all()
+            fed.park_all()
+        produced.commit_projected(d, x, w, k_outs=[ks[0].view(L, dim)], v_outs=[vs[0].view(L, dim)])
+        fed.commit_tensors(d, ks, vs)
+        if park:
+            produced.unpark_all()
+            fed.unpark_all()
+        torch.cuda.synchronize()
+        pk, pv = produced.layer(0).working_set()
+        fk, fv = fed.layer(0).working_set()
+        assert torch.equal(pk.view(torch.int16), fk.view(torch.int16))
+        assert torch.equal(pv.view(torch.int16), fv.view(torch.int16))
+        assert [s.as_tuple() for s in produced.layer(0).working_layout()] == \
+            [s.as_tuple() for s in fed.layer(0).working_layout()]
+        assert produced.metrics().as_dict() == fed.metrics().as_dict()
+    if mode == "recent_capacity":
+        assert produced.metrics().evicted_tokens > 0
