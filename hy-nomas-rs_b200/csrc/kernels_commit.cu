@@ -29,9 +29,10 @@ namespace nkv {
 // the residual e = x - s * q0 computed exactly by an FMA, and
 // q1 = RN(q0 + e * r), Markstein's theorem gives q1 = RN(x / s) whenever the
 // quotient is in the normal range (a subnormal quotient rounds to 0 either
-// way).  Round-half-away-from-zero of q1 is then round-to-nearest-even by
-// the 1.5 * 2^23 magic constant, corrected on exact .5 ties by a select.
-// Rows whose scale is subnormal (or above 1e37) take the IEEE division.
+// way).  Round-half-away-from-zero of the quotient's magnitude is then
+// floor(RN(q1 + (0.5 - 2^-25))), taken by a round-toward-zero add of the
+// 1.5 * 2^23 magic constant (code_bits in nkv_quant.cuh).  Rows whose scale
+// is subnormal (or above 1e37) take the IEEE division.
 // ---------------------------------------------------------------------------
 // The exact per-value path kept out of line: inlined, the compiler turns the
 // rarely taken branch into predicated code that every thread issues.
