@@ -271,6 +271,40 @@ def cpu_sample_project(threads: int, rows: int = 96) -> dict:
                       f"(f64-accumulated GEMM, one host thread per layer), {sec:.2f} s; scaled to 48 layers"}
 
 
+def host_policy_latency(reps: int = 2000) -> dict:
+    """Host latency of the index evaluation and the SWA trim plan (they move
+    ~0 bytes): raw C-ABI calls with preallocated buffers, so the figure is the
+    policy code plus one ctypes transition.  Sizes of the long-session
+    configuration: 1,024 frames, 32 past frames; a trim over 256 records."""
+    import numpy as np
+    import nomas_kv as nk
+
+    lib = nk.lib()
+    out = np.zeros(1100, np.uint64)
+    n = C.c_uint64()
+    res = {}
+    for name, kind, sampling, gamma in (("uniform_frame_indices_us", 0, nk.NKV_SAMPLING_UNIFORM, 2.0),
+                                        ("recent_mix_indices_us", 1, nk.NKV_SAMPLING_RECENT_MIX, 2.0),
+                                        ("temporal_context_indices_us", 2, nk.NKV_SAMPLING_TEMPORAL, 0.9)):
+        ptr = out.ctypes.data_as(C.c_void_p)
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            lib.nkv_frame_indices(kind, 1024, 32, sampling, gamma, ptr, out.size, C.byref(n))
+        res[name] = round((time.perf_counter() - t0) / reps * 1e6, 3)
+    recs = np.array([[i, 4 * i, 4, 4 * TPF, TEXT] for i in range(256)], np.uint64)
+    df, dr, kept = np.zeros(514, np.uint64), np.zeros(257, np.uint64), np.zeros(1285, np.uint64)
+    ndf, ndr, ev, nkp = C.c_uint64(), C.c_uint64(), C.c_uint64(), C.c_uint64()
+    pr, pdf, pdr, pk = (a.ctypes.data_as(C.c_void_p) for a in (recs, df, dr, kept))
+    cap = 200 * SEG_TOKENS + 3 * TPF  # evicts whole records and part of a video block
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        lib.nkv_plan_recent_trim(pr, 256, cap, TPF, pdf, C.byref(ndf), pdr, C.byref(ndr), C.byref(ev), pk,
+                                 C.byref(nkp))
+    res["recent_trim_plan_us"] = round((time.perf_counter() - t0) / reps * 1e6, 3)
+    res["what"] = "host C++ policy per call incl. one ctypes call; 1,024 frames / 32 past; trim over 256 records"
+    return res
+
+
 # ------------------------------------------------------------ GPU side
 def run_gpu(args) -> None:
     import torch
@@ -506,6 +540,7 @@ def run_gpu(args) -> None:
                        "working_set_tokens": rebuild_tokens(), "bytes_per_step": step_bytes(model_layers, wl, swap)["total"],
                        "parallelism": f"layer-sharded x{world}", "l2": "inputs 3.8 GB per step > 126 MB L2"},
             "tokens_per_s": tok,
+            "host_policy_latency": host_policy_latency(),
             "phase_swap": swap_info,
             "roofline": {"bound": "hbm", "achieved": round(gather_gbs, 1) if gather_gbs else None,
                          "peak": peaks["hbm_gbs"], "unit": "GB/s",
