@@ -410,3 +410,42 @@ def test_staged_commit_other_modes(nkv, orc, mode):
         assert produced.metrics().as_dict() == fed.metrics().as_dict()
     if mode == "recent_capacity":
         assert produced.metrics().evicted_tokens > 0
+
+
+def test_staged_commit_8b_geometry(nkv, orc):
+    """Full size: 24 heads, 6,496-token segments (4 x 1,560 video + 256 text),
+    two layers, three segments; the producer-fed bank equals the tensor-fed
+    twin byte for byte."""
+    torch = _torch()
+    n_layers, H, tpf, frames, text = 2, 24, 1560, 4, 256
+    L = tpf * frames + text
+    dim = H * D
+    cfg = nkv.CacheConfig(storage=nkv.CacheStorage.int8(), sampling=nkv.HistorySampling.uniform(), past_frames=16)
+    produced, fed = (nkv.KvBank(cfg, n_layers, 1, H, D, BF16) for _ in range(2))
+    g = torch.Generator(device="cuda")
+    g.manual_seed(5)
+    rnd = lambda *shape, scale=1.0: (torch.randn(*shape, device="cuda", generator=g) * scale).to(torch.bfloat16)  # noqa: E731
+    weights = [dict(wk=rnd(dim, dim, scale=dim ** -0.5), wv=rnd(dim, dim, scale=dim ** -0.5), bk=rnd(dim, scale=0.1),
+                    bv=rnd(dim, scale=0.1), k_gain=(1 + rnd(D, scale=0.1).float()).to(torch.bfloat16))
+               for _ in range(n_layers)]
+    ang = torch.arange(L, device="cuda", dtype=torch.float32)[:, None] * \
+        torch.pow(torch.tensor(256.0, device="cuda"), -torch.arange(0, D, 2, device="cuda") / D)[None, :]
+    rope = (torch.cos(ang).contiguous(), torch.sin(ang).contiguous())
+    for seg in range(3):
+        xs = [rnd(L, dim) for _ in range(n_layers)]
+        ks = [torch.empty((1, L, H, D), dtype=torch.bfloat16, device="cuda") for _ in range(n_layers)]
+        vs = [torch.empty_like(t) for t in ks]
+        d = _abi_desc(seg, tpf, frames, text)
+        produced.commit_projected(d, xs, weights, rope=rope, k_outs=[t.view(L, dim) for t in ks],
+                                  v_outs=[t.view(L, dim) for t in vs])
+        fed.commit_tensors(d, ks, vs)
+        torch.cuda.synchronize()
+        for i in range(n_layers):
+            assert np.array_equal(produced.layer(i).export_segment(seg), fed.layer(i).export_segment(seg))
+            pk, pv = produced.layer(i).working_set()
+            fk, fv = fed.layer(i).working_set()
+            assert torch.equal(pk.view(torch.int16), fk.view(torch.int16))
+            assert torch.equal(pv.view(torch.int16), fv.view(torch.int16))
+    assert produced.metrics().as_dict() == fed.metrics().as_dict()
+    produced.close()
+    fed.close()
