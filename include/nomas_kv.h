@@ -232,8 +232,10 @@ int nkv_bank_kernel_stats(nkv_bank* bank, nkv_kernel_stat* out /* [NKV_KERNEL_CO
  *    time; commit, rollback, save and load are refused while one is pending.
  *  - nkv_bank_commit_staged: archive the staged record and rebuild, with
  *    nkv_bank_commit's semantics from the non-finite check on (a set status
- *    bit rejects the segment, NKV_ERR_MSG, and nothing changes).  The
- *    producer's work must be ordered before the bank's stream.
+ *    bit rejects the segment, NKV_ERR_MSG, and nothing changes).  Stage
+ *    zeroes the status words on the bank's stream, so the producer's work
+ *    must come after stage and before commit_staged in that stream's order
+ *    (simplest: launch it on the bank's stream).
  *  - nkv_bank_discard_staged: drop it (waits for the bank's stream). */
 typedef struct {
   uint8_t* k_codes;
