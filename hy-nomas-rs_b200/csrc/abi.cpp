@@ -279,7 +279,7 @@ int nkv_kv_project(const nkv_kv_project_args* a, void* stream) {
   return guarded([&] {
     need(a, "args");
     if (a->head_dim != 128 || !nkv::kv_project_shape_ok(a->tokens, a->heads, a->head_dim))
-      nkv::fail(NKV_ERR_ARGUMENT, "nkv_kv_project needs head_dim 128, heads * 128 a multiple of 256 and tokens > 0");
+      nkv::fail(NKV_ERR_ARGUMENT, "nkv_kv_project needs head_dim 128, heads * 128 a multiple of 256 (heads <= 256) and 0 < tokens <= 2^26");
     need(a->x, "x"), need(a->wk, "wk"), need(a->wv, "wv"), need(a->status, "status");
     const bool codes = a->k_codes || a->v_codes || a->k_scales || a->v_scales;
     if (codes && !(a->k_codes && a->v_codes && a->k_scales && a->v_scales))

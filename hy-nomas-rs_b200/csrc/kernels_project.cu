@@ -42,6 +42,8 @@
 
 #include <cfloat>
 #include <cstdint>
+#include <map>
+#include <mutex>
 
 #include "nkv_device.cuh"
 #include "nkv_kernels.h"
@@ -622,7 +624,11 @@ bool make_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, ui
 
 }  // namespace
 
-bool kv_project_shape_ok(int64_t M, int H, int D) { return M > 0 && D == 128 && H > 0 && (H * D) % BN == 0; }
+// tokens and heads bounded so tile counts (<= 2^18 x 2^8) and TMA row
+// coordinates stay well inside int32
+bool kv_project_shape_ok(int64_t M, int H, int D) {
+  return M > 0 && M <= (int64_t(1) << 26) && D == 128 && H > 0 && H <= 256 && (H * D) % BN == 0;
+}
 
 cudaError_t launch_kv_project(const void* x, const void* wk, const void* wv, const KvProjectParams& p,
                               cudaStream_t stream) {
@@ -632,7 +638,6 @@ cudaError_t launch_kv_project(const void* x, const void* wk, const void* wv, con
   if (!make_map(&mx, x, uint64_t(p.M), dim, BM) || !make_map(&mk, wk, dim, dim, B_ROWS) ||
       !make_map(&mv, wv, dim, dim, B_ROWS))
     return cudaErrorInvalidValue;
-  static int configured_device = -1, max_pairs = 0;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
@@ -645,20 +650,28 @@ cudaError_t launch_kv_project(const void* x, const void* wk, const void* wv, con
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (configured_device != dev) {
-    e = cudaFuncSetAttribute(k_kv_project, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    if (e != cudaSuccess) return e;
-    // CTA pairs that can be resident at once: the persistent grid
-    int sms = 0;
-    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (e != cudaSuccess) return e;
-    cfg.gridDim = dim3(2 * (sms / 2));
-    int clusters = 0;
-    e = cudaOccupancyMaxActiveClusters(&clusters, k_kv_project, &cfg);
-    if (e != cudaSuccess) return e;
-    if (clusters < 1) return cudaErrorInvalidConfiguration;
-    max_pairs = clusters;
-    configured_device = dev;
+  // once per device: the shared-memory opt-in and the number of CTA pairs
+  // that can be resident at once (the persistent grid)
+  static std::mutex mu;
+  static std::map<int, int> pairs_of_device;
+  int max_pairs = 0;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = pairs_of_device.find(dev);
+    if (it == pairs_of_device.end()) {
+      e = cudaFuncSetAttribute(k_kv_project, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+      if (e != cudaSuccess) return e;
+      int sms = 0;
+      e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+      if (e != cudaSuccess) return e;
+      cfg.gridDim = dim3(2 * (sms / 2));
+      int clusters = 0;
+      e = cudaOccupancyMaxActiveClusters(&clusters, k_kv_project, &cfg);
+      if (e != cudaSuccess) return e;
+      if (clusters < 1) return cudaErrorInvalidConfiguration;
+      it = pairs_of_device.emplace(dev, clusters).first;
+    }
+    max_pairs = it->second;
   }
   const int tiles = int((p.M + PAIR_M - 1) / PAIR_M) * int(2 * dim / BN);
   const int pairs = tiles < max_pairs ? tiles : max_pairs;

@@ -363,7 +363,7 @@ int nkv_qvg_decode(const float* cb_dev, int32_t side, const uint8_t* codes, cons
  * k_norm_gain (D) bf16 or NULL (no gain); qk_norm = 0 skips the norm;
  * rope_cos / rope_sin (tokens, D/2) f32 or NULL (no rotation); k_out / v_out
  * (tokens, H*D) bf16 or NULL; k_codes.. NULL for no codes.  Requirements:
- * D = 128, H*D a multiple of 256, tensor pointers 16-byte aligned, scales
+ * D = 128, H*D a multiple of 256, H <= 256, tokens <= 2^26, tensor pointers 16-byte aligned, scales
  * and status 4-byte aligned (else NKV_ERR_ARGUMENT).  *status (device word) gets bit 0 / bit 1 for a
  * non-finite K / V value in a range row, bit 31 if a bounded wait inside the
  * kernel ran out.  Stream-ordered on `stream` on the current device; no
