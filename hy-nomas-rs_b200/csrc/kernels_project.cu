@@ -66,10 +66,11 @@ constexpr int kThreads = 32 * (2 + kEpiWarps);
 // cos / sin tables (the head-0 warp of a lane quadrant copies cos, the head-1
 // warp sin, for the quadrant's 32 rows), rows padded to 68 floats so the 32
 // lanes' 16-byte reads of one column fall in distinct bank groups; and per
-// epilogue warp its head's 128 bias values and the 128 gain values (bf16).
+// epilogue warp its head's 128 bias values and the 128 gain values, widened
+// to f32 so the epilogue adds and multiplies them as packed f32x2 pairs.
 constexpr int ROPE_PITCH = 68;
 constexpr int ROPE_BYTES = BM * ROPE_PITCH * 4;  // one table
-constexpr int WARP_CONST_BYTES = (128 + 128) * 2;
+constexpr int WARP_CONST_BYTES = (128 + 128) * 4;
 constexpr int kSmemBytes = STAGES * STAGE_BYTES + 2 * ROPE_BYTES + kEpiWarps * WARP_CONST_BYTES +
                            1024 /* barriers */ + 1024 /* alignment */;
 constexpr uint64_t kWaitNs = 1000000000ull;  // 1 s per wait
@@ -243,26 +244,31 @@ __device__ __forceinline__ uint32_t pack_rn(float lo, float hi) { return dev::bf
 // rope_c / rope_s: this row's 64 cos / sin values or null (all in shared
 // memory).
 __device__ __forceinline__ void finish_values(uint32_t (&w)[64], const KvProjectParams& p, int side,
-                                              const uint16_t* bias, const uint16_t* gain, const float* rope_c,
+                                              const float* bias, const float* gain, const float* rope_c,
                                               const float* rope_s) {
   // Lin::fwd (modules/mod.rs:135-138): the GEMM's bf16 result plus the bias,
-  // added in bf16
+  // added in f32 (a packed f32x2 add: two independent roundings) and rounded
+  // to bf16
   if (bias) {
+    const float4* b4 = reinterpret_cast<const float4*>(bias);
 #pragma unroll
-    for (int q = 0; q < 16; ++q) {
-      const uint4 bw = *reinterpret_cast<const uint4*>(bias + 8 * q);
-      const uint32_t bs[4] = {bw.x, bw.y, bw.z, bw.w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        uint32_t& x = w[4 * q + j];
-        x = pack_rn(__fadd_rn(lo_f(x), lo_f(bs[j])), __fadd_rn(hi_f(x), hi_f(bs[j])));
-      }
+    for (int q = 0; q < 32; ++q) {
+      const float4 b = b4[q];
+      uint32_t& x0 = w[2 * q];
+      uint32_t& x1 = w[2 * q + 1];
+      const float2 v0 = __fadd2_rn(make_float2(lo_f(x0), hi_f(x0)), make_float2(b.x, b.y));
+      const float2 v1 = __fadd2_rn(make_float2(lo_f(x1), hi_f(x1)), make_float2(b.z, b.w));
+      x0 = pack_rn(v0.x, v0.y);
+      x1 = pack_rn(v1.x, v1.y);
     }
   }
   if (side == 0 && p.qk_norm) {
     // RmsNorm (norm.rs:55-65): f32 mean of squares over the head dim, four
     // interleaved partial sums (d mod 4) added as (s0 + s1) + (s2 + s3);
-    // 1/sqrt(var + eps) as an IEEE square root and division
+    // 1/sqrt(var + eps) as an IEEE square root and division.  The squares
+    // stay scalar multiplies and adds (a packed multiply feeding a packed
+    // add could be contracted into one rounding); the scaling below is
+    // multiplies only, so it runs on packed pairs.
     float s[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
     for (int j = 0; j < 64; ++j) {
@@ -273,21 +279,25 @@ __device__ __forceinline__ void finish_values(uint32_t (&w)[64], const KvProject
     const float ss = __fadd_rn(__fadd_rn(s[0], s[1]), __fadd_rn(s[2], s[3]));
     const float var = __fmul_rn(ss, 0.0078125f);  // / 128, exact
     const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, p.eps)));
+    const float2 inv2 = make_float2(inv, inv);
     if (gain) {
+      const float4* g4 = reinterpret_cast<const float4*>(gain);
 #pragma unroll
-      for (int q = 0; q < 16; ++q) {
-        const uint4 gw = *reinterpret_cast<const uint4*>(gain + 8 * q);
-        const uint32_t gs[4] = {gw.x, gw.y, gw.z, gw.w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          uint32_t& x = w[4 * q + j];
-          x = pack_rn(__fmul_rn(__fmul_rn(lo_f(x), inv), lo_f(gs[j])),
-                      __fmul_rn(__fmul_rn(hi_f(x), inv), hi_f(gs[j])));
-        }
+      for (int q = 0; q < 32; ++q) {
+        const float4 g = g4[q];
+        uint32_t& x0 = w[2 * q];
+        uint32_t& x1 = w[2 * q + 1];
+        const float2 v0 = __fmul2_rn(__fmul2_rn(make_float2(lo_f(x0), hi_f(x0)), inv2), make_float2(g.x, g.y));
+        const float2 v1 = __fmul2_rn(__fmul2_rn(make_float2(lo_f(x1), hi_f(x1)), inv2), make_float2(g.z, g.w));
+        x0 = pack_rn(v0.x, v0.y);
+        x1 = pack_rn(v1.x, v1.y);
       }
     } else {
 #pragma unroll
-      for (int j = 0; j < 64; ++j) w[j] = pack_rn(__fmul_rn(lo_f(w[j]), inv), __fmul_rn(hi_f(w[j]), inv));
+      for (int j = 0; j < 64; ++j) {
+        const float2 v = __fmul2_rn(make_float2(lo_f(w[j]), hi_f(w[j])), inv2);
+        w[j] = pack_rn(v.x, v.y);
+      }
     }
   }
   if (side == 0 && rope_c) {
@@ -479,7 +489,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float* my_cos = rope_cos_s + rit * ROPE_PITCH;
     const float* my_sin = rope_sin_s + rit * ROPE_PITCH;
     float* my_table = (hh == 0 ? rope_cos_s : rope_sin_s) + rit * ROPE_PITCH;
-    uint16_t* wc = warp_consts + (warp - 2) * (WARP_CONST_BYTES / 2);  // [bias 128][gain 128]
+    float* wc = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(warp_consts) + (warp - 2) * WARP_CONST_BYTES);
+    // wc: [bias 128][gain 128] f32
     const uint32_t pair_bar = 1 + quad;  // named barrier of the two warps of a quadrant
     int buf = 0;
     uint32_t acc_phase = 0;
@@ -492,8 +503,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint16_t* bias_g = side ? p.bias_v : p.bias_k;
       const bool rope = side == 0 && p.rope_cos != nullptr;
       const bool gain = side == 0 && p.qk_norm && p.k_gain != nullptr;
-      if (bias_g && lane < 16) cp_async16(wc + lane * 8, bias_g + head * 128 + lane * 8);
-      if (gain && lane >= 16) cp_async16(wc + 128 + (lane - 16) * 8, p.k_gain + (lane - 16) * 8);
+      // lanes 0-15: 8 bias values each, lanes 16-31: 8 gain values each,
+      // loaded now and widened into the warp's f32 constants after the wait
+      uint4 cw = make_uint4(0, 0, 0, 0);
+      const bool cw_bias = bias_g && lane < 16, cw_gain = gain && lane >= 16;
+      if (cw_bias) cw = __ldg(reinterpret_cast<const uint4*>(bias_g + head * 128 + lane * 8));
+      if (cw_gain) cw = __ldg(reinterpret_cast<const uint4*>(p.k_gain + (lane - 16) * 8));
       if (rope && row < p.M) {
         const float* src = (hh == 0 ? p.rope_cos : p.rope_sin) + row * 64;
 #pragma unroll
@@ -502,8 +517,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       cp_async_commit();
       const bool ok = mbar_wait(tfull_bar(buf), acc_phase, abort_flag, p.err);
       cp_async_wait_all();
-      // both tables of the quadrant's rows are in place (a barrier even on
-      // abort, so the partner warp is never left waiting)
+      if (cw_bias || cw_gain) {
+        float4* dst = reinterpret_cast<float4*>(wc + (cw_bias ? lane * 8 : 128 + (lane - 16) * 8));
+        dst[0] = make_float4(lo_f(cw.x), hi_f(cw.x), lo_f(cw.y), hi_f(cw.y));
+        dst[1] = make_float4(lo_f(cw.z), hi_f(cw.z), lo_f(cw.w), hi_f(cw.w));
+      }
+      // both tables of the quadrant's rows and the warp's constants are in
+      // place (a barrier even on abort, so the partner warp is never left
+      // waiting)
       asm volatile("bar.sync %0, 64;" ::"r"(pair_bar) : "memory");
       if (!ok) break;
       tc_fence_after();
