@@ -84,3 +84,16 @@ def test_product_matches_config1_golden(nkv, name):
             assert blob.size == want["bytes"]
             assert _sha(blob) == want["sha256"], f"layer {l} segment {pos} payload"
     bank.close()
+
+
+# ----------------------------------------------------- the commit producer
+def test_oracle_reproduces_project_golden(orc):
+    """The oracle's restatement of the captured K / V chain (+ quantize) still
+    gives the committed digests (tests/golden/make_project.py)."""
+    import make_project as mp
+
+    golden = json.load(open(os.path.join(os.path.dirname(__file__), "golden", "project_int8.json")))["cases"]
+    for case, want in golden.items():
+        _, got = mp.outputs(orc, case)
+        for name in ("k", "v", "kq", "vq", "ks", "vs"):
+            assert mp.digest(got[name]) == want[name], (case, name)
