@@ -449,3 +449,27 @@ def test_staged_commit_8b_geometry(nkv, orc):
     assert produced.metrics().as_dict() == fed.metrics().as_dict()
     produced.close()
     fed.close()
+
+
+def test_kernel_matches_project_golden(nkv, orc):
+    """The device producer on the golden fixture's inputs gives the committed
+    digests (tests/golden/project_int8.json)."""
+    import json
+    import os
+    import sys
+
+    here = os.path.dirname(os.path.abspath(__file__))
+    sys.path.insert(0, os.path.join(here, "golden"))
+    import make_project as mp
+
+    golden = json.load(open(os.path.join(here, "golden", "project_int8.json")))["cases"]
+    for case, want in golden.items():
+        c = mp.CASES[case]
+        a = mp.inputs(orc, c["M"], c["H"], c["seed"])
+        got = run(nkv, a, c["M"], c["H"], bias=c["bias"], norm=c["norm"], rope=c["rope"])
+        assert got["status"] == 0
+        M, H = c["M"], c["H"]
+        for name, arr in (("k", got["k"]), ("v", got["v"]), ("kq", got["k_codes"].reshape(1, M, H, D)),
+                          ("vq", got["v_codes"].reshape(1, M, H, D)), ("ks", got["k_scales"].reshape(1, M, H)),
+                          ("vs", got["v_scales"].reshape(1, M, H))):
+            assert mp.digest(arr) == want[name], (case, name)
