@@ -195,17 +195,52 @@ __global__ void __launch_bounds__(QB, 6) k_qvg_encode_d128(const QvgEncodeJob* _
       sm.dv[t] = active ? sm.ee[s][c] : 0.0;
       __syncthreads();
       if (t < 32) {
-        // warp 0: the block's sums in token order (qvg.rs:220-229) on lane 0.
-        // Idle tokens add +0, which leaves a sum started at +0 unchanged.
+        // warp 0: alpha = f32(num / den) of the block's sums in token order
+        // (qvg.rs:220-230); idle tokens add +0, which leaves a sum started at
+        // +0 unchanged.  The sums are first taken as a 64-term tree (depth 6)
+        // across the warp: a tree and the sequential order differ by at most
+        // (gamma_6 + gamma_63) sum|x| <= 2^-46 sum|x| (u = 2^-53), so the
+        // reference's quotient lies in an interval computed with outward
+        // rounding; when both ends round to the same f32 (and den > 1e-12 is
+        // certain either way) that is the reference's alpha.  Otherwise (a
+        // numerator interval around 0, non-finite terms, an f32 rounding
+        // boundary inside the interval) lane 0 takes the sequential sums.
+        const double n0 = sm.inner[2 * t], n1 = sm.inner[2 * t + 1];
+        const double d0 = sm.dv[2 * t], d1 = sm.dv[2 * t + 1];
+        double tn = __dadd_rn(n0, n1), an = __dadd_rn(fabs(n0), fabs(n1)), td = __dadd_rn(d0, d1);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          tn = __dadd_rn(tn, __shfl_xor_sync(0xFFFFFFFFu, tn, o));
+          an = __dadd_rn(an, __shfl_xor_sync(0xFFFFFFFFu, an, o));
+          td = __dadd_rn(td, __shfl_xor_sync(0xFFFFFFFFu, td, o));
+        }
         float alpha = 0.0f;
         if (t == 0) {
-          double num = 0.0, den = 0.0;
-#pragma unroll
-          for (int i = 0; i < QB; ++i) {
-            num = __dadd_rn(num, sm.inner[i]);
-            den = __dadd_rn(den, sm.dv[i]);
+          const double kTreeVsSeq = 0x1p-46;  // >= (gamma_6 + gamma_63) / (1 - gamma_6)
+          const double dn = __dmul_ru(an, kTreeVsSeq), dd = __dmul_ru(td, kTreeVsSeq);  // den terms are >= 0
+          const double nlo = __dsub_rd(tn, dn), nhi = __dadd_ru(tn, dn);
+          const double dlo = __dsub_rd(td, dd), dhi = __dadd_ru(td, dd);
+          bool sure = isfinite(nlo) && isfinite(nhi) && isfinite(dlo) && isfinite(dhi);
+          if (sure && dhi <= 1e-12) {
+            alpha = 1.0f;  // den <= 1e-12 for certain
+          } else if (sure && dlo > 1e-12 && (nlo > 0.0 || nhi < 0.0)) {
+            const double qlo = nlo > 0.0 ? __ddiv_rd(nlo, dhi) : __ddiv_rd(nlo, dlo);
+            const double qhi = nlo > 0.0 ? __ddiv_ru(nhi, dlo) : __ddiv_ru(nhi, dhi);
+            const float alo = __double2float_rn(qlo), ahi = __double2float_rn(qhi);
+            sure = alo == ahi;
+            alpha = alo;
+          } else {
+            sure = false;
           }
-          alpha = den > 1e-12 ? __double2float_rn(__ddiv_rn(num, den)) : 1.0f;  // qvg.rs:230
+          if (!sure) {
+            double num = 0.0, den = 0.0;
+#pragma unroll 1
+            for (int i = 0; i < QB; ++i) {
+              num = __dadd_rn(num, sm.inner[i]);
+              den = __dadd_rn(den, sm.dv[i]);
+            }
+            alpha = den > 1e-12 ? __double2float_rn(__ddiv_rn(num, den)) : 1.0f;  // qvg.rs:230
+          }
           J.scales[((size_t)h * n_blocks + blk) * stages + s] = alpha;
         }
         alpha = __shfl_sync(0xFFFFFFFFu, alpha, 0);
