@@ -136,6 +136,29 @@ def test_qvg_head_dim_128_fast_encoder_in_the_bank(H, input_dtype):
     p.close()
 
 
+def test_qvg_d128_block_sums_near_zero(H):
+    """Blocks whose numerator is exactly 0 or tiny and of either sign: the d128
+    encoder's fast block sum cannot certify alpha there and takes the
+    sequential sums (qvg.rs:220-230), which must still equal the oracle."""
+    p = _pair(H, "qvg", "uniform", past=4, model_dtype="bf16", input_dtype="bf16", heads=2, head_dim=128,
+              tpf=64, frames=3, text=4)
+
+    import oracle as orc
+
+    def flatten(layer, side, h):  # h: bf16 bit patterns (uint16)
+        if layer == 0:
+            h[0, 0:64] = 0                                  # a whole block of zero residuals: num = 0
+            h[0, 64:96] = 0                                 # half a block zero ...
+            tiny = orc.bf16_to_f32(h[0, 96:128]) * np.float32(1e-20)
+            h[0, 96:128] = orc.bf16_bits(tiny)              # ... the rest tiny
+            h[0, 128:192, :, 1::2] ^= np.uint16(0x8000)     # sign-mixed products
+
+    for _ in range(2):
+        assert p.commit(poison=flatten) is None
+        p.check()
+    p.close()
+
+
 def test_qvg_frozen_codebooks_and_partial_blocks(H):
     """Frozen synthetic codebooks (as in the QVG benchmark), a last block of
     fewer than 64 tokens, and the sigma_s = 1, .5, .25, .125 stage scales."""
