@@ -198,8 +198,11 @@ __global__ void __launch_bounds__(256) k_int8_quantize_bf16(const QuantJob* __re
           uint32_t c[16];
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
-            c[2 * j] = code_bits(__uint_as_float(ws[8 * k + j] << 16), s, rc);
-            c[2 * j + 1] = code_bits(__uint_as_float(ws[8 * k + j] & 0xFFFF0000u), s, rc);
+            const uint2 cc = code_bits2(
+                make_float2(__uint_as_float(ws[8 * k + j] << 16), __uint_as_float(ws[8 * k + j] & 0xFFFF0000u)), s,
+                rc);
+            c[2 * j] = cc.x;
+            c[2 * j + 1] = cc.y;
           }
           qo[k] = make_uint4(pack4(c[0], c[1], c[2], c[3]), pack4(c[4], c[5], c[6], c[7]),
                              pack4(c[8], c[9], c[10], c[11]), pack4(c[12], c[13], c[14], c[15]));

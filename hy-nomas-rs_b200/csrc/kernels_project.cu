@@ -345,8 +345,9 @@ __device__ __forceinline__ float quantize_row(const uint32_t (&w)[64], uint8_t* 
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const uint32_t a = w[8 * k + 2 * j], b = w[8 * k + 2 * j + 1];
-        c[j] = pack4(code_bits(lo_f(a), s, r), code_bits(hi_f(a), s, r), code_bits(lo_f(b), s, r),
-                     code_bits(hi_f(b), s, r));
+        const uint2 ca = code_bits2(make_float2(lo_f(a), hi_f(a)), s, r);
+        const uint2 cb = code_bits2(make_float2(lo_f(b), hi_f(b)), s, r);
+        c[j] = pack4(ca.x, ca.y, cb.x, cb.y);
       }
       qo[k] = make_uint4(c[0], c[1], c[2], c[3]);
     }

@@ -43,6 +43,23 @@ __device__ __forceinline__ uint32_t code_bits(float x, float s, float r) {
   return __float_as_uint(__fmaf_rn(copysignf(1.0f, x), n, M));   // M + sign(x) n, exact
 }
 
+// code_bits of two values at once on packed f32x2 operations: the same
+// roundings lane by lane (every step is a single add, multiply or fused
+// multiply-add, so nothing can be contracted across steps).
+__device__ __forceinline__ uint2 code_bits2(float2 x, float s, float r) {
+  const float2 M = make_float2(12582912.0f, 12582912.0f);  // 1.5 * 2^23
+  const float2 C = make_float2(0.49999997f, 0.49999997f);
+  const float2 s2 = make_float2(s, s), r2 = make_float2(r, r);
+  const float2 ax = make_float2(fabsf(x.x), fabsf(x.y));
+  const float2 q0 = __fmul2_rn(ax, r2);
+  const float2 e = __ffma2_rn(make_float2(-q0.x, -q0.y), s2, ax);
+  const float2 q1 = __ffma2_rn(e, r2, q0);                        // RN(|x| / s)
+  const float2 z = __fadd2_rz(__fadd2_rn(q1, C), M);              // M + n
+  const float2 n = __fadd2_rn(z, make_float2(-M.x, -M.y));        // n, exact
+  const float2 o = __ffma2_rn(make_float2(copysignf(1.0f, x.x), copysignf(1.0f, x.y)), n, M);
+  return make_uint2(__float_as_uint(o.x), __float_as_uint(o.y));
+}
+
 __device__ __forceinline__ uint32_t pack4(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410) ^ 0x80808080u;
 }
