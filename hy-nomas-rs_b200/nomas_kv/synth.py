@@ -157,3 +157,16 @@ def host_values(seed: int, key_sigma: float | None, B: int, L: int, H: int, D: i
     """numpy (B, L, H, D) raw-dtype array identical to DeviceGen.fill."""
     sc = chan_scale(seed, layer, H, D, key_sigma) if (side == 0 and key_sigma is not None) else None
     return values_numpy(B * L, H, D, stream_key(seed, layer, segment, side), dtype, sc).reshape(B, L, H, D)
+
+
+def qvg_codebooks(layer: int, heads: int = 24, head_dim: int = 128, stages: int = 4, entries: int = 4) -> np.ndarray:
+    """Frozen synthetic QVG codebooks of the 8B QVG configuration for one
+    layer: [side][head][stage][entry][head_dim] f32, codewords ~ N(0, sigma_s)
+    with sigma_s = 1, 0.5, 0.25, 0.125 for stages 0..3 (numpy seed
+    1000 + layer)."""
+    rng = np.random.default_rng(1000 + layer)
+    cb = np.zeros((2, heads, stages, entries, head_dim), np.float32)
+    for s in range(stages):
+        sig = 0.5 ** s
+        cb[:, :, s] = rng.standard_normal((2, heads, entries, head_dim)).astype(np.float32) * np.float32(sig)
+    return cb

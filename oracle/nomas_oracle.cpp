@@ -45,11 +45,45 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <exception>
 #include <limits>
 #include <memory>
 #include <string>
 #include <thread>
 #include <vector>
+
+// Worker threads the checker may use for work the reference does in an
+// independent loop (per head of a QVG encode/decode, per represented segment
+// of a rebuild).  Every iteration computes the same values in the same order
+// as the sequential loop, so results do not depend on it.  1 (the default,
+// used by the timed CPU baseline) keeps every loop sequential; tests raise it
+// to check the 8B geometry in seconds.
+static std::atomic<int> g_threads{1};
+static thread_local bool t_in_parallel = false;  // nested loops stay sequential
+
+template <typename F>
+static void parallel_for(size_t n, F&& fn) {
+  const size_t nt = t_in_parallel ? 1 : std::min<size_t>(size_t(std::max(1, g_threads.load())), n);
+  if (nt <= 1) {
+    for (size_t i = 0; i < n; ++i) fn(i);
+    return;
+  }
+  std::atomic<size_t> next{0};
+  std::vector<std::thread> th;
+  std::vector<std::exception_ptr> err(nt);
+  for (size_t t = 0; t < nt; ++t)
+    th.emplace_back([&, t]() {
+      t_in_parallel = true;
+      try {
+        for (size_t i = next++; i < n; i = next++) fn(i);
+      } catch (...) {
+        err[t] = std::current_exception();
+      }
+    });
+  for (auto& x : th) x.join();
+  for (auto& e : err)
+    if (e) std::rethrow_exception(e);
+}
 
 namespace orc {
 
@@ -228,7 +262,9 @@ static void randn(size_t n, uint64_t seed, double mean, double stdv, float* out)
 // cache/int8.rs:65-81 (quantize_one) over `rows` rows of D values.
 static void quantize_rows(const float* x, size_t rows, size_t D, uint8_t* q, float* s) {
   const float inv127 = float(1.0 / 127.0);
-  for (size_t r = 0; r < rows; ++r) {
+  constexpr size_t kChunk = 4096;  // rows are independent (one scale each)
+  parallel_for((rows + kChunk - 1) / kChunk, [&](size_t c) {
+  for (size_t r = c * kChunk; r < std::min(rows, (c + 1) * kChunk); ++r) {
     const float* xr = x + r * D;
     float peak = std::fabs(xr[0]);
     for (size_t d = 1; d < D; ++d) {
@@ -246,6 +282,7 @@ static void quantize_rows(const float* x, size_t rows, size_t D, uint8_t* q, flo
       q[r * D + d] = as_u8(t);
     }
   }
+  });
 }
 
 // cache/int8.rs:85-134 (quantize_kv_pair): non-finite scan of k, then v,
@@ -466,9 +503,9 @@ struct QvgCodec {
     size_t bpt = cfg.bpt(), E = cfg.entries();
     p.codes.assign(tokens * H * bpt, 0);
     p.scales.assign(H * p.n_blocks * cfg.stages, 0.0f);
-    std::vector<float> residual;
-    std::vector<size_t> codes;
-    for (size_t h = 0; h < H; ++h) {
+    parallel_for(H, [&](size_t h) {
+      std::vector<float> residual;
+      std::vector<size_t> codes;
       for (size_t b = 0; b < p.n_blocks; ++b) {
         size_t start = b * cfg.block, end = std::min((b + 1) * cfg.block, tokens);
         size_t n = end - start;
@@ -502,7 +539,7 @@ struct QvgCodec {
           }
         }
       }
-    }
+    });
     return p;
   }
 
@@ -511,7 +548,7 @@ struct QvgCodec {
     if (!fitted) fail(ERR_CACHE_STATE, "qvg codebooks not fitted");
     size_t bpt = cfg.bpt();
     std::fill(out, out + p.tokens * p.heads * p.head_dim, 0.0f);
-    for (size_t h = 0; h < p.heads; ++h)
+    parallel_for(p.heads, [&](size_t h) {
       for (size_t token = 0; token < p.tokens; ++token) {
         const uint8_t* base = p.codes.data() + (token * p.heads + h) * bpt;
         size_t b = token / cfg.block;
@@ -523,6 +560,7 @@ struct QvgCodec {
           for (size_t d = 0; d < p.head_dim; ++d) o[d] += alpha * e[d];
         }
       }
+    });
   }
 };
 
@@ -891,17 +929,20 @@ struct HistoryCache {  // history.rs:84-100 plus the phase_swap.rs:27-40 wrapper
       }
     }
     std::vector<Layout> layout;
-    std::vector<std::vector<float>> kp, vp;
-    std::vector<size_t> part_len;
-    size_t cursor = 0;
-    std::vector<float> dk, dv;
-    for (auto& [idx, sel] : selection) {
+    const size_t ns = selection.size();
+    std::vector<std::vector<float>> kp(ns), vp(ns);
+    std::vector<size_t> part_len(ns);
+    // per represented segment: decode the whole segment (the reference,
+    // history.rs:398), then index_select its selected frames and text
+    parallel_for(ns, [&](size_t p) {
+      const auto& [idx, sel] = selection[p];
       const Archived& a = archive[idx];
       std::vector<size_t> indices;
       for (size_t f : sel)
         for (size_t t = f * tpf; t < f * tpf + tpf; ++t) indices.push_back(t);
       for (size_t t = a.image_tokens; t < a.image_tokens + a.text_tokens; ++t) indices.push_back(t);
-      decode_segment(a, dk, dv);  // the reference decodes the whole segment (history.rs:398)
+      std::vector<float> dk, dv;
+      decode_segment(a, dk, dv);
       size_t HD = H * D, n = indices.size();
       std::vector<float> k(B * n * HD), v(B * n * HD);
       size_t Ld = dk.size() / (B * HD);
@@ -910,11 +951,15 @@ struct HistoryCache {  // history.rs:84-100 plus the phase_swap.rs:27-40 wrapper
           std::memcpy(&k[(b * n + j) * HD], &dk[(b * Ld + indices[j]) * HD], HD * 4);
           std::memcpy(&v[(b * n + j) * HD], &dv[(b * Ld + indices[j]) * HD], HD * 4);
         }
+      kp[p] = std::move(k), vp[p] = std::move(v), part_len[p] = n;
+    });
+    size_t cursor = 0;
+    for (const auto& [idx, sel] : selection) {
+      const Archived& a = archive[idx];
       size_t video_end = cursor + sel.size() * tpf;
       size_t text_end = video_end + a.text_tokens;
       layout.push_back({a.segment_index, cursor, video_end, video_end, text_end, a.action_start});
       cursor = text_end;
-      kp.push_back(std::move(k)), vp.push_back(std::move(v)), part_len.push_back(n);
     }
     if (cursor > capacity_or_max())
       fail(ERR_GEOMETRY, "history needs " + std::to_string(cursor) + " tokens; capacity is " +
@@ -1039,6 +1084,8 @@ typedef struct {
 } orc_metrics;
 
 const char* orc_last_error(void) { return g_last_error.c_str(); }
+// Worker threads for the checker's independent loops (1 = sequential).
+void orc_set_threads(int32_t n) { g_threads = n < 1 ? 1 : n; }
 
 #define ORC_TRY(...)                          \
   try {                                       \

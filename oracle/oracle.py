@@ -122,6 +122,7 @@ def lib():
         _lib.orc_bank_create.argtypes = [
             C.POINTER(OrcConfig), C.c_uint64, C.c_uint64, C.c_uint64, C.c_uint64, C.c_int32, C.POINTER(C.c_void_p)]
         _lib.orc_bank_destroy.argtypes = [C.c_void_p]
+        _lib.orc_set_threads.argtypes = [C.c_int32]
         _lib.orc_bank_commit.argtypes = [
             C.c_void_p, C.POINTER(OrcSegment), C.c_int32, C.POINTER(C.c_void_p), C.POINTER(C.c_void_p), C.c_int32]
         for name in ("orc_bank_rollback", "orc_bank_park", "orc_bank_unpark"):
@@ -152,6 +153,13 @@ def lib():
         _lib.orc_kv_project.argtypes = [C.c_void_p] * 6 + [C.c_int32, C.c_float, C.c_void_p, C.c_void_p] + [
             C.c_uint64] * 3 + [C.c_void_p] * 2
     return _lib
+
+
+def set_threads(n: int) -> None:
+    """Worker threads for the checker's independent loops (QVG heads, the
+    segments a rebuild decodes); 1 keeps everything sequential.  Results do
+    not depend on it."""
+    lib().orc_set_threads(int(n))
 
 
 def _check(rc: int):

@@ -88,9 +88,14 @@ def torch_to_raw(t) -> np.ndarray:
 class Pair:
     """One oracle bank and one GPU bank with the same configuration."""
 
-    def __init__(self, geo: Geometry, spec: Spec, device="cuda:0"):
+    def __init__(self, geo: Geometry, spec: Spec, device="cuda:0", host_from_device: bool = False):
+        """host_from_device: the oracle's inputs are the device generator's
+        tensors copied back (the same bits as synth.host_values, whose
+        equality with the device generator is tested on its own), which is
+        far faster than the numpy generator at the 8B geometry."""
         import torch
         self.torch = torch
+        self.host_from_device = host_from_device
         self.geo, self.spec = geo, spec
         self.mdt_p, self.mdt_o = DT[geo.model_dtype]
         self.idt_p, self.idt_o = DT[geo.input_dtype]
@@ -121,13 +126,19 @@ class Pair:
         kd, vd, kh, vh = [], [], [], []
         for layer in range(g.n_layers):
             for side, (dl, hl) in enumerate(((kd, kh), (vd, vh))):
-                h = synth.host_values(g.seed, g.key_sigma, g.batch, L, g.heads, g.head_dim, layer, segment, side,
-                                      self.idt_p)
+                h = None
+                if poison is not None or not self.host_from_device:
+                    h = synth.host_values(g.seed, g.key_sigma, g.batch, L, g.heads, g.head_dim, layer, segment,
+                                          side, self.idt_p)
                 if poison is not None:
                     h = h.copy()
                     poison(layer, side, h)
                     t = torch.from_numpy(h.view(np.int16) if h.dtype == np.uint16 else h).to(self.device)
                     t = t.view(tdt) if h.dtype == np.uint16 else t
+                elif self.host_from_device:
+                    t = torch.empty((g.batch, L, g.heads, g.head_dim), dtype=tdt, device=self.device)
+                    self.gen.fill(t, layer, segment, side, self.idt_p)
+                    h = torch_to_raw(t)
                 else:
                     t = torch.empty((g.batch, L, g.heads, g.head_dim), dtype=tdt, device=self.device)
                     self.gen.fill(t, layer, segment, side, self.idt_p)
