@@ -15,7 +15,13 @@ semantics).  Layers are sharded contiguously across ranks (48/N each).
 
 Prints one JSON line (rank 0).  `value` is device-timed with inputs resident
 in HBM; `e2e` repeats the step with the K/V coming from pinned host memory
-inside the timed region.  `--impl reference` times the CPU restatement of the
+inside the timed region.  The banks are ShardedKvBanks: every turn carries
+the per-turn NCCL broadcast of the 1 KB turn record and the status
+all-reduce.  After the INT8 headline the same run adds, in the same
+process, one park + unpark of the working set (phase swap, against the
+measured pinned copy bandwidth), a short QVG turn (config 3) and a short
+turn with the fused K/V producer against the unfused chain (`--no-extras`
+skips them).  `--impl reference` times the CPU restatement of the
 reference cache path (oracle/, the reference itself is Rust and cannot be
 built here) on the host cores with the same metric.
 """
@@ -86,14 +92,9 @@ def step_bytes(n_layers: int, workload: str = "int8", swap: bool = False) -> dic
 
 
 def qvg_codebooks(layer: int):
-    """Frozen synthetic codebooks of the QVG configuration: per (layer, side,
-    head, stage) 4 codewords x 128 dims ~ N(0, sigma_s), sigma = 1, .5, .25, .125."""
-    import numpy as np
-    rng = np.random.default_rng(1000 + layer)
-    cb = np.zeros((2, HEADS, 4, 4, HEAD_DIM), np.float32)
-    for s, sig in enumerate((1.0, 0.5, 0.25, 0.125)):
-        cb[:, :, s] = rng.standard_normal((2, HEADS, 4, HEAD_DIM)).astype(np.float32) * np.float32(sig)
-    return cb
+    """Frozen synthetic codebooks of the QVG configuration (nomas_kv.synth)."""
+    from nomas_kv import synth
+    return synth.qvg_codebooks(layer, HEADS, HEAD_DIM)
 
 
 def load_peaks() -> dict:
@@ -306,11 +307,9 @@ def host_policy_latency(reps: int = 2000) -> dict:
 
 
 # ------------------------------------------------------------ GPU side
-def run_gpu(args) -> None:
+def _dist_setup(args):
     import torch
     import torch.distributed as dist
-    import nomas_kv as nk
-    from nomas_kv import synth
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -322,120 +321,250 @@ def run_gpu(args) -> None:
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    return world, rank, local, dev
 
-    model_layers = args.layers
-    begin, n_layers = nk.partition_layers(model_layers, world, rank)
-    stream = torch.cuda.current_stream(dev)
+
+def _max_over_ranks(world: int, dev, values: list[float]) -> list[float]:
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor(values, dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return [float(x) for x in t.tolist()]
+
+
+def _barrier(world: int) -> None:
+    import torch
+    import torch.distributed as dist
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def host_link_peaks(world: int, dev, nbytes: int = 1 << 30, reps: int = 3) -> dict:
+    """Pinned host <-> device copy bandwidth with every rank copying at the
+    same time (the bound of the e2e figure and of park / unpark): per GPU,
+    and aggregated over the job (bytes of all ranks / the slowest rank)."""
+    import torch
+    host = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+    devb = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    s = torch.cuda.current_stream(dev)
+    out = {}
+    for name, fn in (("h2d", lambda: devb.copy_(host, non_blocking=True)),
+                     ("d2h", lambda: host.copy_(devb, non_blocking=True))):
+        best = float("inf")
+        for _ in range(reps):
+            _barrier(world)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(s)
+            fn()
+            b.record(s)
+            b.synchronize()
+            best = min(best, a.elapsed_time(b))
+        ms = _max_over_ranks(world, dev, [best])[0]
+        out[f"{name}_gbs_per_gpu"] = round(nbytes / (best / 1e3) / 1e9, 2)
+        out[f"{name}_gbs_aggregate"] = round(world * nbytes / (ms / 1e3) / 1e9, 2)
+    del host, devb
+    torch.cuda.empty_cache()
+    out["what"] = f"pinned {nbytes >> 20} MiB copies, all {world} rank(s) at once, best of {reps}"
+    return out
+
+
+class Turns:
+    """One cache workload at the 8B geometry on this rank's layers, driven
+    through the layer-sharded bank (its per-turn NCCL record broadcast and
+    status exchange included): prefill, warm-up and timed turns (commit +
+    rebuild + newest-segment decode), kernel statistics."""
+
+    def __init__(self, args, world, rank, dev, workload: str, phase_swap: bool, archived: int,
+                 max_turns: int):
+        import torch
+        import nomas_kv as nk
+        from nomas_kv import synth
+        from nomas_kv.sharded import ShardedKvBank
+
+        self.torch, self.nk = torch, nk
+        self.world, self.rank, self.dev, self.wl = world, rank, dev, workload
+        self.model_layers = args.layers
+        storage = nk.CacheStorage.qvg_() if workload == "qvg" else nk.CacheStorage.int8()
+        cfg = nk.CacheConfig(storage=storage, sampling=nk.HistorySampling.uniform(), past_frames=PAST,
+                             phase_swap=phase_swap)
+        self.sb = ShardedKvBank(cfg, args.layers, 1, HEADS, HEAD_DIM, torch.bfloat16, device=dev, verify=True)
+        self.bank = self.sb.local
+        self.begin, self.n_layers = self.sb.begin, self.sb.count
+        self.stream = torch.cuda.current_stream(dev)
+        if workload == "qvg":
+            for i in range(self.n_layers):
+                self.bank.layer(i).set_qvg_codebooks(synth.qvg_codebooks(self.begin + i, HEADS, HEAD_DIM))
+        self.prefill = max(1, archived - 1 - args.warmup)
+        self.bank.reserve(self.bank.segment_bytes(self.desc(0)) * self.n_layers * (self.prefill + max_turns),
+                          rebuild_tokens())
+        # two resident input sets (each > L2), alternated turn to turn
+        gen = synth.DeviceGen(dev, seed=0, key_sigma=1.0)
+        self.shape = (1, SEG_TOKENS, HEADS, HEAD_DIM)
+        self.sets = []
+        for s in range(2):
+            ks = [torch.empty(self.shape, dtype=torch.bfloat16, device=dev) for _ in range(self.n_layers)]
+            vs = [torch.empty(self.shape, dtype=torch.bfloat16, device=dev) for _ in range(self.n_layers)]
+            for i in range(self.n_layers):
+                gen.fill(ks[i], self.begin + i, s, 0, nk.NKV_BF16)
+                gen.fill(vs[i], self.begin + i, s, 1, nk.NKV_BF16)
+            self.sets.append((ks, vs))
+        self.recent_k = [torch.empty(self.shape, dtype=torch.bfloat16, device=dev) for _ in range(self.n_layers)]
+        self.recent_v = [torch.empty(self.shape, dtype=torch.bfloat16, device=dev) for _ in range(self.n_layers)]
+        self.seg = 0
+
+    def desc(self, i: int):
+        return self.nk._abi.nkv_segment_desc(i, i * FRAMES, FRAMES, FRAMES * TPF, TEXT, 0)
+
+    def turn(self, ks=None, vs=None):
+        if ks is None:
+            ks, vs = self.sets[self.seg % 2]
+        self.sb.commit(self.desc(self.seg), ks, vs)  # validate + encode + rebuild (one host wait for the flags)
+        self.bank.decode_segment(self.seg, self.recent_k, self.recent_v)  # the newest segment in full
+        self.seg += 1
+
+    def fill_archive(self, warmup: int):
+        for _ in range(self.prefill + warmup):
+            self.turn()
+        assert self.bank.layer(0).valid_len() == rebuild_tokens(), self.bank.layer(0).valid_len()
+
+    def timed(self, steps: int):
+        """Device time of `steps` turns (max over ranks) and the kernel stats."""
+        torch = self.torch
+        self.bank.kernel_stats(reset=True)
+        self.bank.set_timing(True)
+        _barrier(self.world)
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(self.stream)
+        for _ in range(steps):
+            self.turn()
+        t1.record(self.stream)
+        torch.cuda.synchronize()
+        _barrier(self.world)
+        self.bank.set_timing(False)
+        kst = self.bank.kernel_stats(reset=True)
+        return _max_over_ranks(self.world, self.dev, [t0.elapsed_time(t1)])[0], kst
+
+    def kernel_figures(self, kst: dict, steps: int, peak: float) -> dict:
+        """Achieved GB/s of the turn's kernels on this rank (CUDA events on
+        the bank's stream around each launch), algorithmic bytes per launch."""
+        sb = step_bytes(self.n_layers, self.wl)
+        g_launch, g_ms = kst["gather"]
+        d_launch, d_ms = kst["segment_decode"]
+        q_launch, q_ms = kst["quantize"]
+        e_launch, e_ms = kst["qvg_encode"]
+        gbs = lambda b, ms: b / (ms / 1e3) / 1e9 if ms > 0 else None  # noqa: E731
+        out = {"rebuild_gather_gbs": gbs(sb["rebuild"] * steps, g_ms), "segment_decode_gbs": gbs(sb["recent"] * steps, d_ms)}
+        if self.wl == "qvg":
+            out["qvg_encode_gbs"] = gbs(FRAMES * TPF * QVG_BYTES_PER_VIDEO_TOKEN * self.n_layers * steps, e_ms)
+            out["text_quantize_gbs"] = gbs(TEXT * BYTES_PER_TOKEN * self.n_layers * steps, q_ms)
+        else:
+            out["quantize_gbs"] = gbs(sb["commit"] * steps, q_ms)
+        res = {}
+        for k, v in out.items():
+            res[k] = round(v, 1) if v else None
+            res[k.replace("_gbs", "_frac")] = round(v / peak, 4) if v else None
+        res["launches"] = g_launch + d_launch + q_launch + e_launch
+        res["rebuild_gather_ms_per_launch"] = round(g_ms / max(g_launch, 1), 4)
+        return res
+
+    def close(self):
+        self.bank.close()
+        self.sets = self.recent_k = self.recent_v = None
+        self.torch.cuda.synchronize()
+        self.torch.cuda.empty_cache()
+
+
+def run_gpu(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    world, rank, local, dev = _dist_setup(args)
     wl = args.workload
-    storage = nk.CacheStorage.qvg_() if wl == "qvg" else nk.CacheStorage.int8()
     swap = args.swap
-    cfg = nk.CacheConfig(storage=storage, sampling=nk.HistorySampling.uniform(), past_frames=PAST, phase_swap=swap)
-    bank = nk.KvBank(cfg, n_layers, 1, HEADS, HEAD_DIM, torch.bfloat16, device=dev, layer_begin=begin)
-    if wl == "qvg":
-        for i in range(n_layers):
-            bank.layer(i).set_qvg_codebooks(qvg_codebooks(begin + i))
-    gen = synth.DeviceGen(dev, seed=0, key_sigma=1.0)
-    desc = lambda i: nk._abi.nkv_segment_desc(i, i * FRAMES, FRAMES, FRAMES * TPF, TEXT, 0)  # noqa: E731
+    model_layers = args.layers
+    peaks = load_peaks()
+    extras = wl == "int8" and not swap and not args.no_extras
 
     # the swap run holds a 64-segment archive (~142 GB at 48 layers on one
     # GPU): fewer e2e turns, and the e2e staging reuses a resident input set
     e2e_steps = min(args.steps, 2 if swap else 4)
-    prefill = max(1, (ARCHIVED_SWAP if swap else ARCHIVED) - 1 - args.warmup)
-    total_segments = prefill + args.warmup + args.steps + args.warmup + e2e_steps
-    bank.reserve(bank.segment_bytes(desc(0)) * n_layers * total_segments, rebuild_tokens())
-
-    # two resident input sets (each > L2), alternated step to step
-    shape = (1, SEG_TOKENS, HEADS, HEAD_DIM)
-    sets = []
-    for s in range(2):
-        ks = [torch.empty(shape, dtype=torch.bfloat16, device=dev) for _ in range(n_layers)]
-        vs = [torch.empty(shape, dtype=torch.bfloat16, device=dev) for _ in range(n_layers)]
-        for i in range(n_layers):
-            gen.fill(ks[i], begin + i, s, 0, nk.NKV_BF16)
-            gen.fill(vs[i], begin + i, s, 1, nk.NKV_BF16)
-        sets.append((ks, vs))
-    recent_k = [torch.empty(shape, dtype=torch.bfloat16, device=dev) for _ in range(n_layers)]
-    recent_v = [torch.empty(shape, dtype=torch.bfloat16, device=dev) for _ in range(n_layers)]
-
-    seg = 0
+    archived = ARCHIVED_SWAP if swap else ARCHIVED
+    # the INT8 headline bank is a phase-swapped cache (PhaseSwappedCache,
+    # phase_swap.rs:27-161) so that one park + unpark can be timed after the
+    # timed turns; while not parked its turns are the plain HistoryCache's
+    T = Turns(args, world, rank, dev, wl, phase_swap=swap or extras, archived=archived,
+              max_turns=2 * args.warmup + args.steps + e2e_steps + 1)
+    n_layers, stream = T.n_layers, T.stream
     swap_ms = [0.0, 0.0]  # park, unpark: device time on the bank's stream
     sev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
 
-    def step(ks, vs, swap_now=True):
-        nonlocal seg
-        bank.commit_tensors(desc(seg), ks, vs)  # validate + quantize + rebuild (one sync for the error flag)
-        bank.decode_segment(seg, recent_k, recent_v)  # the newest archived segment in full
-        seg += 1
-        if swap and swap_now:
-            # phase_swap.rs:42-92: the working set goes to host memory and back;
-            # both calls return after their copies completed
-            sev[0].record(stream)
-            bank.park_all()
-            sev[1].record(stream)
-            bank.unpark_all()
-            sev[2].record(stream)
-            sev[2].synchronize()
-            swap_ms[0] += sev[0].elapsed_time(sev[1])
-            swap_ms[1] += sev[1].elapsed_time(sev[2])
+    def park_unpark():
+        # phase_swap.rs:42-92: the working set goes to host memory and back;
+        # both calls return after their copies completed
+        sev[0].record(stream)
+        T.sb.park_all()
+        sev[1].record(stream)
+        T.sb.unpark_all()
+        sev[2].record(stream)
+        sev[2].synchronize()
+        swap_ms[0] += sev[0].elapsed_time(sev[1])
+        swap_ms[1] += sev[1].elapsed_time(sev[2])
+
+    def step():
+        T.turn()
+        if swap:
+            park_unpark()
 
     # the prefill only builds the archive: no swaps while the working set is
     # still growing (a re-grown set would briefly coexist with its successor)
-    for _ in range(prefill):
-        step(*sets[seg % 2], swap_now=False)
+    T.fill_archive(0)
     for _ in range(args.warmup):
-        step(*sets[seg % 2])
-    assert bank.layer(0).valid_len() == rebuild_tokens(), bank.layer(0).valid_len()
+        step()
     torch.cuda.synchronize()
 
     # ---------------------------------------------------- timed: resident
     clocks = ClockSampler(local)
-    bank.kernel_stats(reset=True)
-    bank.set_timing(True)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
+    T.bank.kernel_stats(reset=True)
+    T.bank.set_timing(True)
+    _barrier(world)
     clocks.start()
     swap_ms[0] = swap_ms[1] = 0.0
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     t0.record(stream)
     for _ in range(args.steps):
-        step(*sets[seg % 2])
+        step()
     t1.record(stream)
     torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
+    _barrier(world)
     clk = clocks.stop()
-    bank.set_timing(False)
-    kst = bank.kernel_stats(reset=True)
-    ms = t0.elapsed_time(t1)
-    ms_t = torch.tensor([ms], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
-    ms_max = float(ms_t.item())
+    T.bank.set_timing(False)
+    kst = T.bank.kernel_stats(reset=True)
+    ms_max = _max_over_ranks(world, dev, [t0.elapsed_time(t1)])[0]
     bytes_all = step_bytes(model_layers, wl, swap)["total"] * args.steps
     value = bytes_all / (ms_max / 1e3) / 1e9
+    link = host_link_peaks(world, dev)
     swap_info = None
     if swap:
         wsb = working_set_bytes(n_layers) * args.steps
-        pt = torch.tensor(swap_ms, dtype=torch.float64, device=dev)
-        if world > 1:
-            dist.all_reduce(pt, op=dist.ReduceOp.MAX)
+        pt = _max_over_ranks(world, dev, swap_ms)
         swap_info = {"bytes_per_direction_per_step": working_set_bytes(model_layers),
-                     "park_gbs_per_gpu": round(wsb / (float(pt[0]) / 1e3) / 1e9, 2),
-                     "unpark_gbs_per_gpu": round(wsb / (float(pt[1]) / 1e3) / 1e9, 2),
-                     "park_ms_per_step": round(float(pt[0]) / args.steps, 3),
-                     "unpark_ms_per_step": round(float(pt[1]) / args.steps, 3),
-                     "bound": "host link (PCIe), per GPU"}
+                     "park_gbs_per_gpu": round(wsb / (pt[0] / 1e3) / 1e9, 2),
+                     "unpark_gbs_per_gpu": round(wsb / (pt[1] / 1e3) / 1e9, 2),
+                     "park_ms_per_step": round(pt[0] / args.steps, 3),
+                     "unpark_ms_per_step": round(pt[1] / args.steps, 3),
+                     "bound": "host link (PCIe), per GPU", "link": link}
 
     # ---------------------------------------------------- timed: e2e (host buffers)
     host = []
     for s in range(2):
-        hk = [torch.empty(shape, dtype=torch.bfloat16, pin_memory=True) for _ in range(n_layers)]
-        hv = [torch.empty(shape, dtype=torch.bfloat16, pin_memory=True) for _ in range(n_layers)]
+        hk = [torch.empty(T.shape, dtype=torch.bfloat16, pin_memory=True) for _ in range(n_layers)]
+        hv = [torch.empty(T.shape, dtype=torch.bfloat16, pin_memory=True) for _ in range(n_layers)]
         for i in range(n_layers):
-            hk[i].copy_(sets[s][0][i])
-            hv[i].copy_(sets[s][1][i])
+            hk[i].copy_(T.sets[s][0][i])
+            hv[i].copy_(T.sets[s][1][i])
         host.append((hk, hv))
     # Pipelined turns: turn j+1's K/V cross PCIe on a copy stream (into the
     # other resident input set, free again) while turn j commits; commit
@@ -446,12 +575,12 @@ def run_gpu(args) -> None:
     copied = [torch.cuda.Event(), torch.cuda.Event()]
 
     def enqueue_copy(j: int, b: int):
-        hk, hv = host[(seg + j) % 2]
+        hk, hv = host[(T.seg + j) % 2]
         copy_stream.wait_stream(stream)  # after the last reader of buffer b
         with torch.cuda.stream(copy_stream):
             for i in range(n_layers):
-                sets[b][0][i].copy_(hk[i], non_blocking=True)
-                sets[b][1][i].copy_(hv[i], non_blocking=True)
+                T.sets[b][0][i].copy_(hk[i], non_blocking=True)
+                T.sets[b][1][i].copy_(hv[i], non_blocking=True)
         copied[b].record(copy_stream)
 
     def e2e_turns(n_turns: int):
@@ -461,51 +590,56 @@ def run_gpu(args) -> None:
             if j + 1 < n_turns:
                 enqueue_copy(j + 1, 1 - b)
             stream.wait_event(copied[b])
-            step(*sets[b])
+            T.turn(*T.sets[b])
+            if swap:
+                park_unpark()
             # device -> host read of the turn's result: the working-set length
-            vlen_dev.fill_(bank.layer(0).valid_len())
+            vlen_dev.fill_(T.bank.layer(0).valid_len())
             flag_host.copy_(vlen_dev, non_blocking=True)
 
     e2e_turns(args.warmup)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
+    _barrier(world)
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     e2e_turns(e2e_steps)
     e1.record(stream)
     torch.cuda.synchronize()
-    ems = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(ems, op=dist.ReduceOp.MAX)
-    e2e_value = step_bytes(model_layers, wl, swap)["total"] * e2e_steps / (float(ems.item()) / 1e3) / 1e9
+    ems = _max_over_ranks(world, dev, [e0.elapsed_time(e1)])[0]
+    e2e_value = step_bytes(model_layers, wl, swap)["total"] * e2e_steps / (ems / 1e3) / 1e9
     h2d = 2 * SEG_TOKENS * HEADS * HEAD_DIM * 2 * model_layers
     d2h = (4 + 4) * world  # commit's non-finite flag + the result read, per rank
+    # the e2e ceiling when only the K/V upload bounded a turn
+    e2e_bound = step_bytes(model_layers, wl, swap)["total"] / (h2d / (link["h2d_gbs_aggregate"] * 1e9)) / 1e9
+
+    # ---------------------------------------------------- one park + unpark (phase swap)
+    if extras:
+        swap_ms[0] = swap_ms[1] = 0.0
+        _barrier(world)
+        park_unpark()  # first one allocates the pinned host buffers
+        swap_ms[0] = swap_ms[1] = 0.0
+        _barrier(world)
+        park_unpark()
+        pt = _max_over_ranks(world, dev, swap_ms)
+        wsb = working_set_bytes(n_layers)
+        swap_info = {"bytes_per_direction": working_set_bytes(model_layers),
+                     "park_gbs_per_gpu": round(wsb / (pt[0] / 1e3) / 1e9, 2),
+                     "unpark_gbs_per_gpu": round(wsb / (pt[1] / 1e3) / 1e9, 2),
+                     "park_ms": round(pt[0], 3), "unpark_ms": round(pt[1], 3),
+                     "park_frac": round(wsb / (pt[0] / 1e3) / 1e9 / link["d2h_gbs_per_gpu"], 4),
+                     "unpark_frac": round(wsb / (pt[1] / 1e3) / 1e9 / link["h2d_gbs_per_gpu"], 4),
+                     "bound": "host link: fractions of the measured pinned copy bandwidth per GPU with every rank "
+                              "copying at once", "link": link}
+    gk = T.kernel_figures(kst, args.steps, peaks["hbm_gbs"])
+    T.close()
+    del host
+
+    qvg = project = None
+    if extras:
+        qvg = run_qvg_extra(args, world, rank, dev, peaks)
+        project = project_measure(args, world, rank, dev, peaks, steps=3, warmup=3, e2e_steps=0, cpu=False)
 
     # ---------------------------------------------------- roofline (gather)
-    peaks = load_peaks()
-    # the dominant launch is the rebuild gather of each commit; the newest-
-    # segment decode runs the same kernel and is reported beside it
-    g_launch, g_ms = kst["gather"]
-    d_launch, d_ms = kst["segment_decode"]
-    q_launch, q_ms = kst["quantize"]
-    e_launch, e_ms = kst["qvg_encode"]
-    sb = step_bytes(n_layers, wl)
-    gather_bytes = sb["rebuild"] * args.steps
-    gather_gbs = gather_bytes / (g_ms / 1e3) / 1e9 if g_ms > 0 else None
-    dec_gbs = sb["recent"] * args.steps / (d_ms / 1e3) / 1e9 if d_ms > 0 else None
-    if wl == "qvg":
-        enc_bytes = FRAMES * TPF * QVG_BYTES_PER_VIDEO_TOKEN * n_layers * args.steps
-        txt_bytes = TEXT * BYTES_PER_TOKEN * n_layers * args.steps
-        quant_gbs = txt_bytes / (q_ms / 1e3) / 1e9 if q_ms > 0 else None
-        enc_gbs = enc_bytes / (e_ms / 1e3) / 1e9 if e_ms > 0 else None
-    else:
-        quant_gbs = sb["commit"] * args.steps / (q_ms / 1e3) / 1e9 if q_ms > 0 else None
-        enc_gbs = None
-    launches = g_launch + d_launch + q_launch + e_launch
-    # DRAM bytes of one rebuild-gather launch, from an ncu capture of the
-    # same kernel (scaled from the captured layer count to this one)
     traffic = None
     tp = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(tp):
@@ -515,11 +649,13 @@ def run_gpu(args) -> None:
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
+        cores = min(os.cpu_count() or 1, LAYERS)
         try:
-            cpu = cpu_sample(min(os.cpu_count() or 1, 8), workload=wl, swap=swap)
+            cpu = cpu_sample(cores, workload=wl, swap=swap)
             one = cpu_sample(1, workload=wl, swap=swap)
             cpu["single_thread_value"] = one["value"]
             cpu["single_thread_sample"] = one["sample"]
+            cpu["host_nproc"] = os.cpu_count()
         except Exception as e:  # noqa: BLE001
             cpu = {"value": None, "unit": "GB/s", "cores": 0, "kind": "port", "sample": f"failed: {e}"}
     sec = ms_max / 1e3
@@ -527,6 +663,7 @@ def run_gpu(args) -> None:
            "newest_segment_out": round(SEG_TOKENS * args.steps / sec), "unit": "segment tokens/s (all layers)"}
 
     if rank == 0:
+        sbytes = step_bytes(n_layers, wl)
         out = {
             "metric": (METRIC_SWAP.format(wl.upper()) if swap else METRIC if wl == "int8" else METRIC_QVG),
             "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
@@ -535,36 +672,59 @@ def run_gpu(args) -> None:
             "config": {"workload": WORKLOADS[wl] + (" + park/unpark (phase swap) every turn" if swap else ""),
                        "layers": model_layers, "heads": HEADS, "head_dim": HEAD_DIM, "segment_tokens": SEG_TOKENS,
                        "tokens_per_frame": TPF, "frames_per_segment": FRAMES, "text_tokens": TEXT,
-                       "past_frames": PAST, "archived_segments_at_first_timed_step": prefill + args.warmup + 1,
+                       "past_frames": PAST, "archived_segments_at_first_timed_step": T.prefill + args.warmup + 1,
                        "phase_swap": swap,
                        "working_set_tokens": rebuild_tokens(), "bytes_per_step": step_bytes(model_layers, wl, swap)["total"],
-                       "parallelism": f"layer-sharded x{world}", "l2": "inputs 3.8 GB per step > 126 MB L2"},
+                       "parallelism": f"layer-sharded x{world} (ShardedKvBank: per-turn NCCL broadcast of the "
+                                      f"1 KB turn record + status all-reduce, no data-path collective)",
+                       "l2": "inputs 3.8 GB per step > 126 MB L2"},
             "tokens_per_s": tok,
             "host_policy_latency": host_policy_latency(),
             "phase_swap": swap_info,
-            "roofline": {"bound": "hbm", "achieved": round(gather_gbs, 1) if gather_gbs else None,
+            "roofline": {"bound": "hbm", "achieved": gk["rebuild_gather_gbs"],
                          "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                         "frac": round(gather_gbs / peaks["hbm_gbs"], 4) if gather_gbs else None,
+                         "frac": gk["rebuild_gather_frac"],
                          "traffic": traffic, "kernel": "k_gather (rebuild launch of each commit)",
-                         "algorithmic_bytes_per_launch": sb["rebuild"],
-                         "peak_src": peaks["src"], "launches": g_launch,
-                         "segment_decode_gbs": round(dec_gbs, 1) if dec_gbs else None,
-                         "segment_decode_frac": round(dec_gbs / peaks["hbm_gbs"], 4) if dec_gbs else None,
-                         "quantize_gbs": round(quant_gbs, 1) if quant_gbs else None,
-                         "quantize_frac": round(quant_gbs / peaks["hbm_gbs"], 4) if quant_gbs else None,
-                         "qvg_encode_gbs": round(enc_gbs, 1) if enc_gbs else None,
-                         "qvg_encode_frac": round(enc_gbs / peaks["hbm_gbs"], 4) if enc_gbs else None},
+                         "algorithmic_bytes_per_launch": sbytes["rebuild"],
+                         "peak_src": peaks["src"], **{k: v for k, v in gk.items()
+                                                      if k not in ("rebuild_gather_gbs", "rebuild_gather_frac")}},
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h, "steps": e2e_steps},
-            "gpu_launches": launches,
+                    "d2h_bytes_per_step": d2h, "steps": e2e_steps,
+                    "result": "the rebuilt working set stays in HBM, where attention reads it; the device-to-host "
+                              "read per turn is the commit's status word and the working-set length",
+                    "bound_gbs": round(e2e_bound, 1),
+                    "bound": f"the K/V upload: {h2d / 1e9:.2f} GB per turn at the measured aggregate pinned H2D "
+                             f"{link['h2d_gbs_aggregate']} GB/s with all {world} GPU(s) copying at once"},
+            "qvg": qvg,
+            "producer": project,
+            "gpu_launches": gk["launches"],
             "clocks": clk,
             "cpu_baseline": cpu,
         }
         print(json.dumps(out), flush=True)
-    bank.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def run_qvg_extra(args, world, rank, dev, peaks, steps: int = 3, warmup: int = 3) -> dict:
+    """A short QVG turn (config 3: frozen codebooks, 98-block video encode,
+    INT8 text, uniform decode-gather rebuild of 16 frames, newest segment)
+    after the INT8 bank is closed."""
+    import torch
+    T = Turns(args, world, rank, dev, "qvg", phase_swap=False, archived=PAST + 1 + warmup,
+              max_turns=warmup + steps + 1)
+    T.fill_archive(warmup)
+    ms, kst = T.timed(steps)
+    gk = T.kernel_figures(kst, steps, peaks["hbm_gbs"])
+    T.close()
+    del T
+    torch.cuda.empty_cache()
+    total = step_bytes(args.layers, "qvg")["total"]
+    return {"metric": METRIC_QVG, "value": round(total * steps / (ms / 1e3) / 1e9, 2), "unit": "GB/s",
+            "ms_per_step": round(ms / steps, 4), "steps": steps, "warmup": warmup,
+            "archived_segments": PAST + 1 + warmup, "peak": peaks["hbm_gbs"], "peak_src": peaks["src"],
+            "gpu_launches": gk.pop("launches"), **gk}
 
 
 # ------------------------------------------------- producer (projection)
@@ -573,7 +733,8 @@ DIM = HEADS * HEAD_DIM  # 3072
 PROJECT_FLOPS = 2 * SEG_TOKENS * (2 * DIM) * DIM  # one layer's K and V projection of a segment
 
 
-def run_project(args) -> None:
+def project_measure(args, world, rank, dev, peaks, steps: int, warmup: int, e2e_steps: int, cpu: bool,
+                    archived: int = PAST + 1) -> dict:
     """The commit with its producer: per layer, the K / V projection of the
     segment's attention input (Lin + bias, RmsNorm and RoPE on K) with the
     INT8 archive rows written by the same tcgen05 kernel (nkv_kv_project),
@@ -582,27 +743,17 @@ def run_project(args) -> None:
     RmsNorm / RoPE chain in eager PyTorch, then commit_tensors, which
     quantizes) and cuBLAS alone on the same GEMM shape."""
     import torch
-    import torch.distributed as dist
     import nomas_kv as nk
     from nomas_kv import synth
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
     begin, n_layers = nk.partition_layers(args.layers, world, rank)
     stream = torch.cuda.current_stream(dev)
     cfg = nk.CacheConfig(storage=nk.CacheStorage.int8(), sampling=nk.HistorySampling.uniform(), past_frames=PAST)
     bank = nk.KvBank(cfg, n_layers, 1, HEADS, HEAD_DIM, torch.bfloat16, device=dev, layer_begin=begin)
     desc = lambda i: nk._abi.nkv_segment_desc(i, i * FRAMES, FRAMES, FRAMES * TPF, TEXT, 0)  # noqa: E731
     L = SEG_TOKENS
-    e2e_steps = 2
-    prefill = ARCHIVED - 1 - args.warmup
-    total = prefill + 2 * (args.warmup + args.steps) + e2e_steps + 2
+    prefill = max(1, archived - 1 - warmup)
+    total = prefill + 2 * (warmup + steps) + e2e_steps + 3
     bank.reserve(bank.segment_bytes(desc(0)) * n_layers * total, rebuild_tokens())
 
     g = torch.Generator(device=dev)
@@ -625,7 +776,6 @@ def run_project(args) -> None:
     v_out = [torch.empty_like(t) for t in k_out]
     recent_k = [torch.empty_like(t) for t in k_out]
     recent_v = [torch.empty_like(t) for t in k_out]
-    weights = [dict(wk=wk[i], wv=wv[i], bk=bk[i], bv=bv[i], k_gain=gain[i]) for i in range(n_layers)]
     seg = 0
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(n_layers)]
     proj_ms = [0.0, 0]
@@ -674,32 +824,27 @@ def run_project(args) -> None:
         bank.commit_tensors(desc(seg), k_out, v_out)
         seg += 1
 
-    def timed(fn, steps):
-        for _ in range(args.warmup):
+    def timed(fn, n):
+        for _ in range(warmup):
             fn(seg % 2)
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
+        _barrier(world)
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(stream)
-        for _ in range(steps):
+        for _ in range(n):
             fn(seg % 2)
         b.record(stream)
         torch.cuda.synchronize()
-        t = torch.tensor([a.elapsed_time(b)], dtype=torch.float64, device=dev)
-        if world > 1:
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return _max_over_ranks(world, dev, [a.elapsed_time(b)])[0]
 
-    clocks = ClockSampler(local)
+    clocks = ClockSampler(int(dev.index or 0))
     clocks.start()
-    ms_fused = timed(fused, args.steps)
+    ms_fused = timed(fused, steps)
     clk = clocks.stop()
     # per-launch device time of the producer kernel (separate, event-bracketed turns)
     for _ in range(2):
         fused(seg % 2, time_launches=True)
     launch_ms = proj_ms[0] / proj_ms[1]
-    ms_unfused = timed(unfused, args.steps)
+    ms_unfused = timed(unfused, steps)
     # cuBLAS alone on the same GEMM (x [L, 3072] x [3072, 6144])
     torch.cuda.synchronize()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -714,30 +859,37 @@ def run_project(args) -> None:
     torch.cuda.synchronize()
     cublas_ms = a.elapsed_time(b) / (reps * n_layers)
 
-    # e2e: the attention inputs come from pinned host memory every turn
-    host_x = [[t.cpu().pin_memory() for t in xs[s]] for s in range(2)]
-    torch.cuda.synchronize()
-    ea, eb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ea.record(stream)
-    for st in range(e2e_steps):
-        for i in range(n_layers):
-            xs[st % 2][i].copy_(host_x[st % 2][i], non_blocking=True)
-        fused(st % 2)  # returns after reading the layers' non-finite flags back
-    eb.record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = torch.tensor([ea.elapsed_time(eb)], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
-    e2e_ms = float(e2e_ms.item())
+    e2e = None
+    if e2e_steps:
+        # e2e: the attention inputs come from pinned host memory every turn
+        host_x = [[t.cpu().pin_memory() for t in xs[s]] for s in range(2)]
+        _barrier(world)
+        ea, eb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ea.record(stream)
+        for st in range(e2e_steps):
+            for i in range(n_layers):
+                xs[st % 2][i].copy_(host_x[st % 2][i], non_blocking=True)
+            fused(st % 2)  # returns after reading the layers' non-finite flags back
+        eb.record(stream)
+        torch.cuda.synchronize()
+        e2e_ms = _max_over_ranks(world, dev, [ea.elapsed_time(eb)])[0]
+        e2e = {"value": round(SEG_TOKENS * e2e_steps / (e2e_ms / 1e3), 1), "unit": "segment tokens/s (all layers)",
+               "h2d_bytes_per_step": SEG_TOKENS * DIM * 2 * args.layers,
+               "d2h_bytes_per_step": 4 * (n_layers + 1) * world, "steps": e2e_steps,
+               "result": "the K / V and the rebuilt working set stay in HBM; the device-to-host read per turn is "
+                         "the layers' non-finite status words"}
 
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu:
+    cpu_line = None
+    if cpu and rank == 0 and world == 1:
         try:
-            cpu = cpu_sample_project(min(os.cpu_count() or 1, 8))
+            cpu_line = cpu_sample_project(min(os.cpu_count() or 1, LAYERS))
         except Exception as e:  # noqa: BLE001
-            cpu = {"value": None, "unit": "segment tokens/s (all layers)", "cores": 0, "kind": "port",
-                   "sample": f"failed: {e}"}
-    peaks = load_peaks()
+            cpu_line = {"value": None, "unit": "segment tokens/s (all layers)", "cores": 0, "kind": "port",
+                        "sample": f"failed: {e}"}
+    bank.close()
+    del xs, wk, wv, wkv
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
     tflops = PROJECT_FLOPS / (launch_ms / 1e3) / 1e12
     traffic = None
     tp = os.path.join(ROOT, "profiles", "traffic.json")
@@ -746,36 +898,42 @@ def run_project(args) -> None:
         if t:
             traffic = int(t["dram_bytes"] / t["layers"])
     cublas_tflops = PROJECT_FLOPS / (cublas_ms / 1e3) / 1e12
-    value = SEG_TOKENS * args.steps / (ms_fused / 1e3)
+    return {
+        "metric": METRIC_PROJECT, "value": round(SEG_TOKENS * steps / (ms_fused / 1e3), 1),
+        "unit": "segment tokens/s (all layers)", "steps": steps, "warmup": warmup,
+        "ms_per_step": round(ms_fused / steps, 4),
+        "unfused": {"ms_per_step": round(ms_unfused / steps, 4),
+                    "what": "cuBLAS projection (torch.matmul) + eager bias / RmsNorm / RoPE + commit_tensors",
+                    "speedup_fused": round(ms_unfused / ms_fused, 3)},
+        "roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": peaks["bf16_tflops"],
+                     "unit": "TFLOP/s", "frac": round(tflops / peaks["bf16_tflops"], 4), "traffic": traffic,
+                     "kernel": "k_kv_project (one launch per layer)", "flops_per_launch": PROJECT_FLOPS,
+                     "launch_ms": round(launch_ms, 4), "peak_src": peaks["src"] + " (burst cuBLAS bf16)",
+                     "cublas_same_gemm_ms": round(cublas_ms, 4), "cublas_same_gemm_tflops": round(cublas_tflops, 1)},
+        "e2e": e2e, "gpu_launches": steps * (n_layers + 3), "clocks": clk, "cpu_baseline": cpu_line,
+    }
+
+
+def run_project(args) -> None:
+    import torch.distributed as dist
+
+    world, rank, local, dev = _dist_setup(args)
+    peaks = load_peaks()
+    r = project_measure(args, world, rank, dev, peaks, steps=args.steps, warmup=args.warmup, e2e_steps=2,
+                        cpu=not args.no_cpu, archived=ARCHIVED)
     if rank == 0:
-        out = {
-            "metric": METRIC_PROJECT, "value": round(value, 1), "unit": "segment tokens/s (all layers)",
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(ms_fused / args.steps, 4), "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "nomas-8B commit with its producer: per layer the K / V projection of a "
-                                   "6,496-token segment (Lin + bias, RmsNorm + RoPE on K) with INT8 archive rows "
-                                   "in the epilogue, staged commit, uniform rebuild (16 past frames), newest "
-                                   "segment", "layers": args.layers, "heads": HEADS, "head_dim": HEAD_DIM,
-                       "model_dim": DIM, "segment_tokens": SEG_TOKENS, "parallelism": f"layer-sharded x{world}",
-                       "l2": "attention inputs 1.9 GB per step > 126 MB L2"},
-            "unfused": {"ms_per_step": round(ms_unfused / args.steps, 4),
-                        "what": "cuBLAS projection (torch.matmul) + eager bias / RmsNorm / RoPE + commit_tensors",
-                        "speedup_fused": round(ms_unfused / ms_fused, 3)},
-            "roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": peaks["bf16_tflops"],
-                         "unit": "TFLOP/s", "frac": round(tflops / peaks["bf16_tflops"], 4), "traffic": traffic,
-                         "kernel": "k_kv_project (one launch per layer)", "flops_per_launch": PROJECT_FLOPS,
-                         "launch_ms": round(launch_ms, 4), "peak_src": peaks["src"] + " (burst cuBLAS bf16)",
-                         "cublas_same_gemm_ms": round(cublas_ms, 4), "cublas_same_gemm_tflops": round(cublas_tflops, 1)},
-            "e2e": {"value": round(SEG_TOKENS * e2e_steps / (e2e_ms / 1e3), 1), "unit": "segment tokens/s (all layers)",
-                    "h2d_bytes_per_step": SEG_TOKENS * DIM * 2 * args.layers,
-                    "d2h_bytes_per_step": 4 * (n_layers + 1) * world,
-                    "steps": e2e_steps},
-            "gpu_launches": args.steps * (n_layers + 3),
-            "clocks": clk, "cpu_baseline": cpu,
-        }
+        out = {"metric": r["metric"], "value": r["value"], "unit": r["unit"], "n_gpus": world, "steps": args.steps,
+               "warmup": args.warmup, "ms_per_step": r["ms_per_step"], "higher_is_better": True,
+               "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+               "config": {"workload": "nomas-8B commit with its producer: per layer the K / V projection of a "
+                                      "6,496-token segment (Lin + bias, RmsNorm + RoPE on K) with INT8 archive rows "
+                                      "in the epilogue, staged commit, uniform rebuild (16 past frames), newest "
+                                      "segment", "layers": args.layers, "heads": HEADS, "head_dim": HEAD_DIM,
+                          "model_dim": DIM, "segment_tokens": SEG_TOKENS, "parallelism": f"layer-sharded x{world}",
+                          "l2": "attention inputs 1.9 GB per step > 126 MB L2"},
+               "unfused": r["unfused"], "roofline": r["roofline"], "e2e": r["e2e"],
+               "gpu_launches": r["gpu_launches"], "clocks": r["clocks"], "cpu_baseline": r["cpu_baseline"]}
         print(json.dumps(out), flush=True)
-    bank.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -817,6 +975,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="INT8 line only: skip the QVG turn, the park + unpark and the producer turn")
     ap.add_argument("--workload", default="int8", choices=["int8", "qvg", "project"],
                     help="int8 = the headline configuration; qvg = the QVG configuration (frozen codebooks); "
                          "project = the commit with its fused K/V projection producer")

@@ -91,29 +91,34 @@ void ArchiveArena::reserve(size_t bytes) {
 Staging::~Staging() { release(); }
 
 void Staging::release() {
-  if (done_) {
-    cudaEventSynchronize(done_);
-    cudaEventDestroy(done_);
+  for (auto& sl : slot_) {
+    if (sl.done) {
+      cudaEventSynchronize(sl.done);
+      cudaEventDestroy(sl.done);
+    }
+    if (sl.host) cudaFreeHost(sl.host);
+    if (sl.dev) cudaFree(sl.dev);
+    sl = Slot{};
   }
-  if (host_) cudaFreeHost(host_);
-  if (dev_) cudaFree(dev_);
-  host_ = dev_ = nullptr;
-  done_ = nullptr;
-  cap_ = used_ = 0;
+  cur_ = 0;
+  used_ = 0;
 }
 
 void Staging::begin() {
-  if (!done_) NKV_CUDA(cudaEventCreateWithFlags(&done_, cudaEventDisableTiming));
-  if (pending_) {
-    NKV_CUDA(cudaEventSynchronize(done_));
-    pending_ = false;
+  cur_ = (cur_ + 1) % kSlots;
+  Slot& sl = slot_[cur_];
+  if (!sl.done) NKV_CUDA(cudaEventCreateWithFlags(&sl.done, cudaEventDisableTiming));
+  if (sl.pending) {
+    NKV_CUDA(cudaEventSynchronize(sl.done));
+    sl.pending = false;
   }
   used_ = 0;
 }
 
 size_t Staging::add(const void* p, size_t bytes) {
+  Slot& sl = slot_[cur_];
   size_t off = align_up(used_, 16);
-  if (off + bytes > cap_) {
+  if (off + bytes > sl.cap) {
     size_t cap = std::max<size_t>(align_up(off + bytes, 4096) * 2, 64 * 1024);
     unsigned char *h = nullptr, *d = nullptr;
     NKV_CUDA(cudaHostAlloc(&h, cap, cudaHostAllocDefault));
@@ -121,23 +126,24 @@ size_t Staging::add(const void* p, size_t bytes) {
       cudaFreeHost(h);
       fail(NKV_ERR_CUDA, "staging: cudaMalloc failed");
     }
-    if (used_) std::memcpy(h, host_, used_);
+    if (used_) std::memcpy(h, sl.host, used_);
     // the old device buffer may still be read by kernels in flight
-    if (dev_) cudaDeviceSynchronize();
-    if (host_) cudaFreeHost(host_);
-    if (dev_) cudaFree(dev_);
-    host_ = h, dev_ = d, cap_ = cap;
+    if (sl.dev) cudaDeviceSynchronize();
+    if (sl.host) cudaFreeHost(sl.host);
+    if (sl.dev) cudaFree(sl.dev);
+    sl.host = h, sl.dev = d, sl.cap = cap;
   }
-  if (bytes) std::memcpy(host_ + off, p, bytes);
+  if (bytes) std::memcpy(sl.host + off, p, bytes);
   used_ = off + bytes;
   return off;
 }
 
 void Staging::upload(cudaStream_t s) {
   if (used_ == 0) return;
-  NKV_CUDA(cudaMemcpyAsync(dev_, host_, used_, cudaMemcpyHostToDevice, s));
-  NKV_CUDA(cudaEventRecord(done_, s));
-  pending_ = true;
+  Slot& sl = slot_[cur_];
+  NKV_CUDA(cudaMemcpyAsync(sl.dev, sl.host, used_, cudaMemcpyHostToDevice, s));
+  NKV_CUDA(cudaEventRecord(sl.done, s));
+  sl.pending = true;
 }
 
 // ------------------------------------------------------------------- Bank --

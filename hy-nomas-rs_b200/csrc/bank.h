@@ -65,22 +65,32 @@ class ArchiveArena {
 };
 
 // Pinned host -> device upload area for per-call metadata (job lists, run
-// and tile tables, pointer arrays).  One H2D copy per call.
+// and tile tables, pointer arrays).  One H2D copy per call.  A ring of
+// slots: a call's tables stay untouched on the device until the slot comes
+// round again, and begin() waits only for that slot's upload of kSlots calls
+// ago, so the host never waits for the upload queued behind the previous
+// call's kernels.
 class Staging {
  public:
+  static constexpr int kSlots = 4;
   ~Staging();
-  void begin();  // waits until the previous upload has left the host buffer
+  void begin();  // next slot; waits until its previous upload has left the host buffer
   size_t add(const void* p, size_t bytes);
   void upload(cudaStream_t s);
-  const void* dev(size_t off) const { return dev_ + off; }
+  const void* dev(size_t off) const { return slot_[cur_].dev + off; }
   void release();
 
  private:
-  unsigned char* host_ = nullptr;
-  unsigned char* dev_ = nullptr;
-  size_t cap_ = 0, used_ = 0;
-  cudaEvent_t done_ = nullptr;
-  bool pending_ = false;
+  struct Slot {
+    unsigned char* host = nullptr;
+    unsigned char* dev = nullptr;
+    size_t cap = 0;
+    cudaEvent_t done = nullptr;
+    bool pending = false;
+  };
+  Slot slot_[kSlots];
+  int cur_ = 0;
+  size_t used_ = 0;
 };
 
 struct Rec {  // one archived segment (history.rs:40-55), all local layers

@@ -5,20 +5,30 @@ independent cache per DiT layer (cache/mod.rs:257-297).  Sharding therefore
 needs no data exchange: rank r owns the contiguous layer block
 ``partition_layers(n_layers, world, r)`` and every archive, working set and
 codebook of those layers stays in that GPU's HBM.  The only cross-rank
-traffic is host metadata:
+traffic is host metadata, at most 1 KB per turn:
 
-* ``verify=True`` checks that every rank commits the same segment
-  descriptor (one all_gather of six integers per commit; off on the hot path
-  of the benchmark, where each rank derives the descriptor itself);
-* a failed operation on any rank is reported on every rank (all_reduce MAX
-  of the status), so ranks never silently diverge in what they report;
+* the turn record (``verify=True``): before a commit or rollback, rank 0
+  broadcasts its record of the turn (operation, segment descriptor, the
+  timeline length after the turn, and the frames the history sampler picks
+  then, or the Recent-mode trim plan; cache/uniform_history.rs:76-125,
+  cache/swa.rs:52-95).  Every rank evaluates the same samplers on its own
+  state and compares, and one all-reduce of the comparisons lets every rank
+  take the same decision: when any rank disagrees no bank is touched and
+  every rank raises CacheState;
+* the status: every rank's outcome is all-reduced (MAX of the status code),
+  so when one rank fails every rank raises and no rank silently diverges in
+  what it reports;
 * ``metrics()`` reproduces KvBank::metrics (cache/mod.rs:305-319) over all
   layers of the model: MAX of archived_segments / rebuilds / evicted_tokens /
   rollbacks, SUM of the byte and encode counters.
 
-Works with any torch.distributed backend (NCCL on the GPUs, gloo in the CPU
-tests).  ``bank_factory(begin, count)`` builds the local bank; by default a
-KvBank on the current CUDA device.
+On NCCL both per-turn collectives run on a dedicated stream that does not
+wait for the cache's stream, so they overlap the rebuild gather the commit
+left running instead of draining it.  Works with any torch.distributed
+backend (NCCL on the GPUs, gloo in the CPU tests), and without an
+initialised process group as a single-rank bank (no collectives).
+``bank_factory(begin, count)`` builds the local bank; by default a KvBank
+on the current CUDA device.
 """
 from __future__ import annotations
 
@@ -27,26 +37,51 @@ from typing import Callable, Optional
 import torch
 import torch.distributed as dist
 
-from . import (CacheConfig, CacheMetrics, CacheStateError, KvBank, NomasError, _ERRORS, partition_layers)
+from . import (NKV_SAMPLING_RECENT, CacheConfig, CacheMetrics, CacheStateError, KvBank, NomasError, _ERRORS,
+               history_frame_indices, partition_layers, plan_recent_trim)
 from . import _abi
 
 _MAX_FIELDS = ("archived_segments", "rebuilds", "evicted_tokens", "rollbacks")
 _SUM_FIELDS = ("archived_bytes", "encode_calls", "d2h_bytes", "h2d_bytes")
+
+RECORD_WORDS = 128  # int64 words: 1 KB per turn
+_HEADER = 16  # op, 6 descriptor fields, frames after the turn, n items, FNV-1a of the items, ...
+OP_COMMIT, OP_ROLLBACK = 1, 2
+_FNV_OFFSET, _FNV_PRIME, _M64 = 0xCBF29CE484222325, 0x100000001B3, (1 << 64) - 1
+
+
+def _fnv1a(values) -> int:
+    h = _FNV_OFFSET
+    for v in values:
+        h = ((h ^ (int(v) & _M64)) * _FNV_PRIME) & _M64
+    return h - (1 << 64) if h >= (1 << 63) else h  # as a signed int64
 
 
 class ShardedKvBank:
     def __init__(self, cfg: CacheConfig, n_layers: int, batch: int, heads: int, head_dim: int, dtype,
                  group=None, bank_factory: Optional[Callable[[int, int], object]] = None, verify: bool = True,
                  device: Optional[torch.device] = None):
+        self.cfg = cfg
         self.group = group
-        self.rank = dist.get_rank(group)
-        self.world = dist.get_world_size(group)
+        self.distributed = dist.is_available() and dist.is_initialized()
+        self.rank = dist.get_rank(group) if self.distributed else 0
+        self.world = dist.get_world_size(group) if self.distributed else 1
         self.n_layers = n_layers
         self.begin, self.count = partition_layers(n_layers, self.world, self.rank)
         self.verify = verify
-        backend = dist.get_backend(group)
-        self.comm_device = torch.device("cuda", torch.cuda.current_device()) if backend == "nccl" \
-            else torch.device("cpu")
+        nccl = self.distributed and dist.get_backend(group) == "nccl"
+        self.comm_device = torch.device("cuda", torch.cuda.current_device()) if nccl else torch.device("cpu")
+        self.comm_stream = torch.cuda.Stream(self.comm_device) if nccl else None
+        pin = nccl
+        self._rec_host = torch.zeros(RECORD_WORDS, dtype=torch.int64, pin_memory=pin)
+        self._rec_dev = torch.zeros(RECORD_WORDS, dtype=torch.int64, device=self.comm_device)
+        self._st_host = torch.zeros(1, dtype=torch.int64, pin_memory=pin)
+        self._st_dev = torch.zeros(1, dtype=torch.int64, device=self.comm_device)
+        # the descriptors this bank holds, oldest first: the Recent-mode trim
+        # plan of the next turn needs them (swa.rs:52-95)
+        self._records: list[tuple[int, int, int, int, int]] = []
+        self._total_frames = 0
+        self._tpf = 0
         if bank_factory is None:
             bank_factory = lambda begin, count: KvBank(cfg, count, batch, heads, head_dim, dtype,  # noqa: E731
                                                        device=device, layer_begin=begin)
@@ -61,48 +96,136 @@ class ShardedKvBank:
             raise CacheStateError(f"layer {layer} lives on another rank")
         return layer - self.begin
 
-    def _agree(self, desc) -> None:
-        mine = torch.tensor([desc.segment_index, desc.frame_start, desc.frame_count, desc.image_tokens,
-                             desc.text_tokens, desc.action_start], dtype=torch.int64, device=self.comm_device)
-        allv = [torch.empty_like(mine) for _ in range(self.world)]
-        dist.all_gather(allv, mine, group=self.group)
-        if any(not torch.equal(allv[0], a) for a in allv[1:]):
-            raise CacheStateError("ranks disagree on the committed segment descriptor")
+    def _sampled(self, records, total_frames: int, tpf: int) -> list[int]:
+        """What the history sampler selects after a turn: the frame ids, or
+        for Recent mode the trim plan (evicted tokens, dropped records, then
+        (record, frames) pairs of dropped head frames)."""
+        if not records:
+            return []
+        s = self.cfg.sampling
+        if s.kind == NKV_SAMPLING_RECENT:
+            cap = self.cfg.capacity if self.cfg.capacity is not None else (1 << 63) - 1
+            drop_frames, drop_records, evicted, _ = plan_recent_trim(list(records), cap, max(tpf, 1))
+            out = [evicted, len(drop_records), *drop_records]
+            for r, f in drop_frames:
+                out += [r, f]
+            return out
+        return history_frame_indices(total_frames, self.cfg.past_frames, s)
 
-    def _collective_status(self, fn) -> None:
-        """Run fn locally, then make every rank raise if any rank failed."""
+    def _record(self, op: int, desc=None) -> list[int]:
+        """This rank's record of the next turn, from its own state."""
+        records, total, tpf = list(self._records), self._total_frames, self._tpf
+        d = [0] * 6
+        if op == OP_COMMIT:
+            d = [desc.segment_index, desc.frame_start, desc.frame_count, desc.image_tokens, desc.text_tokens,
+                 desc.action_start]
+            if desc.frame_count > 0 and tpf == 0:
+                tpf = desc.image_tokens // desc.frame_count
+            records.append((desc.segment_index, desc.frame_start, desc.frame_count, desc.image_tokens,
+                            desc.text_tokens))
+            total += desc.frame_count
+        elif records:
+            total -= records.pop()[2]
+        items = self._sampled(records, total, tpf)
+        head = [op, *d, total, len(items), _fnv1a(items)]
+        body = items[: RECORD_WORDS - _HEADER]
+        rec = head + [0] * (_HEADER - len(head)) + body
+        return rec + [0] * (RECORD_WORDS - len(rec))
+
+    def _collective(self, fn):
+        if self.comm_stream is None:
+            return fn()
+        with torch.cuda.stream(self.comm_stream):
+            return fn()
+
+    def _check_record(self, mine: list[int]) -> bool:
+        """Broadcast rank 0's turn record; True when this rank's equals it."""
+        def run():
+            self._rec_host.copy_(torch.tensor(mine, dtype=torch.int64))
+            self._rec_dev.copy_(self._rec_host, non_blocking=True)
+            dist.broadcast(self._rec_dev, src=dist.get_global_rank(self.group, 0) if self.group else 0,
+                           group=self.group)
+            self._rec_host.copy_(self._rec_dev, non_blocking=True)
+            if self.comm_stream is not None:
+                self.comm_stream.synchronize()
+            return self._rec_host.tolist() == mine
+        return self._collective(run)
+
+    def _any(self, flag: int) -> int:
+        return self._status(flag)
+
+    def _status(self, code: int) -> int:
+        def run():
+            self._st_host[0] = code
+            self._st_dev.copy_(self._st_host, non_blocking=True)
+            dist.all_reduce(self._st_dev, op=dist.ReduceOp.MAX, group=self.group)
+            self._st_host.copy_(self._st_dev, non_blocking=True)
+            if self.comm_stream is not None:
+                self.comm_stream.synchronize()
+            return int(self._st_host[0])
+        return self._collective(run)
+
+    def _turn(self, op: int, fn, desc=None) -> None:
+        """Check the turn record, run fn locally, make every rank raise if any
+        rank failed."""
         err: Optional[NomasError] = None
-        try:
-            fn()
-        except NomasError as e:
-            err = e
-        code = torch.tensor([err.code if err is not None else 0], dtype=torch.int64, device=self.comm_device)
-        dist.all_reduce(code, op=dist.ReduceOp.MAX, group=self.group)
-        c = int(code.item())
+        if self.world > 1 and self.verify and op in (OP_COMMIT, OP_ROLLBACK):
+            same = self._check_record(self._record(op, desc))
+            if self._any(0 if same else 1) != 0:
+                raise CacheStateError("ranks disagree on the turn record (segment descriptor or sampled history)")
+        if err is None:
+            try:
+                fn()
+            except NomasError as e:
+                err = e
+        code = err.code if err is not None else 0
+        c = self._status(code) if self.world > 1 else code
+        if err is None and c == 0:
+            return
         if err is not None:
             raise err
-        if c != 0:
-            raise _ERRORS.get(c, NomasError)(f"operation failed on another rank (status {c})")
+        raise _ERRORS.get(c, NomasError)(f"operation failed on another rank (status {c})")
 
     # ------------------------------------------------------------ API
     def commit(self, desc: _abi.nkv_segment_desc, ks, vs) -> None:
         """Commit one segment: ks / vs are this rank's layers' K / V."""
-        if self.verify:
-            self._agree(desc)
-        self._collective_status(lambda: self.local.commit_tensors(desc, ks, vs))
+        def run():
+            try:
+                self.local.commit_tensors(desc, ks, vs)
+            except NomasError as e:
+                # a rebuild over capacity still archived the segment (history.rs:416-421)
+                if not (e.code == _abi.NKV_ERR_GEOMETRY and "capacity" in e.msg):
+                    raise
+                self._archived(desc)
+                raise
+            self._archived(desc)
+        self._turn(OP_COMMIT, run, desc)
+
+    def _archived(self, desc) -> None:
+        self._records.append((desc.segment_index, desc.frame_start, desc.frame_count, desc.image_tokens,
+                              desc.text_tokens))
+        self._total_frames += desc.frame_count
+        if self._tpf == 0 and desc.frame_count > 0:
+            self._tpf = desc.image_tokens // desc.frame_count
 
     def rollback(self) -> None:
-        self._collective_status(self.local.rollback)
+        def run():
+            self.local.rollback()
+            if self._records:
+                self._total_frames -= self._records.pop()[2]
+        self._turn(OP_ROLLBACK, run)
 
     def park_all(self) -> None:
-        self._collective_status(self.local.park_all)
+        self._turn(0, self.local.park_all)
 
     def unpark_all(self) -> None:
-        self._collective_status(self.local.unpark_all)
+        self._turn(0, self.local.unpark_all)
 
     def metrics(self) -> CacheMetrics:
         m = self.local.metrics()
         d = m.as_dict() if isinstance(m, CacheMetrics) else dict(m)
+        if self.world == 1:
+            return CacheMetrics(**d)
         mx = torch.tensor([d[f] for f in _MAX_FIELDS], dtype=torch.int64, device=self.comm_device)
         sm = torch.tensor([d[f] for f in _SUM_FIELDS], dtype=torch.int64, device=self.comm_device)
         dist.all_reduce(mx, op=dist.ReduceOp.MAX, group=self.group)

@@ -106,6 +106,19 @@ def _worker(rank, world, port, q):
         except nk.NomasError as e:
             assert e.code == nk.MsgError.code
         sb.close()
+        # Recent mode with SWA eviction: the turn records carry the trim plan,
+        # which every rank derives alike (swa.rs:52-95)
+        rcfg = orc.Config(storage=orc.INT8, sampling=orc.RECENT, capacity=2 * L + tpf)
+        rb = ShardedKvBank(nk.CacheConfig(sampling=nk.HistorySampling.recent(), capacity=2 * L + tpf), n_layers, 1,
+                           H, D, 0, bank_factory=lambda b, c: OracleShard(orc, rcfg, b, c, H, D))
+        for s in range(4):
+            desc = nk._abi.nkv_segment_desc(s, s * frames, frames, frames * tpf, text, -1)
+            kv = [_inputs(1, rb.begin + i, s, L, H, D) for i in range(rb.count)]
+            rb.commit(desc, [k for k, _ in kv], [v for _, v in kv])
+        rec = rb._record(1, nk._abi.nkv_segment_desc(4, 8, frames, frames * tpf, text, -1))
+        assert rec[8] > 0  # the trim plan of the next turn is not empty
+        assert rb.metrics().evicted_tokens > 0
+        rb.close()
         dist.destroy_process_group()
         q.put((rank, "ok"))
     except BaseException as e:  # noqa: BLE001
@@ -131,3 +144,29 @@ def test_sharded_bank_two_gloo_ranks():
     for p in procs:
         p.join(timeout=60)
     assert results == {0: "ok", 1: "ok"}, results
+
+
+def test_sharded_bank_without_a_process_group_is_one_rank():
+    """Without torch.distributed initialised the sharded bank is the whole
+    model on one rank, with no collectives."""
+    import nomas_kv as nk
+    import oracle as orc
+    from nomas_kv.sharded import ShardedKvBank
+
+    n_layers, H, D, tpf, frames, text = 3, 2, 16, 8, 2, 3
+    L = frames * tpf + text
+    ocfg = orc.Config(storage=orc.INT8, sampling=orc.UNIFORM, past_frames=3)
+    sb = ShardedKvBank(nk.CacheConfig(), n_layers, 1, H, D, 0,
+                       bank_factory=lambda b, c: OracleShard(orc, ocfg, b, c, H, D))
+    assert (sb.rank, sb.world, sb.begin, sb.count) == (0, 1, 0, n_layers)
+    full = orc.Bank(ocfg, n_layers, 1, H, D, orc.F32)
+    for s in range(3):
+        desc = nk._abi.nkv_segment_desc(s, s * frames, frames, frames * tpf, text, -1)
+        kv = [_inputs(0, layer, s, L, H, D) for layer in range(n_layers)]
+        sb.commit(desc, [k for k, _ in kv], [v for _, v in kv])
+        full.commit(dict(segment_index=s, frame_start=s * frames, frame_count=frames, image_tokens=frames * tpf,
+                         text_tokens=text, action_start=-1), orc.F32, [k for k, _ in kv], [v for _, v in kv])
+    assert sb.metrics().as_dict() == full.metrics()
+    assert sb._record(2)[7] == 4  # a rollback would leave 4 frames
+    sb.close()
+    full.close()
