@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 
 #include <cstring>
+#include <functional>
 #include <string>
 
 #include "bank.h"
@@ -58,6 +59,8 @@ void check_dtype(int32_t dt) {
 namespace nkv {
 // Lets entry points outside this file report through nkv_last_error().
 void set_abi_error(const std::string& msg) { g_last_error = msg; }
+// The exception-to-status guard for entry points outside this file.
+int guarded_call(const std::function<void()>& f) { return guarded(f); }
 }  // namespace nkv
 
 extern "C" {

@@ -4,21 +4,26 @@
 // Some callers cannot call cudaMalloc: a process whose GPU memory is owned
 // entirely by another allocator (a framework's caching allocator that has
 // reserved the device, a server running under a fixed memory budget), or a
-// latency-critical caller that must not risk cudaMalloc's implicit device
-// synchronisation.  nkv_int8_quantize_layers_noalloc serves them: the
-// per-layer job table and the non-finite flags the quantize kernel needs live
-// in the file-scope array below instead of memory allocated per call.  The
-// caller still provides every input and output buffer.
+// caller that must not risk cudaMalloc's device-wide implicit
+// synchronisation (this entry point waits for its own stream only).
+// nkv_int8_quantize_layers_noalloc serves them: the per-layer job table and
+// the non-finite flags the quantize kernel needs live in the file-scope array
+// below instead of memory allocated per call.  The caller still provides
+// every input and output buffer.
 //
 // The array is a host-side stand-in in host code, not a device address; the
-// device address is looked up once per device with cudaGetSymbolAddress
-// (that device current) and passed to the kernel.  Every GPU that loads this
-// library holds the array until exit.  All calls share it and it keeps the
-// last call's contents, so calls whose work overlaps on the GPU (e.g. on two
-// streams) race with each other.
+// device address is looked up on every call with cudaGetSymbolAddress (with
+// the caller's device current, so a reset device or another context is
+// never handed a stale address) and passed to the kernel.  Every GPU that
+// loads this library holds the array until exit.  All calls share it and it
+// keeps the last call's contents: a call clears the flags it uses, and a
+// per-device mutex held from the first copy to the final stream
+// synchronisation serialises the calls of one process on one GPU, whichever
+// host threads and streams they come from.
 #include <cuda_runtime.h>
 
 #include <cstring>
+#include <functional>
 #include <mutex>
 #include <string>
 
@@ -27,7 +32,7 @@
 #include "nomas_kv.h"
 
 namespace nkv {
-void set_abi_error(const std::string& msg);  // abi.cpp
+int guarded_call(const std::function<void()>& f);  // abi.cpp
 }
 
 namespace {
@@ -43,12 +48,10 @@ struct Scratch {
 // 64 layers x 56-byte jobs + flags: about 3.9 KB per device.
 static __device__ __align__(256) unsigned char g_noalloc_scratch[sizeof(Scratch)];
 
-std::mutex g_mu;
-void* g_addr[kMaxDevices] = {nullptr};
+std::mutex g_dev_mu[kMaxDevices];
 
-int fail(int code, const std::string& msg) {
-  nkv::set_abi_error(msg);  // read back through nkv_last_error()
-  return code;
+void cuda_ok(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) nkv::fail(NKV_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
 }
 
 }  // namespace
@@ -57,62 +60,52 @@ extern "C" int nkv_int8_quantize_layers_noalloc(const void* const* k, const void
                                                 int32_t in_dtype, uint64_t rows, int64_t head_dim,
                                                 uint8_t* const* kq, uint8_t* const* vq, float* const* ks,
                                                 float* const* vs, uint32_t* nonfinite_out, void* stream) {
-  if (n_layers < 1 || n_layers > kMaxLayers)
-    return fail(NKV_ERR_ARGUMENT, "n_layers must be in [1, " + std::to_string(kMaxLayers) + "], got " +
+  return nkv::guarded_call([&] {
+    if (n_layers < 1 || n_layers > kMaxLayers)
+      nkv::fail(NKV_ERR_ARGUMENT, "n_layers must be in [1, " + std::to_string(kMaxLayers) + "], got " +
                                       std::to_string(n_layers));
-  if (in_dtype < NKV_F32 || in_dtype > NKV_F16) return fail(NKV_ERR_ARGUMENT, "unknown dtype");
-  if (head_dim < 1) return fail(NKV_ERR_ARGUMENT, "head_dim must be >= 1");
-  if (!k || !v || !kq || !vq || !ks || !vs || !nonfinite_out) return fail(NKV_ERR_ARGUMENT, "null pointer array");
-  for (int i = 0; i < n_layers; ++i)
-    if (!k[i] || !v[i] || !kq[i] || !vq[i] || !ks[i] || !vs[i])
-      return fail(NKV_ERR_ARGUMENT, "null pointer for layer " + std::to_string(i));
-  for (int i = 0; i < n_layers; ++i) nonfinite_out[i] = 0;
-  if (rows == 0) return NKV_OK;
+    if (in_dtype < NKV_F32 || in_dtype > NKV_F16) nkv::fail(NKV_ERR_ARGUMENT, "unknown dtype");
+    if (head_dim < 1) nkv::fail(NKV_ERR_ARGUMENT, "head_dim must be >= 1");
+    if (!k || !v || !kq || !vq || !ks || !vs || !nonfinite_out) nkv::fail(NKV_ERR_ARGUMENT, "null pointer array");
+    for (int i = 0; i < n_layers; ++i)
+      if (!k[i] || !v[i] || !kq[i] || !vq[i] || !ks[i] || !vs[i])
+        nkv::fail(NKV_ERR_ARGUMENT, "null pointer for layer " + std::to_string(i));
+    for (int i = 0; i < n_layers; ++i) nonfinite_out[i] = 0;
+    if (rows == 0) return;
 
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return fail(NKV_ERR_CUDA, std::string("cudaGetDevice: ") + cudaGetErrorString(e));
-  if (dev < 0 || dev >= kMaxDevices) return fail(NKV_ERR_ARGUMENT, "device index too large");
-  void* base = nullptr;
-  {
-    // First call on this device: resolve the array's device address with the
-    // device current (this first call should come before any stream capture).
-    std::lock_guard<std::mutex> lock(g_mu);
-    if (!g_addr[dev]) {
-      void* p = nullptr;
-      e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-      if (e != cudaSuccess) return fail(NKV_ERR_CUDA, std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(e));
-      g_addr[dev] = p;
+    int dev = 0;
+    cuda_ok(cudaGetDevice(&dev), "cudaGetDevice");
+    if (dev < 0 || dev >= kMaxDevices) nkv::fail(NKV_ERR_ARGUMENT, "device index too large");
+    std::lock_guard<std::mutex> lock(g_dev_mu[dev]);
+    // The array's device address in the current device's context.
+    void* base = nullptr;
+    cuda_ok(cudaGetSymbolAddress(&base, g_noalloc_scratch), "cudaGetSymbolAddress");
+    Scratch* sc = static_cast<Scratch*>(base);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+
+    nkv::QuantJob host_jobs[kMaxLayers];
+    bool aligned = true;
+    auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+    for (int i = 0; i < n_layers; ++i) {
+      host_jobs[i] = nkv::QuantJob{k[i], v[i], kq[i], vq[i], ks[i], vs[i], &sc->flags[1 + i]};
+      aligned &= a16(k[i]) && a16(v[i]) && a16(kq[i]) && a16(vq[i]);
     }
-    base = g_addr[dev];
-  }
-  Scratch* sc = static_cast<Scratch*>(base);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-
-  Scratch host_jobs;
-  bool aligned = true;
-  auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
-  for (int i = 0; i < n_layers; ++i) {
-    host_jobs.jobs[i] = nkv::QuantJob{k[i], v[i], kq[i], vq[i], ks[i], vs[i], &sc->flags[1 + i]};
-    aligned &= a16(k[i]) && a16(v[i]) && a16(kq[i]) && a16(vq[i]);
-  }
-  // The flags keep the previous call's values: clear them before the kernel.
-  e = cudaMemsetAsync(sc->flags, 0, sizeof(uint32_t) * (n_layers + 1), s);
-  if (e == cudaSuccess)
-    e = cudaMemcpyAsync(sc->jobs, host_jobs.jobs, sizeof(nkv::QuantJob) * n_layers, cudaMemcpyHostToDevice, s);
-  if (e == cudaSuccess)
-    e = nkv::launch_int8_quantize(sc->jobs, n_layers, rows, 0, head_dim, in_dtype, aligned, sc->flags, s);
-  uint32_t flags[kMaxLayers + 1];
-  if (e == cudaSuccess)
-    e = cudaMemcpyAsync(flags, sc->flags, sizeof(uint32_t) * (n_layers + 1), cudaMemcpyDeviceToHost, s);
-  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
-  if (e != cudaSuccess) return fail(NKV_ERR_CUDA, std::string("quantize: ") + cudaGetErrorString(e));
-  for (int i = 0; i < n_layers; ++i) nonfinite_out[i] = flags[1 + i];
-  if (flags[0] != 0) {
-    int first = 0;
-    while (first < n_layers && flags[1 + first] == 0) ++first;
-    const bool k_bad = first < n_layers && (flags[1 + first] & 1u) != 0;
-    return fail(NKV_ERR_MSG, std::string("cannot quantize non-finite ") + (k_bad ? "k" : "v") + " values");
-  }
-  return NKV_OK;
+    // The flags keep the previous call's values: clear them before the kernel.
+    cuda_ok(cudaMemsetAsync(sc->flags, 0, sizeof(uint32_t) * (n_layers + 1), s), "cudaMemsetAsync");
+    cuda_ok(cudaMemcpyAsync(sc->jobs, host_jobs, sizeof(nkv::QuantJob) * n_layers, cudaMemcpyHostToDevice, s),
+            "cudaMemcpyAsync");
+    cuda_ok(nkv::launch_int8_quantize(sc->jobs, n_layers, rows, 0, head_dim, in_dtype, aligned, sc->flags, s),
+            "quantize");
+    uint32_t flags[kMaxLayers + 1];
+    cuda_ok(cudaMemcpyAsync(flags, sc->flags, sizeof(uint32_t) * (n_layers + 1), cudaMemcpyDeviceToHost, s),
+            "cudaMemcpyAsync");
+    cuda_ok(cudaStreamSynchronize(s), "quantize");
+    for (int i = 0; i < n_layers; ++i) nonfinite_out[i] = flags[1 + i];
+    if (flags[0] != 0) {
+      int first = 0;
+      while (first < n_layers && flags[1 + first] == 0) ++first;
+      const bool k_bad = first < n_layers && (flags[1 + first] & 1u) != 0;
+      nkv::fail(NKV_ERR_MSG, std::string("cannot quantize non-finite ") + (k_bad ? "k" : "v") + " values");
+    }
+  });
 }

@@ -418,16 +418,18 @@ int nkv_synth_fill(void* dst, int32_t dtype, uint64_t rows, int64_t heads, int64
 /* INT8 quantize (the same kernel and results as nkv_int8_quantize, applied
  * to n_layers K/V pairs in one launch) that allocates no device memory, for
  * callers that cannot call cudaMalloc: a process whose GPU memory is owned
- * by another allocator or capped by a fixed budget, or a latency-critical
- * caller that must avoid cudaMalloc's implicit synchronisation.  No
- * counterpart in the reference.  k[i], v[i] hold `rows` x head_dim values of
- * in_dtype; kq/vq/ks/vs[i] receive codes and scales; nonfinite_out (host,
- * n_layers words) gets each layer's non-finite bits.  The job table and
- * flags live in one library-wide device array sized for
- * NKV_NOALLOC_MAX_LAYERS layers; larger n_layers is rejected with
- * NKV_ERR_ARGUMENT.  The first call on a device looks up that array's
- * address (make it before any stream capture); calls whose GPU work overlaps
- * (e.g. on two streams) race on the array.  Synchronizes `stream`. */
+ * by another allocator or capped by a fixed budget, or a caller that must
+ * not risk cudaMalloc's device-wide implicit synchronisation (this call
+ * waits for `stream` only).  No counterpart in the reference.  k[i], v[i]
+ * hold `rows` x head_dim values of in_dtype; kq/vq/ks/vs[i] receive codes
+ * and scales; nonfinite_out (host, n_layers words) gets each layer's
+ * non-finite bits.  The job table and flags live in one library-wide device
+ * array sized for NKV_NOALLOC_MAX_LAYERS layers; larger n_layers is rejected
+ * with NKV_ERR_ARGUMENT.  Every call looks up that array's address on the
+ * current device.  Calls share the array: within one process the library
+ * serialises them per GPU (a mutex held until the call's work finished),
+ * whatever host threads and streams they come from.  Synchronizes `stream`
+ * before returning. */
 int nkv_int8_quantize_layers_noalloc(const void* const* k, const void* const* v, int32_t n_layers, int32_t in_dtype,
                                      uint64_t rows, int64_t head_dim, uint8_t* const* kq, uint8_t* const* vq,
                                      float* const* ks, float* const* vs, uint32_t* nonfinite_out, void* stream);

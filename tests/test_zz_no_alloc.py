@@ -45,33 +45,59 @@ def _call(nk, ks_in, vs_in, dtype, rows, D, outs):
     return rc, list(flags)
 
 
-def test_noalloc_quantize_matches_allocating_entry_point_twice():
-    torch = pytest.importorskip("torch")
-    import nomas_kv as nk
-    from nomas_kv import synth
-
-    assert torch.cuda.is_available(), "needs a CUDA device"
-    n_layers, L, H, D = 3, 1000, 4, 128
+def _check_against_allocating(nk, torch, gen, cases, n_layers, L, H, D):
+    """Runs the no-alloc entry point on each (dtype code, torch dtype) case in
+    turn, reusing the same outputs, and compares every call with
+    nkv_int8_quantize layer by layer."""
     rows = L * H
-    gen = synth.DeviceGen(torch.device("cuda", 0), seed=5, key_sigma=1.0)
     outs = ([torch.empty(rows * D, dtype=torch.uint8, device="cuda") for _ in range(n_layers)],
             [torch.empty(rows * D, dtype=torch.uint8, device="cuda") for _ in range(n_layers)],
             [torch.empty(rows, dtype=torch.float32, device="cuda") for _ in range(n_layers)],
             [torch.empty(rows, dtype=torch.float32, device="cuda") for _ in range(n_layers)])
-    for call, (dtype, tdt) in enumerate(((nk.NKV_BF16, torch.bfloat16), (nk.NKV_F32, torch.float32))):
+    for call, (dtype, tdt) in enumerate(cases):
         ks = [gen.fill(torch.empty((1, L, H, D), dtype=tdt, device="cuda"), layer, call, 0, dtype)
               for layer in range(n_layers)]
         vs = [gen.fill(torch.empty((1, L, H, D), dtype=tdt, device="cuda"), layer, call, 1, dtype)
               for layer in range(n_layers)]
+        torch.cuda.synchronize()
+        free_before = torch.cuda.mem_get_info()[0]
         rc, flags = _call(nk, ks, vs, dtype, rows, D, outs)
+        free_after = torch.cuda.mem_get_info()[0]
         assert rc == 0, nk.lib().nkv_last_error()
         assert flags == [0] * n_layers
+        # the call itself allocated nothing on the device
+        assert free_after == free_before, (free_before, free_after)
         for i in range(n_layers):
             ref = _reference(nk, torch, ks[i], vs[i], dtype, rows, D)
             for got, want in zip((outs[0][i], outs[1][i], outs[2][i], outs[3][i]), ref):
                 g = got.cpu().numpy()
                 w = want.cpu().numpy()
                 assert np.array_equal(g.view(np.uint8), w.view(np.uint8)), f"call {call} layer {i} differs"
+
+
+def test_noalloc_quantize_matches_allocating_entry_point_twice():
+    torch = pytest.importorskip("torch")
+    import nomas_kv as nk
+    from nomas_kv import synth
+
+    assert torch.cuda.is_available(), "needs a CUDA device"
+    gen = synth.DeviceGen(torch.device("cuda", 0), seed=5, key_sigma=1.0)
+    # one warm-up call so the library's module and the array are resident
+    # before the free-memory comparison
+    _check_against_allocating(nk, torch, gen, [(nk.NKV_BF16, torch.bfloat16)], 1, 16, 4, 128)
+    _check_against_allocating(nk, torch, gen, [(nk.NKV_BF16, torch.bfloat16), (nk.NKV_F32, torch.float32),
+                                               (nk.NKV_F16, torch.float16)], 3, 1000, 4, 128)
+
+
+def test_noalloc_quantize_generic_head_dim_twice():
+    """head_dim 96 goes through the generic (non-vectorised) quantize kernel."""
+    torch = pytest.importorskip("torch")
+    import nomas_kv as nk
+    from nomas_kv import synth
+
+    gen = synth.DeviceGen(torch.device("cuda", 0), seed=9, key_sigma=1.0)
+    _check_against_allocating(nk, torch, gen, [(nk.NKV_BF16, torch.bfloat16), (nk.NKV_F16, torch.float16)],
+                              2, 333, 3, 96)
 
 
 def test_noalloc_quantize_rejects_more_layers_than_its_array_holds():
