@@ -27,9 +27,12 @@ __device__ __forceinline__ uint32_t quant_exact(float x, float s) {
 // XOR 0x80); valid for s in [FLT_MIN, 1e37] with r = RN(1/s) and
 // |x / s| < 128.
 //  * RN(|x| / s) without a divide: q0 = RN(|x| r), the residual
-//    e = |x| - s q0 exact by an FMA, q1 = RN(q0 + e r) (Markstein);
+//    e = |x| - s q0 exact by an FMA, q1 = RN(q0 + e r) (Markstein) wherever
+//    the quotient is normal (a subnormal quotient rounds to 0 either way);
 //  * round half away from zero of q1 >= 0 is floor(RN(q1 + C)) with
-//    C = 0.5 - 2^-25 (true for every f32 in [0, 128], checked exhaustively);
+//    C = 0.5 - 2^-25 (true for every f32 in [0, 128]);
+//  the two identities and the resulting code byte are checked on the device
+//  for every bf16 value and row peak (tests/test_gpu_quant_identities.py);
 //    adding M with round-toward-zero takes the floor and leaves n in the low
 //    bits, and M + sign(x) n (an exact FMA) puts the sign back.
 __device__ __forceinline__ uint32_t code_bits(float x, float s, float r) {
