@@ -98,6 +98,14 @@ int nkv_bank_commit(nkv_bank* bank, const nkv_segment_desc* seg, int32_t kv_dtyp
   });
 }
 
+int nkv_bank_commit_decode(nkv_bank* bank, const nkv_segment_desc* seg, int32_t kv_dtype, const void* const* k_dev,
+                           const void* const* v_dev, void* const* k_out, void* const* v_out) {
+  return guarded([&] {
+    need(seg, "segment descriptor");
+    bank_of(bank).commit_decode(*seg, kv_dtype, k_dev, v_dev, k_out, v_out);
+  });
+}
+
 int nkv_bank_rollback(nkv_bank* bank) {
   return guarded([&] { bank_of(bank).rollback(); });
 }

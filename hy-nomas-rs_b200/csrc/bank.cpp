@@ -96,6 +96,10 @@ void Staging::release() {
       cudaEventSynchronize(sl.done);
       cudaEventDestroy(sl.done);
     }
+    if (sl.consumed) {
+      cudaEventSynchronize(sl.consumed);
+      cudaEventDestroy(sl.consumed);
+    }
     if (sl.host) cudaFreeHost(sl.host);
     if (sl.dev) cudaFree(sl.dev);
     sl = Slot{};
@@ -104,14 +108,22 @@ void Staging::release() {
   used_ = 0;
 }
 
-void Staging::begin() {
+void Staging::begin(cudaStream_t main) {
+  // everything the previous call enqueued on `main` has read its slot by the
+  // time this event completes
+  Slot& prev = slot_[cur_];
+  if (prev.used) NKV_CUDA(cudaEventRecord(prev.consumed, main));
   cur_ = (cur_ + 1) % kSlots;
   Slot& sl = slot_[cur_];
-  if (!sl.done) NKV_CUDA(cudaEventCreateWithFlags(&sl.done, cudaEventDisableTiming));
+  if (!sl.done) {
+    NKV_CUDA(cudaEventCreateWithFlags(&sl.done, cudaEventDisableTiming));
+    NKV_CUDA(cudaEventCreateWithFlags(&sl.consumed, cudaEventDisableTiming));
+  }
   if (sl.pending) {
     NKV_CUDA(cudaEventSynchronize(sl.done));
     sl.pending = false;
   }
+  sl.used = false;
   used_ = 0;
 }
 
@@ -138,12 +150,16 @@ size_t Staging::add(const void* p, size_t bytes) {
   return off;
 }
 
-void Staging::upload(cudaStream_t s) {
+void Staging::upload(cudaStream_t aux, cudaStream_t main) {
   if (used_ == 0) return;
   Slot& sl = slot_[cur_];
-  NKV_CUDA(cudaMemcpyAsync(sl.dev, sl.host, used_, cudaMemcpyHostToDevice, s));
-  NKV_CUDA(cudaEventRecord(sl.done, s));
+  // the slot's previous tables were read by work on `main` (kSlots calls ago)
+  NKV_CUDA(cudaStreamWaitEvent(aux, sl.consumed, 0));
+  NKV_CUDA(cudaMemcpyAsync(sl.dev, sl.host, used_, cudaMemcpyHostToDevice, aux));
+  NKV_CUDA(cudaEventRecord(sl.done, aux));
+  NKV_CUDA(cudaStreamWaitEvent(main, sl.done, 0));
   sl.pending = true;
+  sl.used = true;
 }
 
 // ------------------------------------------------------------------- Bank --
@@ -202,10 +218,17 @@ Bank::Bank(const nkv_cache_config& cfg, int n_layers, int layer_begin, int64_t b
   if (device < 0 || device >= n_dev) fail(NKV_ERR_ARGUMENT, "device " + std::to_string(device) + " out of range");
   DeviceScope ds(device_);
   NKV_CUDA(cudaStreamCreateWithFlags(&side_, cudaStreamNonBlocking));
+  NKV_CUDA(cudaStreamCreateWithFlags(&aux_, cudaStreamNonBlocking));
   // [0]: any layer saw a non-finite value (aborts the gather); [1 + i]: layer i
-  NKV_CUDA(cudaMalloc(&d_flag_, sizeof(uint32_t) * (n_layers_ + 1)));
+  for (int b = 0; b < 2; ++b) {
+    NKV_CUDA(cudaMalloc(&d_flags_[b], sizeof(uint32_t) * (n_layers_ + 1)));
+    NKV_CUDA(cudaMemset(d_flags_[b], 0, sizeof(uint32_t) * (n_layers_ + 1)));
+    NKV_CUDA(cudaEventCreateWithFlags(&flags_free_[b], cudaEventDisableTiming));
+  }
+  d_flag_ = d_flags_[0];
   NKV_CUDA(cudaHostAlloc(&h_flag_, sizeof(uint32_t) * (n_layers_ + 1), cudaHostAllocDefault));
   NKV_CUDA(cudaEventCreateWithFlags(&flag_ev_, cudaEventDisableTiming));
+  NKV_CUDA(cudaEventCreateWithFlags(&encoded_, cudaEventDisableTiming));
   std::memset(h_flag_, 0, sizeof(uint32_t) * (n_layers_ + 1));
   if (cfg.storage == NKV_STORAGE_QVG) {
     cb_layer_ = size_t(2) * H_ * q_stages_ * q_E_ * D_;
@@ -224,6 +247,10 @@ Bank::~Bank() {
     cudaStreamSynchronize(side_);
     cudaStreamDestroy(side_);
   }
+  if (aux_) {
+    cudaStreamSynchronize(aux_);
+    cudaStreamDestroy(aux_);
+  }
   for (auto& p : pending_) {
     cudaEventDestroy(p.a);
     cudaEventDestroy(p.b);
@@ -232,9 +259,13 @@ Bank::~Bank() {
   if (cur_a_) cudaEventDestroy(cur_a_);
   if (ws_) cudaFree(ws_);
   if (cb_dev_) cudaFree(cb_dev_);
-  if (d_flag_) cudaFree(d_flag_);
+  for (int b = 0; b < 2; ++b) {
+    if (d_flags_[b]) cudaFree(d_flags_[b]);
+    if (flags_free_[b]) cudaEventDestroy(flags_free_[b]);
+  }
   if (h_flag_) cudaFreeHost(h_flag_);
   if (flag_ev_) cudaEventDestroy(flag_ev_);
+  if (encoded_) cudaEventDestroy(encoded_);
   for (auto p : p_host_)
     if (p) cudaFreeHost(p);
   stg_.release();
@@ -396,7 +427,7 @@ Plan Bank::plan_rebuild() {
 }
 
 // Device run/tile tables for a plan, appended to the staging area.
-GatherTables Bank::add_runs(const Plan& plan, bool outputs_aligned) {
+GatherTables Bank::add_runs(const Plan& plan, bool outputs_aligned, const Plan* plan2) {
   constexpr int64_t kTile = 32;
   std::vector<GatherRun> runs;
   std::vector<GatherTile> tiles;
@@ -405,10 +436,16 @@ GatherTables Bank::add_runs(const Plan& plan, bool outputs_aligned) {
   // <= 64 tokens inside one payload block (one alpha per head and stage)
   const bool qvg_fast = cfg_.storage == NKV_STORAGE_QVG && qvg_gather_fast_ok(int(H_), int(D_), q_stages_, q_bits_) &&
                         B_ == 1 && outputs_aligned;
-  runs.reserve(plan.runs.size());
-  for (const auto& rs : plan.runs) {
+  runs.reserve(plan.runs.size() + (plan2 ? plan2->runs.size() : 0));
+  std::vector<std::pair<const RunSpec*, int32_t>> all;
+  for (const auto& rs : plan.runs) all.push_back({&rs, 0});
+  if (plan2)
+    for (const auto& rs : plan2->runs) all.push_back({&rs, 1});
+  for (const auto& [rsp, out_set] : all) {
+    const RunSpec& rs = *rsp;
     const Rec& r = archive_[rs.rec];
     GatherRun g{};
+    g.out_set = out_set;
     g.src = r.slab;
     g.layer_stride = int64_t(r.layer_stride);
     g.src_tok = rs.src_tok;
@@ -458,7 +495,8 @@ GatherTables Bank::add_runs(const Plan& plan, bool outputs_aligned) {
 }
 
 void Bank::launch_gather_into(const GatherTables& t, size_t outk_off, size_t outv_off, uint64_t out_L,
-                              bool vector_ok, const uint32_t* abort_flag, int timing_id) {
+                              bool vector_ok, const uint32_t* abort_flag, int timing_id, size_t out2k_off,
+                              size_t out2v_off, uint64_t out2_L) {
   if (t.n_tiles + t.n_qtiles == 0) return;
   GatherArgs a{};
   a.runs = static_cast<const GatherRun*>(stg_.dev(t.runs_off));
@@ -470,6 +508,11 @@ void Bank::launch_gather_into(const GatherTables& t, size_t outk_off, size_t out
   a.out_k = static_cast<void* const*>(stg_.dev(outk_off));
   a.out_v = static_cast<void* const*>(stg_.dev(outv_off));
   a.out_L = int64_t(out_L);
+  if (out2_L > 0) {
+    a.out2_k = static_cast<void* const*>(stg_.dev(out2k_off));
+    a.out2_v = static_cast<void* const*>(stg_.dev(out2v_off));
+    a.out2_L = int64_t(out2_L);
+  }
   a.H = int32_t(H_), a.D = int32_t(D_);
   a.out_dtype = dtype_;
   a.cb = cb_dev_;
@@ -582,6 +625,37 @@ void Bank::commit(const nkv_segment_desc& s, int kv_dtype, const void* const* k,
   finish_commit(s, r, kv_dtype, k, v, false);
 }
 
+void Bank::commit_decode(const nkv_segment_desc& s, int kv_dtype, const void* const* k, const void* const* v,
+                         void* const* k_out, void* const* v_out) {
+  if (!k || !v) fail(NKV_ERR_ARGUMENT, "null K/V pointer array");
+  if (!k_out || !v_out) fail(NKV_ERR_ARGUMENT, "null output pointer array");
+  for (int i = 0; i < n_layers_; ++i) {
+    if (!k[i] || !v[i]) fail(NKV_ERR_ARGUMENT, "null K/V pointer for layer " + std::to_string(i));
+    if (!k_out[i] || !v_out[i]) fail(NKV_ERR_ARGUMENT, "null output pointer for layer " + std::to_string(i));
+  }
+  no_staged("commit");
+  DeviceScope ds(device_);
+  validate(s, kv_dtype, k, v);
+  Rec r = make_rec(s);
+  r.slab = arena_.push(r.layer_stride * n_layers_);
+  finish_commit(s, r, kv_dtype, k, v, false, k_out, v_out);
+}
+
+// Picks the next set of non-finite flags and clears it: on the auxiliary
+// stream after the last gather that read the set, or (a staged commit,
+// whose producer writes the flags on the cache's stream) on the cache's
+// stream.
+void Bank::next_flags(bool clear_on_aux) {
+  flag_set_ ^= 1;
+  d_flag_ = d_flags_[flag_set_];
+  if (clear_on_aux) {
+    NKV_CUDA(cudaStreamWaitEvent(aux_, flags_free_[flag_set_], 0));
+    NKV_CUDA(cudaMemsetAsync(d_flag_, 0, sizeof(uint32_t) * (n_layers_ + 1), aux_));
+  } else {
+    NKV_CUDA(cudaMemsetAsync(d_flag_, 0, sizeof(uint32_t) * (n_layers_ + 1), stream_));
+  }
+}
+
 // validate_segment (history.rs:168-238) and the record's slab; the
 // producer then writes the INT8 rows (int8.rs:65-81 layout: codes (B, L, H, D)
 // u8, scales (B, L, H) f32) and ORs its non-finite bits into the layer's
@@ -595,7 +669,7 @@ void Bank::stage(const nkv_segment_desc& s, nkv_staged_layer* out) {
   Rec r = make_rec(s);
   r.slab = arena_.push(r.layer_stride * n_layers_);
   try {
-    NKV_CUDA(cudaMemsetAsync(d_flag_, 0, sizeof(uint32_t) * (n_layers_ + 1), stream_));
+    next_flags(false);
   } catch (...) {
     arena_.pop();
     throw;
@@ -629,7 +703,7 @@ void Bank::discard_staged() {
 }
 
 void Bank::finish_commit(const nkv_segment_desc& s, Rec r, int kv_dtype, const void* const* k, const void* const* v,
-                         bool staged) {
+                         bool staged, void* const* dk, void* const* dv) {
   const nkv_metrics saved = m_;
   const uint64_t L = s.image_tokens + s.text_tokens;
   bool pushed = false, popped = false;
@@ -658,7 +732,10 @@ void Bank::finish_commit(const nkv_segment_desc& s, Rec r, int kv_dtype, const v
       plan_err = e;
     }
 
-    stg_.begin();
+    stg_.begin(stream_);
+    // a plain commit clears its flag set on the auxiliary stream, ahead of
+    // the table upload the cache's stream waits for
+    if (!staged) next_flags(true);
     bool in_aligned = true;
     if (!staged)
       for (int i = 0; i < n_layers_; ++i) in_aligned &= aligned16(k[i]) && aligned16(v[i]);
@@ -696,25 +773,38 @@ void Bank::finish_commit(const nkv_segment_desc& s, Rec r, int kv_dtype, const v
       text_jobs_off = stg_.add(tj.data(), tj.size() * sizeof(QuantJob));
     }
 
-    size_t outk_off = 0, outv_off = 0;
+    size_t outk_off = 0, outv_off = 0, out2k_off = 0, out2v_off = 0;
     GatherTables gt;
-    if (plan_ok && plan.valid > 0) {
-      ensure_ws(plan.valid, &fresh, &fresh_cap);
-      unsigned char* base = fresh ? fresh : ws_;
-      const uint64_t cap = fresh ? fresh_cap : ws_cap_;
-      gt = add_runs(plan);
-      std::vector<void*> ok(n_layers_), ov(n_layers_);
-      for (int i = 0; i < n_layers_; ++i) ok[i] = ws_plane(base, cap, i, 0), ov[i] = ws_plane(base, cap, i, 1);
+    // the new segment decoded in full into the caller's buffers, in the same
+    // launch as the rebuild (decode_segment, history.rs:308-338)
+    Plan dplan;
+    const bool decode = dk != nullptr && plan_ok;
+    bool dec_aligned = true;
+    if (decode) {
+      dplan = decode_plan(archive_.size() - 1);
+      for (int i = 0; i < n_layers_; ++i) dec_aligned &= aligned16(dk[i]) && aligned16(dv[i]);
+      out2k_off = stg_.add(dk, n_layers_ * sizeof(void*));
+      out2v_off = stg_.add(dv, n_layers_ * sizeof(void*));
+    }
+    if (plan_ok && (plan.valid > 0 || decode)) {
+      unsigned char* base = ws_;
+      uint64_t cap = ws_cap_;
+      if (plan.valid > 0) {
+        ensure_ws(plan.valid, &fresh, &fresh_cap);
+        base = fresh ? fresh : ws_;
+        cap = fresh ? fresh_cap : ws_cap_;
+      }
+      gt = add_runs(plan, dec_aligned, decode ? &dplan : nullptr);
+      gt.aligned = dec_aligned;
+      std::vector<void*> ok(n_layers_, nullptr), ov(n_layers_, nullptr);
+      if (plan.valid > 0)
+        for (int i = 0; i < n_layers_; ++i) ok[i] = ws_plane(base, cap, i, 0), ov[i] = ws_plane(base, cap, i, 1);
       outk_off = stg_.add(ok.data(), ok.size() * sizeof(void*));
       outv_off = stg_.add(ov.data(), ov.size() * sizeof(void*));
     }
-    stg_.upload(stream_);
+    stg_.upload(aux_, stream_);
 
-    if (staged) {
-      NKV_CUDA(launch_flag_reduce(d_flag_, n_layers_, stream_));  // the gather aborts on word 0
-    } else {
-      NKV_CUDA(cudaMemsetAsync(d_flag_, 0, sizeof(uint32_t) * (n_layers_ + 1), stream_));
-    }
+    if (staged) NKV_CUDA(launch_flag_reduce(d_flag_, n_layers_, stream_));  // the gather aborts on word 0
     if (staged) {
     } else if (cfg_.storage == NKV_STORAGE_FLOAT) {
       tbegin(NKV_KERNEL_FLOAT_ARCHIVE);
@@ -739,14 +829,19 @@ void Bank::finish_commit(const nkv_segment_desc& s, Rec r, int kv_dtype, const v
         tend(NKV_KERNEL_QUANTIZE);
       }
     }
-    // The non-finite flags are final once the archive kernels ran: read them
-    // back ahead of the rebuild gather (which aborts on them by itself), so
-    // the host waits only for the kernels that read the caller's K/V and the
-    // gather overlaps the caller's next calls (all stream-ordered).
-    NKV_CUDA(cudaMemcpyAsync(h_flag_, d_flag_, sizeof(uint32_t) * (n_layers_ + 1), cudaMemcpyDeviceToHost,
-                             stream_));
-    NKV_CUDA(cudaEventRecord(flag_ev_, stream_));
-    if (gt.n_tiles + gt.n_qtiles > 0) launch_gather_into(gt, outk_off, outv_off, plan.valid, gt.aligned, d_flag_);
+    // The non-finite flags are final once the archive kernels ran: they are
+    // read back on the auxiliary stream while the rebuild gather (which
+    // aborts on them by itself) follows the archive kernels directly on the
+    // cache's stream, so the host waits only for the kernels that read the
+    // caller's K/V and the gather overlaps the caller's next calls.
+    NKV_CUDA(cudaEventRecord(encoded_, stream_));
+    NKV_CUDA(cudaStreamWaitEvent(aux_, encoded_, 0));
+    NKV_CUDA(cudaMemcpyAsync(h_flag_, d_flag_, sizeof(uint32_t) * (n_layers_ + 1), cudaMemcpyDeviceToHost, aux_));
+    NKV_CUDA(cudaEventRecord(flag_ev_, aux_));
+    if (gt.n_tiles + gt.n_qtiles > 0)
+      launch_gather_into(gt, outk_off, outv_off, plan.valid, gt.aligned, d_flag_, NKV_KERNEL_GATHER, out2k_off,
+                         out2v_off, decode ? dplan.valid : 0);
+    NKV_CUDA(cudaEventRecord(flags_free_[flag_set_], stream_));
     NKV_CUDA(cudaEventSynchronize(flag_ev_));
     collect_timing(false);
 
@@ -811,7 +906,7 @@ void Bank::rebuild_now() {
   uint64_t fresh_cap = 0;
   if (plan.valid > 0) {
     ensure_ws(plan.valid, &fresh, &fresh_cap);
-    stg_.begin();
+    stg_.begin(stream_);
     const GatherTables gt = add_runs(plan);
     unsigned char* base = fresh ? fresh : ws_;
     const uint64_t cap = fresh ? fresh_cap : ws_cap_;
@@ -819,7 +914,7 @@ void Bank::rebuild_now() {
     for (int i = 0; i < n_layers_; ++i) ok[i] = ws_plane(base, cap, i, 0), ov[i] = ws_plane(base, cap, i, 1);
     const size_t outk_off = stg_.add(ok.data(), ok.size() * sizeof(void*));
     const size_t outv_off = stg_.add(ov.data(), ov.size() * sizeof(void*));
-    stg_.upload(stream_);
+    stg_.upload(aux_, stream_);
     try {
       launch_gather_into(gt, outk_off, outv_off, plan.valid, gt.aligned, nullptr);
     } catch (...) {
@@ -939,13 +1034,9 @@ void Bank::unpark() {
   parked_ = false;
 }
 
-// decode_segment (history.rs:308-338) of every local layer into caller buffers.
-void Bank::decode_segment(uint64_t pos, void* const* k_out, void* const* v_out) {
-  if (pos >= archive_.size()) fail(NKV_ERR_ARGUMENT, "archive position out of range");
-  if (!k_out || !v_out) fail(NKV_ERR_ARGUMENT, "null output pointer array");
-  for (int i = 0; i < n_layers_; ++i)
-    if (!k_out[i] || !v_out[i]) fail(NKV_ERR_ARGUMENT, "null output pointer for layer " + std::to_string(i));
-  DeviceScope ds(device_);
+// Runs of a whole archived segment in its own order (decode_segment,
+// history.rs:308-338): QVG video then the INT8 text block, else one run.
+Plan Bank::decode_plan(size_t pos) const {
   const Rec& r = archive_[pos];
   Plan p;
   const int64_t Lv = int64_t(r.desc.image_tokens), Lt = int64_t(r.desc.text_tokens);
@@ -956,14 +1047,25 @@ void Bank::decode_segment(uint64_t pos, void* const* k_out, void* const* v_out) 
     p.runs.push_back({pos, false, 0, 0, Lv + Lt});
   }
   p.valid = uint64_t(Lv + Lt);
-  stg_.begin();
+  return p;
+}
+
+// decode_segment (history.rs:308-338) of every local layer into caller buffers.
+void Bank::decode_segment(uint64_t pos, void* const* k_out, void* const* v_out) {
+  if (pos >= archive_.size()) fail(NKV_ERR_ARGUMENT, "archive position out of range");
+  if (!k_out || !v_out) fail(NKV_ERR_ARGUMENT, "null output pointer array");
+  for (int i = 0; i < n_layers_; ++i)
+    if (!k_out[i] || !v_out[i]) fail(NKV_ERR_ARGUMENT, "null output pointer for layer " + std::to_string(i));
+  DeviceScope ds(device_);
+  const Plan p = decode_plan(pos);
+  stg_.begin(stream_);
   bool aligned = true;
   for (int i = 0; i < n_layers_; ++i) aligned &= aligned16(k_out[i]) && aligned16(v_out[i]);
   const GatherTables gt = add_runs(p, aligned);
   aligned &= gt.aligned;
   const size_t outk_off = stg_.add(k_out, n_layers_ * sizeof(void*));
   const size_t outv_off = stg_.add(v_out, n_layers_ * sizeof(void*));
-  stg_.upload(stream_);
+  stg_.upload(aux_, stream_);
   launch_gather_into(gt, outk_off, outv_off, p.valid, aligned, nullptr, NKV_KERNEL_SEGMENT_DECODE);
 }
 

@@ -65,18 +65,22 @@ class ArchiveArena {
 };
 
 // Pinned host -> device upload area for per-call metadata (job lists, run
-// and tile tables, pointer arrays).  One H2D copy per call.  A ring of
-// slots: a call's tables stay untouched on the device until the slot comes
-// round again, and begin() waits only for that slot's upload of kSlots calls
-// ago, so the host never waits for the upload queued behind the previous
-// call's kernels.
+// and tile tables, pointer arrays).  One H2D copy per call, issued on an
+// auxiliary stream so that it never sits between two kernels of the cache's
+// stream; the cache's stream waits for it with an event.  A ring of slots: a
+// call's tables stay untouched on the device until the slot comes round
+// again (the upload into a slot waits for the cache-stream work of the
+// slot's previous call), and begin() waits only for that slot's host buffer
+// to have left, kSlots calls ago.
 class Staging {
  public:
   static constexpr int kSlots = 4;
   ~Staging();
-  void begin();  // next slot; waits until its previous upload has left the host buffer
+  // next slot; `main` is the stream whose work consumes the tables
+  void begin(cudaStream_t main);
   size_t add(const void* p, size_t bytes);
-  void upload(cudaStream_t s);
+  // the copy on `aux`, ordered before everything enqueued on `main` afterwards
+  void upload(cudaStream_t aux, cudaStream_t main);
   const void* dev(size_t off) const { return slot_[cur_].dev + off; }
   void release();
 
@@ -85,8 +89,9 @@ class Staging {
     unsigned char* host = nullptr;
     unsigned char* dev = nullptr;
     size_t cap = 0;
-    cudaEvent_t done = nullptr;
-    bool pending = false;
+    cudaEvent_t done = nullptr;      // the upload left the host buffer
+    cudaEvent_t consumed = nullptr;  // the cache-stream work of the slot's call
+    bool pending = false, used = false;
   };
   Slot slot_[kSlots];
   int cur_ = 0;
@@ -131,6 +136,10 @@ class Bank {
   ~Bank();
 
   void commit(const nkv_segment_desc& s, int kv_dtype, const void* const* k, const void* const* v);
+  // commit, then the new segment decoded in full (decode_segment) into
+  // k_out / v_out by the rebuild's gather launch
+  void commit_decode(const nkv_segment_desc& s, int kv_dtype, const void* const* k, const void* const* v,
+                     void* const* k_out, void* const* v_out);
   // Two-phase INT8 commit for a producer that writes the archive rows itself
   // (the fused K/V projection): stage validates the segment and reserves its
   // record, commit_staged archives it and rebuilds, discard_staged drops it.
@@ -172,13 +181,17 @@ class Bank {
   // archive_segment + rebuild of a validated segment whose slab is pushed;
   // `staged`: the codes are already in the slab and the per-layer flags set
   void finish_commit(const nkv_segment_desc& s, Rec r, int kv_dtype, const void* const* k, const void* const* v,
-                     bool staged);
+                     bool staged, void* const* dk = nullptr, void* const* dv = nullptr);
+  Plan decode_plan(size_t pos) const;
   void no_staged(const char* what) const;
   Plan plan_rebuild();
-  GatherTables add_runs(const Plan& plan, bool outputs_aligned = true);
+  // device run/tile tables of `plan` (out_set 0) and, when given, of
+  // `plan2` (out_set 1, the second output set of the same launch)
+  GatherTables add_runs(const Plan& plan, bool outputs_aligned = true, const Plan* plan2 = nullptr);
   std::vector<int> fit_qvg(const nkv_segment_desc& s, int kv_dtype, const void* const* k, const void* const* v);
   void launch_gather_into(const GatherTables& t, size_t outk_off, size_t outv_off, uint64_t out_L, bool vector_ok,
-                          const uint32_t* abort_flag, int timing_id = NKV_KERNEL_GATHER);
+                          const uint32_t* abort_flag, int timing_id = NKV_KERNEL_GATHER, size_t out2k_off = 0,
+                          size_t out2v_off = 0, uint64_t out2_L = 0);
   void ensure_ws(uint64_t tokens, unsigned char** fresh, uint64_t* fresh_cap);
   unsigned char* ws_plane(unsigned char* base, uint64_t cap, int layer, int side) const;
   size_t ws_plane_bytes(uint64_t cap) const;
@@ -223,9 +236,18 @@ class Bank {
   std::vector<char> fitted_;
   size_t cb_layer_ = 0;
 
-  uint32_t* d_flag_ = nullptr;  // n_layers + 1 non-finite flags (see the constructor)
+  // Two sets of n_layers + 1 non-finite flags (see the constructor), used
+  // by alternate commits: a commit clears its set while the previous commit's
+  // gather, which reads the other set, may still run.
+  uint32_t* d_flags_[2] = {nullptr, nullptr};
+  uint32_t* d_flag_ = nullptr;  // the current commit's set
+  int flag_set_ = 0;
+  cudaEvent_t flags_free_[2] = {nullptr, nullptr};  // the last gather that read set i is done
   uint32_t* h_flag_ = nullptr;
   cudaEvent_t flag_ev_ = nullptr;  // the flags' read-back has landed
+  cudaEvent_t encoded_ = nullptr;  // the commit's archive kernels ran
+  cudaStream_t aux_ = nullptr;     // table uploads, flag clears and read-backs
+  void next_flags(bool clear_on_aux);
   Staging stg_;
 
   bool timing_ = false;

@@ -83,8 +83,9 @@ __global__ void __launch_bounds__(kGatherThreads) k_gather(const GatherArgs a) {
   const unsigned char* base = run.src + (int64_t)layer * run.layer_stride;
   const int64_t off_data = side ? run.off[1] : run.off[0];
   const int64_t off_scale = side ? run.off[3] : run.off[2];
-  void* out_base = side ? a.out_v[layer] : a.out_k[layer];
-  const int64_t out_tok = (int64_t)tile.b * a.out_L + run.dst_tok + tile.tok0;
+  void* const* outs = run.out_set ? (side ? a.out2_v : a.out2_k) : (side ? a.out_v : a.out_k);
+  void* out_base = outs[layer];
+  const int64_t out_tok = (int64_t)tile.b * (run.out_set ? a.out2_L : a.out_L) + run.dst_tok + tile.tok0;
   const int64_t src_tok = (int64_t)tile.b * run.src_L + run.src_tok + tile.tok0;
   // Chunk arithmetic in 32 bits: a tile holds at most 32 tokens.
   const int chunks_per_tok = (int)(HD / 16);
@@ -189,8 +190,9 @@ __global__ void __launch_bounds__(kGatherThreads) k_gather_generic(const GatherA
   const unsigned char* base = run.src + (int64_t)layer * run.layer_stride;
   const int64_t off_data = side ? run.off[1] : run.off[0];
   const int64_t off_scale = side ? run.off[3] : run.off[2];
-  void* out_base = side ? a.out_v[layer] : a.out_k[layer];
-  const int64_t out_tok = (int64_t)tile.b * a.out_L + run.dst_tok + tile.tok0;
+  void* const* outs = run.out_set ? (side ? a.out2_v : a.out2_k) : (side ? a.out_v : a.out_k);
+  void* out_base = outs[layer];
+  const int64_t out_tok = (int64_t)tile.b * (run.out_set ? a.out2_L : a.out_L) + run.dst_tok + tile.tok0;
   const int64_t src_tok = (int64_t)tile.b * run.src_L + run.src_tok + tile.tok0;
   const int64_t n = (int64_t)tile.ntok * HD;
   for (int64_t i = threadIdx.x; i < n; i += kGatherThreads) {
@@ -418,7 +420,8 @@ __global__ void __launch_bounds__(kQvgThreads) k_gather_qvg(const GatherArgs a) 
   // overflow to +-inf), so the hardware converters are exact.
   const bool all_finite = __syncthreads_and(nonfinite == 0) != 0;
   if (hh >= nh) return;
-  void* out = side ? a.out_v[layer] : a.out_k[layer];
+  void* const* outs = run.out_set ? (side ? a.out2_v : a.out2_k) : (side ? a.out_v : a.out_k);
+  void* out = outs[layer];
   const int64_t dst0 = run.dst_tok + tile.tok0;  // batch 1
   if (all_finite) decode_rows<OUT_DT, true>(out, T, p3, tile.ntok, dst0, H, h0 + hh, hh, tpar, lane);
   else decode_rows<OUT_DT, false>(out, T, p3, tile.ntok, dst0, H, h0 + hh, hh, tpar, lane);

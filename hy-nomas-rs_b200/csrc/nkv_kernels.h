@@ -99,6 +99,8 @@ struct GatherRun {
   int64_t ntok;
   int32_t kind;
   int32_t n_blocks;  // QVG: blocks in the payload
+  int32_t out_set;   // 0: out_k / out_v / out_L; 1: out2_k / out2_v / out2_L
+  int32_t pad_;
 };
 
 // Work unit of one CTA: `ntok` tokens of run `run` for batch row `b`,
@@ -137,6 +139,11 @@ struct GatherArgs {
   void* const* out_k;  // [n_layers] output bases (device array)
   void* const* out_v;
   int64_t out_L;  // tokens per batch row of the output
+  // A second output set for runs with out_set == 1 (a segment decoded in the
+  // same launch as the rebuild); unused otherwise.
+  void* const* out2_k;
+  void* const* out2_v;
+  int64_t out2_L;
   int32_t H, D;
   int32_t out_dtype;
   // QVG

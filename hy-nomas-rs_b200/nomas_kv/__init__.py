@@ -421,8 +421,11 @@ class KvBank:
         vs = [s.v for s in per_layer]
         self.commit_tensors(d0.desc(), ks, vs)
 
-    def commit_tensors(self, desc: _abi.nkv_segment_desc, ks, vs) -> None:
-        """Commit one segment given per-layer K/V tensors (the C-ABI shape)."""
+    def commit_tensors(self, desc: _abi.nkv_segment_desc, ks, vs, decode_k=None, decode_v=None) -> None:
+        """Commit one segment given per-layer K/V tensors (the C-ABI shape).
+        With decode_k / decode_v (per-layer tensors of the same shape, model
+        dtype) the new segment is also decoded in full into them, by the
+        rebuild's gather launch (nkv_bank_commit_decode)."""
         expected = (self.batch, desc.image_tokens + desc.text_tokens, self.heads, self.head_dim)
         dt = None
         for name, ts in (("k", ks), ("v", vs)):
@@ -438,7 +441,19 @@ class KvBank:
                     raise GeometryError("k and v of every layer must share one dtype")
         kp = (C.c_void_p * self.n_layers)(*[t.data_ptr() for t in ks])
         vp = (C.c_void_p * self.n_layers)(*[t.data_ptr() for t in vs])
-        _check(lib().nkv_bank_commit(self._h, C.byref(desc), dt, kp, vp))
+        if decode_k is None:
+            _check(lib().nkv_bank_commit(self._h, C.byref(desc), dt, kp, vp))
+            return
+        want = torch_dtype(self.dtype_code)
+        for name, ts in (("decode_k", decode_k), ("decode_v", decode_v)):
+            if ts is None or len(ts) != self.n_layers:
+                raise ArgumentError(f"{name} needs one tensor per layer")
+            for t in ts:
+                if tuple(t.shape) != expected or t.dtype != want or not t.is_contiguous():
+                    raise GeometryError(f"{name} tensors must be contiguous {list(expected)} {want}")
+        dkp = (C.c_void_p * self.n_layers)(*[t.data_ptr() for t in decode_k])
+        dvp = (C.c_void_p * self.n_layers)(*[t.data_ptr() for t in decode_v])
+        _check(lib().nkv_bank_commit_decode(self._h, C.byref(desc), dt, kp, vp, dkp, dvp))
 
     def commit_ptrs(self, desc: _abi.nkv_segment_desc, kv_dtype: int, k_ptrs, v_ptrs) -> None:
         kp = (C.c_void_p * self.n_layers)(*k_ptrs)

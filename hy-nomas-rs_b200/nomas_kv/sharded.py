@@ -187,11 +187,15 @@ class ShardedKvBank:
         raise _ERRORS.get(c, NomasError)(f"operation failed on another rank (status {c})")
 
     # ------------------------------------------------------------ API
-    def commit(self, desc: _abi.nkv_segment_desc, ks, vs) -> None:
-        """Commit one segment: ks / vs are this rank's layers' K / V."""
+    def commit(self, desc: _abi.nkv_segment_desc, ks, vs, decode_k=None, decode_v=None) -> None:
+        """Commit one segment: ks / vs are this rank's layers' K / V; with
+        decode_k / decode_v the new segment is also decoded into them."""
         def run():
             try:
-                self.local.commit_tensors(desc, ks, vs)
+                if decode_k is None:
+                    self.local.commit_tensors(desc, ks, vs)
+                else:
+                    self.local.commit_tensors(desc, ks, vs, decode_k, decode_v)
             except NomasError as e:
                 # a rebuild over capacity still archived the segment (history.rs:416-421)
                 if not (e.code == _abi.NKV_ERR_GEOMETRY and "capacity" in e.msg):

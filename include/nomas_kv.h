@@ -215,6 +215,17 @@ int nkv_bank_segment_bytes(const nkv_bank* bank, const nkv_segment_desc* seg, ui
  * into the caller's device buffers k_out[i] / v_out[i]. */
 int nkv_bank_decode_segment(nkv_bank* bank, uint64_t archive_pos, void* const* k_out, void* const* v_out);
 
+/* nkv_bank_commit followed by nkv_bank_decode_segment of the segment it
+ * archived (no reference counterpart as one call: commit_segment,
+ * history.rs:458-463, then decode_segment, history.rs:308-338).  The new
+ * segment's K/V as the archive holds them (INT8 dequantized, QVG decoded
+ * plus the INT8 text, Float as stored), model dtype (B, L_seg, H, D), go to
+ * k_out[i] / v_out[i] from the same gather launch that rebuilds the working
+ * set.  Errors as nkv_bank_commit; when it fails the outputs are not
+ * written. */
+int nkv_bank_commit_decode(nkv_bank* bank, const nkv_segment_desc* seg, int32_t kv_dtype, const void* const* k_dev,
+                           const void* const* v_dev, void* const* k_out, void* const* v_out);
+
 /* Enable/disable per-kernel CUDA-event timing and read / reset the totals. */
 int nkv_bank_set_timing(nkv_bank* bank, int32_t enable);
 int nkv_bank_kernel_stats(nkv_bank* bank, nkv_kernel_stat* out /* [NKV_KERNEL_COUNT] */, int32_t reset);
