@@ -320,7 +320,11 @@ def _dist_setup(args):
     dev = torch.device("cuda", local)
     if world > 1:
         from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+        # high-priority NCCL streams: the per-turn collectives of the sharded
+        # bank must not queue behind the rebuild gather's CTAs
+        opts = dist.ProcessGroupNCCL.Options()
+        opts.is_high_priority_stream = True
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev, pg_options=opts)
     return world, rank, local, dev
 
 

@@ -22,9 +22,9 @@ traffic is host metadata, at most 1 KB per turn:
   layers of the model: MAX of archived_segments / rebuilds / evicted_tokens /
   rollbacks, SUM of the byte and encode counters.
 
-On NCCL both per-turn collectives run on a dedicated stream that does not
-wait for the cache's stream, so they overlap the rebuild gather the commit
-left running instead of draining it.  Works with any torch.distributed
+On NCCL the per-turn collectives run on a dedicated high-priority stream
+that does not wait for the cache's stream, so they overlap the rebuild
+gather the commit left running instead of waiting for it to drain.  Works with any torch.distributed
 backend (NCCL on the GPUs, gloo in the CPU tests), and without an
 initialised process group as a single-rank bank (no collectives).
 ``bank_factory(begin, count)`` builds the local bank; by default a KvBank
@@ -71,7 +71,9 @@ class ShardedKvBank:
         self.verify = verify
         nccl = self.distributed and dist.get_backend(group) == "nccl"
         self.comm_device = torch.device("cuda", torch.cuda.current_device()) if nccl else torch.device("cpu")
-        self.comm_stream = torch.cuda.Stream(self.comm_device) if nccl else None
+        # high priority: the collectives' kernels are scheduled ahead of the
+        # rebuild gather's pending CTAs instead of after the whole grid
+        self.comm_stream = torch.cuda.Stream(self.comm_device, priority=-1) if nccl else None
         pin = nccl
         self._rec_host = torch.zeros(RECORD_WORDS, dtype=torch.int64, pin_memory=pin)
         self._rec_dev = torch.zeros(RECORD_WORDS, dtype=torch.int64, device=self.comm_device)
