@@ -401,6 +401,11 @@ class Turns:
             for i in range(self.n_layers):
                 self.bank.layer(i).set_qvg_codebooks(synth.qvg_codebooks(self.begin + i, HEADS, HEAD_DIM))
         self.prefill = max(1, archived - 1 - args.warmup)
+        tier_gb = getattr(args, "archive_device_gb", 0.0) if workload == args.workload else 0.0
+        if tier_gb > 0:
+            # the tiered archive: slabs beyond this many device bytes live in
+            # pinned, device-mapped host memory and are read over the host link
+            self.bank.set_archive_device_limit(int(tier_gb * 1e9))
         self.bank.reserve(self.bank.segment_bytes(self.desc(0)) * self.n_layers * (self.prefill + max_turns),
                           rebuild_tokens())
         # two resident input sets (each > L2), alternated turn to turn
@@ -637,6 +642,13 @@ def run_gpu(args) -> None:
                      "bound": "host link: fractions of the measured pinned copy bandwidth per GPU with every rank "
                               "copying at once", "link": link}
     gk = T.kernel_figures(kst, args.steps, peaks["hbm_gbs"])
+    tiers = None
+    if args.archive_device_gb > 0:
+        dev_b, host_b = T.bank.archive_usage()
+        tiers = {"device_limit_gb": args.archive_device_gb, "archive_device_gb": round(dev_b / 1e9, 2),
+                 "archive_host_gb": round(host_b / 1e9, 2),
+                 "what": "archive slabs beyond the device limit in pinned, device-mapped host memory; the rebuild "
+                         "gather reads those over the host link"}
     T.close()
     del host
 
@@ -705,6 +717,7 @@ def run_gpu(args) -> None:
                              f"{link['h2d_gbs_aggregate']} GB/s with all {world} GPU(s) copying at once"},
             "qvg": qvg,
             "producer": project,
+            "archive_tiers": tiers,
             "gpu_launches": gk["launches"],
             "clocks": clk,
             "cpu_baseline": cpu,
@@ -990,6 +1003,8 @@ def main():
                          "project = the commit with its fused K/V projection producer")
     ap.add_argument("--swap", action="store_true",
                     help="box-run configuration: phase-swapped cache, park + unpark every turn, 64-segment archive")
+    ap.add_argument("--archive-device-gb", type=float, default=0.0,
+                    help="tiered archive: keep at most this many GB of archive slabs in device memory (0: no limit)")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="model layers (48 = the 8B geometry; fewer only for small profiling cases)")
     args = ap.parse_args()

@@ -98,6 +98,18 @@ int nkv_bank_commit(nkv_bank* bank, const nkv_segment_desc* seg, int32_t kv_dtyp
   });
 }
 
+int nkv_bank_set_archive_device_limit(nkv_bank* bank, uint64_t device_bytes) {
+  return guarded([&] { bank_of(bank).set_archive_device_limit(device_bytes); });
+}
+
+int nkv_bank_archive_usage(nkv_bank* bank, uint64_t* device_bytes, uint64_t* host_bytes) {
+  return guarded([&] {
+    need(device_bytes, "device_bytes");
+    need(host_bytes, "host_bytes");
+    bank_of(bank).archive_usage(device_bytes, host_bytes);
+  });
+}
+
 int nkv_bank_commit_decode(nkv_bank* bank, const nkv_segment_desc* seg, int32_t kv_dtype, const void* const* k_dev,
                            const void* const* v_dev, void* const* k_out, void* const* v_out) {
   return guarded([&] {

@@ -46,9 +46,31 @@ DeviceScope::~DeviceScope() {
 ArchiveArena::~ArchiveArena() { release(); }
 
 void ArchiveArena::release() {
-  for (auto& c : chunks_) cudaFree(c.base);
+  for (auto& c : chunks_) {
+    if (c.host) cudaFreeHost(c.base);
+    else cudaFree(c.base);
+  }
   chunks_.clear();
   stack_.clear();
+  device_chunk_bytes_ = 0;
+}
+
+unsigned char* ArchiveArena::alloc_chunk(size_t bytes, bool* host) {
+  unsigned char* p = nullptr;
+  if (device_chunk_bytes_ + bytes <= device_limit_) {
+    NKV_CUDA(cudaMalloc(&p, bytes));
+    device_chunk_bytes_ += bytes;
+    *host = false;
+    return p;
+  }
+  NKV_CUDA(cudaHostAlloc(&p, bytes, cudaHostAllocMapped | cudaHostAllocPortable));
+  void* d = nullptr;
+  if (cudaHostGetDevicePointer(&d, p, 0) != cudaSuccess || d != p) {
+    cudaFreeHost(p);
+    fail(NKV_ERR_CUDA, "host archive tier: the device does not address mapped host memory by its host pointer");
+  }
+  *host = true;
+  return p;
 }
 
 size_t ArchiveArena::free_from_top() const {
@@ -68,9 +90,9 @@ unsigned char* ArchiveArena::push(size_t bytes) {
     off = 0;
   }
   if (ci == chunks_.size()) {
-    unsigned char* p = nullptr;
-    NKV_CUDA(cudaMalloc(&p, bytes));
-    chunks_.push_back({p, bytes});
+    bool host = false;
+    unsigned char* p = alloc_chunk(bytes, &host);
+    chunks_.push_back({p, bytes, host});
   }
   stack_.push_back({ci, off, bytes});
   return chunks_[ci].base + off;
@@ -82,9 +104,27 @@ void ArchiveArena::pop() {
 
 void ArchiveArena::reserve(size_t bytes) {
   if (free_from_top() >= bytes) return;
-  unsigned char* p = nullptr;
-  NKV_CUDA(cudaMalloc(&p, align_up(bytes)));
-  chunks_.push_back({p, align_up(bytes)});
+  size_t b = align_up(bytes);
+  // what the device limit still allows goes to device memory, the rest to
+  // the host tier
+  if (device_chunk_bytes_ < device_limit_ && device_chunk_bytes_ + b > device_limit_) {
+    const size_t room = (device_limit_ - device_chunk_bytes_) / 256 * 256;
+    if (room > 0) {
+      bool host = false;
+      unsigned char* p = alloc_chunk(room, &host);
+      chunks_.push_back({p, room, host});
+      b -= std::min(b, room);
+    }
+  }
+  if (b == 0) return;
+  bool host = false;
+  unsigned char* p = alloc_chunk(b, &host);
+  chunks_.push_back({p, b, host});
+}
+
+void ArchiveArena::usage(size_t* device, size_t* host) const {
+  *device = *host = 0;
+  for (const auto& sl : stack_) (chunks_[sl.chunk].host ? *host : *device) += sl.size;
 }
 
 // ---------------------------------------------------------------- Staging --
@@ -663,6 +703,8 @@ void Bank::next_flags(bool clear_on_aux) {
 void Bank::stage(const nkv_segment_desc& s, nkv_staged_layer* out) {
   if (!out) fail(NKV_ERR_ARGUMENT, "null staged-layer array");
   if (cfg_.storage != NKV_STORAGE_INT8) fail(NKV_ERR_INVALID_CONFIG, "staged commits need INT8 storage");
+  if (arena_.device_limit() != SIZE_MAX)
+    fail(NKV_ERR_INVALID_CONFIG, "staged commits need the whole archive in device memory (no archive device limit)");
   if (staged_) fail(NKV_ERR_CACHE_STATE, "a staged segment is already pending");
   DeviceScope ds(device_);
   validate(s, NKV_BF16, nullptr, nullptr);
@@ -1075,6 +1117,17 @@ void Bank::synchronize() {
   collect_timing(false);
 }
 
+void Bank::set_archive_device_limit(uint64_t bytes) {
+  if (staged_) fail(NKV_ERR_CACHE_STATE, "a staged segment is pending");
+  arena_.set_device_limit(bytes == 0 ? SIZE_MAX : size_t(bytes));
+}
+
+void Bank::archive_usage(uint64_t* device, uint64_t* host) const {
+  size_t d = 0, h = 0;
+  arena_.usage(&d, &h);
+  *device = d, *host = h;
+}
+
 void Bank::reserve(uint64_t archive_bytes, uint64_t working_tokens) {
   DeviceScope ds(device_);
   if (archive_bytes) arena_.reserve(archive_bytes);
@@ -1186,7 +1239,7 @@ uint64_t Bank::export_segment(int layer, uint64_t pos, void* host, uint64_t cap)
   unsigned char* out = static_cast<unsigned char*>(host);
   const unsigned char* lb = r.slab + size_t(layer) * r.layer_stride;
   for (auto& p : parts) {
-    NKV_CUDA(cudaMemcpy(out, lb + p.first, p.second, cudaMemcpyDeviceToHost));
+    NKV_CUDA(cudaMemcpy(out, lb + p.first, p.second, cudaMemcpyDefault));  // the slab may be in either tier
     out += p.second;
   }
   return total;
@@ -1346,7 +1399,7 @@ void Bank::save(const char* path) {
     for (uint64_t o = 0; o < bytes; o += kIoChunk) {
       const size_t n = size_t(std::min<uint64_t>(kIoChunk, bytes - o));
       buf.resize(n);
-      NKV_CUDA(cudaMemcpy(buf.data(), r.slab + o, n, cudaMemcpyDeviceToHost));
+      NKV_CUDA(cudaMemcpy(buf.data(), r.slab + o, n, cudaMemcpyDefault));  // either tier
       f.put(buf.data(), n);
     }
   }
@@ -1406,7 +1459,7 @@ void Bank::load(const char* path) {
         const size_t c = size_t(std::min<uint64_t>(kIoChunk, bytes - o));
         buf.resize(c);
         f.get(buf.data(), c);
-        NKV_CUDA(cudaMemcpy(r.slab + o, buf.data(), c, cudaMemcpyHostToDevice));
+        NKV_CUDA(cudaMemcpy(r.slab + o, buf.data(), c, cudaMemcpyDefault));  // either tier
       }
     }
     if (frames != total_frames) fail(NKV_ERR_MSG, std::string(path) + ": the segments do not cover the timeline");

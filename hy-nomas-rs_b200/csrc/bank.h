@@ -42,7 +42,12 @@ class DeviceScope {
 
 // LIFO allocator for archive slabs.  The archive only grows at the end
 // (commit) and shrinks at the end (rollback), so slabs are carved out of a
-// few large cudaMalloc'd chunks in stack order and never fragment.
+// few large chunks in stack order and never fragment.  Chunks are device
+// memory up to a device byte limit (none by default); beyond it they are
+// pinned host memory mapped into the device's address space, which the
+// kernels read and write through the same pointers over the host link: an
+// archive larger than HBM (256 segments x 48 layers at the 8B geometry is
+// 506 GB) stays usable on one GPU.
 class ArchiveArena {
  public:
   ~ArchiveArena();
@@ -50,12 +55,19 @@ class ArchiveArena {
   void pop();
   void reserve(size_t bytes);
   void release();
+  void set_device_limit(size_t bytes) { device_limit_ = bytes; }
+  size_t device_limit() const { return device_limit_; }
+  // bytes of the live slabs in device memory / in host memory
+  void usage(size_t* device, size_t* host) const;
 
  private:
   struct Chunk {
     unsigned char* base;
     size_t cap;
+    bool host;
   };
+  unsigned char* alloc_chunk(size_t bytes, bool* host);
+  size_t device_limit_ = SIZE_MAX, device_chunk_bytes_ = 0;
   struct Slot {
     size_t chunk, off, size;
   };
@@ -153,6 +165,8 @@ class Bank {
   void decode_segment(uint64_t pos, void* const* k_out, void* const* v_out);
   void synchronize();
   void reserve(uint64_t archive_bytes, uint64_t working_tokens);
+  void set_archive_device_limit(uint64_t bytes);
+  void archive_usage(uint64_t* device, uint64_t* host) const;
   uint64_t segment_bytes(const nkv_segment_desc& s) const;
 
   void working_set(int layer, const void** k, const void** v, uint64_t* valid) const;

@@ -480,6 +480,17 @@ class KvBank:
     def reserve(self, archive_bytes: int, working_tokens: int = 0) -> None:
         _check(lib().nkv_bank_reserve(self._h, archive_bytes, working_tokens))
 
+    def set_archive_device_limit(self, device_bytes: int) -> None:
+        """Archive chunks allocated from now on go to pinned, device-mapped
+        host memory once the device chunks reach `device_bytes` (0: no limit)."""
+        _check(lib().nkv_bank_set_archive_device_limit(self._h, int(device_bytes)))
+
+    def archive_usage(self) -> tuple[int, int]:
+        """(device bytes, host bytes) of the archived slabs."""
+        d, h = C.c_uint64(), C.c_uint64()
+        _check(lib().nkv_bank_archive_usage(self._h, C.byref(d), C.byref(h)))
+        return int(d.value), int(h.value)
+
     def segment_bytes(self, desc: _abi.nkv_segment_desc) -> int:
         n = C.c_uint64()
         _check(lib().nkv_bank_segment_bytes(self._h, C.byref(desc), C.byref(n)))

@@ -149,6 +149,8 @@ SIGNATURES = {
     "nkv_bank_reserve": (C.c_int, [P, U64, U64]),
     "nkv_bank_segment_bytes": (C.c_int, [P, C.POINTER(nkv_segment_desc), C.POINTER(U64)]),
     "nkv_bank_decode_segment": (C.c_int, [P, U64, C.POINTER(P), C.POINTER(P)]),
+    "nkv_bank_set_archive_device_limit": (C.c_int, [P, U64]),
+    "nkv_bank_archive_usage": (C.c_int, [P, C.POINTER(U64), C.POINTER(U64)]),
     "nkv_bank_commit_decode": (C.c_int, [P, C.POINTER(nkv_segment_desc), I32, C.POINTER(P), C.POINTER(P), C.POINTER(P),
                                          C.POINTER(P)]),
     "nkv_bank_set_timing": (C.c_int, [P, I32]),

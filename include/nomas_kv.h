@@ -215,6 +215,18 @@ int nkv_bank_segment_bytes(const nkv_bank* bank, const nkv_segment_desc* seg, ui
  * into the caller's device buffers k_out[i] / v_out[i]. */
 int nkv_bank_decode_segment(nkv_bank* bank, uint64_t archive_pos, void* const* k_out, void* const* v_out);
 
+/* Tiered archive (no reference counterpart; the reference's archive lives in
+ * host memory of its own process).  Archive chunks allocated after this call
+ * go to device memory while the bank's device archive chunks total at most
+ * `device_bytes`, and to pinned host memory mapped into the device's address
+ * space beyond it; the kernels read and write host slabs over the host link,
+ * with the same results.  0 removes the limit.  Staged commits
+ * (nkv_bank_stage_segment) are refused while a limit is set.  Reserve
+ * (nkv_bank_reserve) after setting the limit to place the chunks up front. */
+int nkv_bank_set_archive_device_limit(nkv_bank* bank, uint64_t device_bytes);
+/* Bytes of the archived slabs (all local layers) in device / host memory. */
+int nkv_bank_archive_usage(nkv_bank* bank, uint64_t* device_bytes, uint64_t* host_bytes);
+
 /* nkv_bank_commit followed by nkv_bank_decode_segment of the segment it
  * archived (no reference counterpart as one call: commit_segment,
  * history.rs:458-463, then decode_segment, history.rs:308-338).  The new
