@@ -641,6 +641,7 @@ def run_gpu(args) -> None:
                      "unpark_frac": round(wsb / (pt[1] / 1e3) / 1e9 / link["h2d_gbs_per_gpu"], 4),
                      "bound": "host link: fractions of the measured pinned copy bandwidth per GPU with every rank "
                               "copying at once", "link": link}
+    attend = attend_measure(T, peaks) if extras else None
     gk = T.kernel_figures(kst, args.steps, peaks["hbm_gbs"])
     tiers = None
     if args.archive_device_gb > 0:
@@ -718,6 +719,7 @@ def run_gpu(args) -> None:
             "qvg": qvg,
             "producer": project,
             "archive_tiers": tiers,
+            "attend_history": attend,
             "gpu_launches": gk["launches"],
             "clocks": clk,
             "cpu_baseline": cpu,
@@ -726,6 +728,47 @@ def run_gpu(args) -> None:
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def attend_measure(T, peaks, reps: int = 3) -> dict:
+    """The fused consumer: one segment's queries (6,496 x 24 heads) attending
+    to layer 0's history (29,056 keys) straight from the INT8 archive
+    (nkv_bank_attend_history), beside torch's scaled_dot_product_attention
+    over the materialised bf16 working set (the library path it replaces)."""
+    import torch
+    import torch.nn.functional as F
+    dev = T.dev
+    g = torch.Generator(device=dev).manual_seed(11)
+    q = torch.randn((SEG_TOKENS, HEADS, HEAD_DIM), generator=g, device=dev).to(torch.bfloat16)
+    lay = T.bank.layer(0)
+    out, lse = lay.attend_history(q)  # warm-up
+    T.bank.kernel_stats(reset=True)
+    T.bank.set_timing(True)
+    for _ in range(reps):
+        lay.attend_history(q, out=out, lse=lse)
+    T.bank.set_timing(False)
+    n, ms = T.bank.kernel_stats(reset=True)["attend"]
+    ms /= max(n, 1)
+    k, v = lay.working_set()
+    keys = k.shape[1]
+    flops = 4.0 * SEG_TOKENS * keys * HEAD_DIM * HEADS
+    qt, kt, vt = q.unsqueeze(0).transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
+    F.scaled_dot_product_attention(qt, kt, vt)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        F.scaled_dot_product_attention(qt, kt, vt)
+    b.record()
+    torch.cuda.synchronize()
+    sdpa_ms = a.elapsed_time(b) / reps
+    tf = flops / (ms / 1e3) / 1e12
+    return {"kernel": "k_attend_int8 (tcgen05, INT8 K/V dequantized in shared memory)", "queries": SEG_TOKENS,
+            "history_keys": keys, "heads": HEADS, "ms": round(ms, 3), "tflops": round(tf, 1),
+            "frac_of_bf16_peak": round(tf / peaks["bf16_tflops"], 4), "peak_tflops": peaks["bf16_tflops"],
+            "sdpa_bf16_working_set_ms": round(sdpa_ms, 3),
+            "sdpa_tflops": round(flops / (sdpa_ms / 1e3) / 1e12, 1),
+            "int8_bytes_read": keys * HEADS * HEAD_DIM * 2 + keys * HEADS * 8,
+            "bf16_bytes_read_by_sdpa": keys * HEADS * HEAD_DIM * 4}
 
 
 def run_qvg_extra(args, world, rank, dev, peaks, steps: int = 3, warmup: int = 3) -> dict:

@@ -25,6 +25,7 @@ LIB = os.path.join(PKG, "nomas_kv", "libnomas_kv.so")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
 SOURCES = ["kernels_commit.cu", "kernels_gather.cu", "kernels_qvg.cu", "kernels_qvg_fit.cu", "kernels_project.cu",
+           "kernels_attn.cu",
            "bank.cpp", "abi.cpp",
            "noalloc.cu"]
 HEADERS = ["nkv_kernels.h", "nkv_device.cuh", "nkv_quant.cuh", "nkv_policy.h", "bank.h"]

@@ -98,6 +98,11 @@ int nkv_bank_commit(nkv_bank* bank, const nkv_segment_desc* seg, int32_t kv_dtyp
   });
 }
 
+int nkv_bank_attend_history(nkv_bank* bank, int32_t layer, const void* q, uint64_t q_len, float scale, float* out,
+                            float* lse) {
+  return guarded([&] { bank_of(bank).attend_history(layer, q, q_len, scale, out, lse); });
+}
+
 int nkv_bank_set_archive_device_limit(nkv_bank* bank, uint64_t device_bytes) {
   return guarded([&] { bank_of(bank).set_archive_device_limit(device_bytes); });
 }

@@ -306,6 +306,7 @@ Bank::~Bank() {
   if (h_flag_) cudaFreeHost(h_flag_);
   if (flag_ev_) cudaEventDestroy(flag_ev_);
   if (encoded_) cudaEventDestroy(encoded_);
+  if (d_attn_status_) cudaFree(d_attn_status_);
   for (auto p : p_host_)
     if (p) cudaFreeHost(p);
   stg_.release();
@@ -922,6 +923,7 @@ void Bank::finish_commit(const nkv_segment_desc& s, Rec r, int kv_dtype, const v
       ws_ = fresh, ws_cap_ = fresh_cap;
       fresh = nullptr;
     }
+    ws_runs_ = plan.runs;
     layout_ = std::move(plan.layout);
     valid_ = plan.valid;
     ws_current_ = true;
@@ -971,6 +973,7 @@ void Bank::rebuild_now() {
       ws_ = fresh, ws_cap_ = fresh_cap;
     }
   }
+  ws_runs_ = plan.runs;
   layout_ = std::move(plan.layout);
   valid_ = plan.valid;
   ws_current_ = true;
@@ -1028,6 +1031,7 @@ void Bank::park() {
   if (ws_) cudaFree(ws_);
   ws_ = nullptr, ws_cap_ = 0;
   p_layout_ = layout_;
+  p_runs_ = ws_runs_;
   p_valid_ = valid_;
   p_bytes_ = 2 * plane;
   layout_.clear();  // release_working_set (history.rs:539-544)
@@ -1070,6 +1074,7 @@ void Bank::unpark() {
     cudaEventDestroy(done);
   }
   layout_ = p_layout_;
+  ws_runs_ = p_runs_;
   valid_ = p_valid_;
   ws_current_ = p_ws_current_ && !changed_while_parked_;
   m_.h2d_bytes += p_bytes_;
@@ -1109,6 +1114,62 @@ void Bank::decode_segment(uint64_t pos, void* const* k_out, void* const* v_out) 
   const size_t outv_off = stg_.add(v_out, n_layers_ * sizeof(void*));
   stg_.upload(aux_, stream_);
   launch_gather_into(gt, outk_off, outv_off, p.valid, aligned, nullptr, NKV_KERNEL_SEGMENT_DECODE);
+}
+
+// Attention of q over this layer's history, straight from the INT8 archive
+// (kernels_attn.cu): key tiles of <= 128 tokens along the runs of the current
+// working set, so the keys are the working set's, in its order.
+void Bank::attend_history(int layer, const void* q, uint64_t q_len, float scale, float* out, float* lse) {
+  if (layer < 0 || layer >= n_layers_) fail(NKV_ERR_ARGUMENT, "layer out of range");
+  if (!q || !out || !lse) fail(NKV_ERR_ARGUMENT, "null q / out / lse pointer");
+  if (cfg_.storage != NKV_STORAGE_INT8) fail(NKV_ERR_INVALID_CONFIG, "history attention reads INT8 archives");
+  if (D_ != 128 || B_ != 1 || dtype_ != NKV_BF16)
+    fail(NKV_ERR_GEOMETRY, "history attention needs head_dim 128, batch 1 and a bf16 model");
+  if (parked_) fail(NKV_ERR_CACHE_STATE, "working set is parked; call unpark() before attention");
+  if (!ws_current_) fail(NKV_ERR_CACHE_STATE, "the working set is not the rebuild of the archive");
+  if (valid_ == 0) fail(NKV_ERR_CACHE_STATE, "no history to attend to");
+  if (q_len == 0) return;
+  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(out)) & 15u)
+    fail(NKV_ERR_ARGUMENT, "q and out must be 16-byte aligned");
+  DeviceScope ds(device_);
+  std::vector<AttnKeyTile> tiles;
+  for (const auto& rs : ws_runs_) {
+    const Rec& r = archive_[rs.rec];
+    const unsigned char* lb = r.slab + size_t(layer) * r.layer_stride;
+    for (int64_t t0 = 0; t0 < rs.ntok; t0 += 128) {
+      const int64_t tok = rs.src_tok + t0;
+      AttnKeyTile t{};
+      t.k_codes = lb + r.off[0] + tok * H_ * D_;
+      t.v_codes = lb + r.off[1] + tok * H_ * D_;
+      t.k_scales = reinterpret_cast<const float*>(lb + r.off[2]) + tok * H_;
+      t.v_scales = reinterpret_cast<const float*>(lb + r.off[3]) + tok * H_;
+      t.ntok = int32_t(std::min<int64_t>(128, rs.ntok - t0));
+      tiles.push_back(t);
+    }
+  }
+  if (!d_attn_status_) NKV_CUDA(cudaMalloc(&d_attn_status_, sizeof(uint32_t)));
+  stg_.begin(stream_);
+  const size_t toff = stg_.add(tiles.data(), tiles.size() * sizeof(AttnKeyTile));
+  stg_.upload(aux_, stream_);
+  NKV_CUDA(cudaMemsetAsync(d_attn_status_, 0, sizeof(uint32_t), stream_));
+  AttnArgs a{};
+  a.tiles = static_cast<const AttnKeyTile*>(stg_.dev(toff));
+  a.n_tiles = int32_t(tiles.size());
+  a.H = int32_t(H_);
+  a.q = static_cast<const uint16_t*>(q);
+  a.Lq = int64_t(q_len);
+  a.scale_log2 = scale * 1.4426950408889634f;
+  a.out = out;
+  a.lse = lse;
+  a.status = d_attn_status_;
+  tbegin(NKV_KERNEL_ATTEND);
+  NKV_CUDA(launch_attend_int8(a, stream_));
+  tend(NKV_KERNEL_ATTEND);
+  uint32_t st = 0;
+  NKV_CUDA(cudaMemcpyAsync(&st, d_attn_status_, sizeof(uint32_t), cudaMemcpyDeviceToHost, stream_));
+  NKV_CUDA(cudaStreamSynchronize(stream_));
+  collect_timing(false);
+  if (st) fail(NKV_ERR_CUDA, "history attention: a bounded wait ran out");
 }
 
 void Bank::synchronize() {

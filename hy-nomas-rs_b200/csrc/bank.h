@@ -163,6 +163,9 @@ class Bank {
   void park();
   void unpark();
   void decode_segment(uint64_t pos, void* const* k_out, void* const* v_out);
+  // attention of q (q_len, H, 128) bf16 over `layer`'s history read from
+  // the INT8 archive; out (q_len, H, 128) f32, lse (H, q_len) f32
+  void attend_history(int layer, const void* q, uint64_t q_len, float scale, float* out, float* lse);
   void synchronize();
   void reserve(uint64_t archive_bytes, uint64_t working_tokens);
   void set_archive_device_limit(uint64_t bytes);
@@ -227,6 +230,9 @@ class Bank {
   uint64_t total_frames_ = 0, tpf_ = 0;
   nkv_metrics m_{};
   std::vector<nkv_segment_layout> layout_;
+  std::vector<RunSpec> ws_runs_;  // the runs the current working set was gathered from
+  std::vector<RunSpec> p_runs_;   // ... of the parked one
+  uint32_t* d_attn_status_ = nullptr;
   uint64_t valid_ = 0;
 
   bool parked_ = false;

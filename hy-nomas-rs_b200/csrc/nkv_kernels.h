@@ -200,6 +200,33 @@ bool kv_project_shape_ok(int64_t M, int H, int D);
 // OR of flags[1..n] into flags[0] (a staged commit's per-layer status words
 // into the word the rebuild gather aborts on)
 cudaError_t launch_flag_reduce(uint32_t* flags, int n, cudaStream_t s);
+
+// ------------------------------------------------- history attention ---
+// A tile of <= 128 consecutive history keys inside one archived INT8
+// segment: the addresses of its first token (head 0) in the archive.
+struct AttnKeyTile {
+  const uint8_t* k_codes;
+  const uint8_t* v_codes;
+  const float* k_scales;
+  const float* v_scales;
+  int32_t ntok;
+  int32_t pad_;
+};
+// Attention of q (Lq, H, 128) bf16 over the history keys of `tiles`, head
+// by head: out (Lq, H, 128) f32 normalised, lse (H, Lq) f32 natural log;
+// bit 0 of *status is set when a bounded wait ran out.
+struct AttnArgs {
+  const AttnKeyTile* tiles;
+  int32_t n_tiles;
+  int32_t H;
+  const uint16_t* q;
+  int64_t Lq;
+  float scale_log2;  // softmax scale x log2(e)
+  float* out;
+  float* lse;
+  uint32_t* status;
+};
+cudaError_t launch_attend_int8(const AttnArgs& a, cudaStream_t s);
 cudaError_t launch_kv_project(const void* x, const void* wk, const void* wv, const KvProjectParams& p,
                               cudaStream_t stream);
 

@@ -332,6 +332,25 @@ class LayerCache:
         _check(lib().nkv_cache_metrics(self._bank._h, self._layer, C.byref(m)))
         return CacheMetrics.from_c(m)
 
+    def attend_history(self, q, scale: Optional[float] = None, out=None, lse=None):
+        """softmax(q k^T * scale) v over this layer's history, read from the
+        INT8 archive (nkv_bank_attend_history).  q: (q_len, H, 128) bf16 on
+        the bank's device; returns (out (q_len, H, 128) f32, lse (H, q_len)
+        f32).  scale defaults to 1 / sqrt(head_dim), the reference's."""
+        torch = _torch()
+        b = self._bank
+        if q.dim() != 3 or q.shape[1:] != (b.heads, b.head_dim) or q.dtype != torch.bfloat16 or not q.is_contiguous():
+            raise GeometryError(f"q must be a contiguous (q_len, {b.heads}, {b.head_dim}) bf16 tensor")
+        n = q.shape[0]
+        if out is None:
+            out = torch.empty((n, b.heads, b.head_dim), dtype=torch.float32, device=q.device)
+        if lse is None:
+            lse = torch.empty((b.heads, n), dtype=torch.float32, device=q.device)
+        s = float(scale) if scale is not None else 1.0 / math.sqrt(b.head_dim)
+        _check(lib().nkv_bank_attend_history(b._h, self._layer, C.c_void_p(q.data_ptr()), n, s,
+                                             C.c_void_p(out.data_ptr()), C.c_void_p(lse.data_ptr())))
+        return out, lse
+
     # QvgCodec::with_codebooks (qvg.rs:101-104) / codebooks readback
     def set_qvg_codebooks(self, cb) -> None:
         import numpy as np

@@ -26,8 +26,9 @@ NKV_SAMPLING_RECENT, NKV_SAMPLING_UNIFORM, NKV_SAMPLING_RECENT_MIX, NKV_SAMPLING
 NKV_KERNEL_QUANTIZE, NKV_KERNEL_FLOAT_ARCHIVE, NKV_KERNEL_QVG_ENCODE, NKV_KERNEL_GATHER = 0, 1, 2, 3
 NKV_KERNEL_SEGMENT_DECODE = 4
 NKV_KERNEL_QVG_FIT = 5
-NKV_KERNEL_COUNT = 6
-KERNEL_NAMES = ("quantize", "float_archive", "qvg_encode", "gather", "segment_decode", "qvg_fit")
+NKV_KERNEL_ATTEND = 6
+NKV_KERNEL_COUNT = 7
+KERNEL_NAMES = ("quantize", "float_archive", "qvg_encode", "gather", "segment_decode", "qvg_fit", "attend")
 NKV_NOALLOC_MAX_LAYERS = 64
 
 
@@ -149,6 +150,7 @@ SIGNATURES = {
     "nkv_bank_reserve": (C.c_int, [P, U64, U64]),
     "nkv_bank_segment_bytes": (C.c_int, [P, C.POINTER(nkv_segment_desc), C.POINTER(U64)]),
     "nkv_bank_decode_segment": (C.c_int, [P, U64, C.POINTER(P), C.POINTER(P)]),
+    "nkv_bank_attend_history": (C.c_int, [P, I32, P, U64, C.c_float, P, P]),
     "nkv_bank_set_archive_device_limit": (C.c_int, [P, U64]),
     "nkv_bank_archive_usage": (C.c_int, [P, C.POINTER(U64), C.POINTER(U64)]),
     "nkv_bank_commit_decode": (C.c_int, [P, C.POINTER(nkv_segment_desc), I32, C.POINTER(P), C.POINTER(P), C.POINTER(P),

@@ -147,7 +147,8 @@ enum {
   NKV_KERNEL_GATHER = 3,        /* rebuild: gather + dequant/decode                  */
   NKV_KERNEL_SEGMENT_DECODE = 4, /* nkv_bank_decode_segment: the same gather kernel  */
   NKV_KERNEL_QVG_FIT = 5,       /* first QVG commit: device codebook fit             */
-  NKV_KERNEL_COUNT = 6
+  NKV_KERNEL_ATTEND = 6,        /* nkv_bank_attend_history                          */
+  NKV_KERNEL_COUNT = 7
 };
 
 typedef struct nkv_bank nkv_bank;
@@ -214,6 +215,21 @@ int nkv_bank_segment_bytes(const nkv_bank* bank, const nkv_segment_desc* seg, ui
  * `archive_pos` for every local layer, written as model-dtype (B, L_seg, H, D)
  * into the caller's device buffers k_out[i] / v_out[i]. */
 int nkv_bank_decode_segment(nkv_bank* bank, uint64_t archive_pos, void* const* k_out, void* const* v_out);
+
+/* The history part of the reference's attention (modules/attention.rs:
+ * 143-189; every current token sees every history token, masks.rs) computed
+ * straight from the INT8 archive, without the materialised BF16 working set:
+ * softmax(q k^T * scale) v over this layer's working-set keys and values (the
+ * same tokens, dequantized as the rebuild does), head by head.  q: (q_len, H,
+ * 128) bf16 device; out: (q_len, H, 128) f32, normalised; lse: (H, q_len) f32,
+ * the natural-log log-sum-exp of each row's scaled scores, for merging with
+ * the current segment's (masked) part.  INT8 storage, head_dim 128, batch 1,
+ * bf16 model dtype; CacheState while parked, with an empty history or a
+ * working set that is not the archive's rebuild.  Runs on the bank's stream
+ * and returns after the kernel.  No reference counterpart as a separate
+ * call. */
+int nkv_bank_attend_history(nkv_bank* bank, int32_t layer, const void* q, uint64_t q_len, float scale, float* out,
+                            float* lse);
 
 /* Tiered archive (no reference counterpart; the reference's archive lives in
  * host memory of its own process).  Archive chunks allocated after this call
