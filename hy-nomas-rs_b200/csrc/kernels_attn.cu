@@ -37,13 +37,15 @@
 namespace nkv {
 namespace {
 
-constexpr int AQ = 128;                    // queries per CTA (TMEM lanes)
+constexpr int AQ = 128;                    // queries per half (TMEM lanes)
+constexpr int kHalves = 2;                 // query halves per CTA, sharing every K / V tile
 constexpr int AK = 128;                    // keys per tile
 constexpr int AD = 128;                    // head_dim
-constexpr int kAttnThreads = 128;
+constexpr int kAttnThreads = 256;
 constexpr int HALF_BYTES = 128 * 128;      // 128 rows x 64 bf16
 constexpr int TILE_BYTES = 2 * HALF_BYTES; // 32 KB
-constexpr int kAttnSmem = 4 * TILE_BYTES + 2 * AK * 4 + 64 + 1024;
+// Q (two halves), K (two buffers), V, P (two halves); barriers; alignment.
+constexpr int kAttnSmem = 7 * TILE_BYTES + 128 + 1024;
 constexpr uint64_t kAttnWaitNs = 1000000000ull;
 
 // S: f32 accumulate, bf16 A and B, both K-major, N = 128, M = 128.
@@ -151,126 +153,187 @@ __device__ __forceinline__ void tmem_store32(uint32_t taddr, const float* v) {
       : "memory");
 }
 
-// The rebuild's dequantization (int8.rs:139-155) of 8 codes into 4 bf16 pairs.
+// The rebuild's dequantization (int8.rs:139-155) of 8 codes into 4 bf16
+// pairs: RN((code - 128) * s) rounded to bf16.  code - 128 is exact as
+// (2^23 + code) - (2^23 + 128), with 2^23 + code assembled by one byte
+// permute; the product is the reference's one rounding; the values are
+// finite, where the hardware pair conversion is the library's round to
+// nearest even.
 __device__ __forceinline__ uint4 dequant8(uint2 codes, float s) {
   uint32_t w[4];
   const uint32_t c[2] = {codes.x, codes.y};
+  const float2 bias = make_float2(-8388736.0f, -8388736.0f);  // -(2^23 + 128)
+  const float2 s2 = make_float2(s, s);
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     const uint32_t word = c[j >> 1];
-    const int sh = (j & 1) * 16;
-    const float a = __fmul_rn(__fadd_rn(__fmul_rn((float)((word >> sh) & 0xFFu), 1.0f), -128.0f), s);
-    const float b = __fmul_rn(__fadd_rn(__fmul_rn((float)((word >> (sh + 8)) & 0xFFu), 1.0f), -128.0f), s);
-    w[j] = (dev::bf16_bits(a) & 0xFFFFu) | (dev::bf16_bits(b) << 16);
+    const uint32_t i0 = uint32_t((j & 1) * 2);
+    // bytes [0x4B, 0, 0, code]: 0x4B0000xx = 2^23 + code
+    const float a = __uint_as_float(__byte_perm(word, 0x4Bu, 0x4550u | i0));
+    const float b = __uint_as_float(__byte_perm(word, 0x4Bu, 0x4550u | (i0 + 1)));
+    const float2 v = __fmul2_rn(__fadd2_rn(make_float2(a, b), bias), s2);
+    w[j] = dev::bf16x2_bits_nonnan(v.x, v.y);
   }
   return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 }  // namespace
 
-// One CTA per (128-query tile, head).  Thread t owns query row t (TMEM lane
-// t) for the softmax and key row t of each tile for the dequantization.
+// One CTA per (256-query tile, head): two halves of 128 queries share each
+// dequantized K / V tile.  Warp w runs the softmax of half w / 4, rows
+// 32 (w % 4) + lane (its TMEM lane quadrant); thread j dequantizes key row
+// j % 128 of the next K tile (j < 128) or of the current V tile (j >= 128),
+// from codes loaded one iteration ahead.  Per tile t:
+//   1. thread 0 issues S_h = Q_h K_t^T for both halves (after P V of t - 1 in
+//      the tensor pipe);
+//   2. wait for P V of t - 1 (it read V and P);
+//   3. dequantize K_{t+1} (second K buffer) and V_t; load the next codes;
+//   4. wait for S; softmax, lazy rescale of O_h, P_h to shared memory;
+//   5. thread 0 issues O_h += P_h V_t.
 __global__ void __launch_bounds__(kAttnThreads, 1) k_attend_int8(const AttnArgs a) {
   extern __shared__ unsigned char attn_raw[];
   unsigned char* base =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(attn_raw) + 1023) & ~uintptr_t(1023));
-  unsigned char* Qs = base;
-  unsigned char* Ks = base + TILE_BYTES;
-  unsigned char* Vs = base + 2 * TILE_BYTES;
-  unsigned char* Ps = base + 3 * TILE_BYTES;
-  uint64_t* bar = reinterpret_cast<uint64_t*>(base + 4 * TILE_BYTES + 2 * AK * 4);
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 1);
+  unsigned char* Qs = base;                   // halves at 0 / TILE_BYTES
+  unsigned char* Kb = base + 2 * TILE_BYTES;  // buffers at 0 / TILE_BYTES
+  unsigned char* Vs = base + 4 * TILE_BYTES;
+  unsigned char* Ps = base + 5 * TILE_BYTES;  // halves at 0 / TILE_BYTES
+  uint64_t* bars = reinterpret_cast<uint64_t*>(base + 7 * TILE_BYTES);  // [0] S done, [1] P V done
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 2);
   volatile uint32_t* abort_flag = tslot + 1;
-  const int tid = threadIdx.x, warp = tid >> 5;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int hf = warp >> 2;                   // the softmax half of this warp
+  const int row = (warp & 3) * 32 + lane;     // its query row in the half
   const int h = blockIdx.y, H = a.H;
-  const int64_t q0 = int64_t(blockIdx.x) * AQ;
-  const uint32_t bar_a = smem_addr(bar);
+  const int64_t q0 = int64_t(blockIdx.x) * (kHalves * AQ);
+  const uint32_t barS = smem_addr(&bars[0]), barO = smem_addr(&bars[1]);
+  const int n = a.n_tiles;
 
   if (warp == 0) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;" ::"r"(smem_addr(tslot))
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_addr(tslot))
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
   if (tid == 0) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar_a) : "memory");
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(barS) : "memory");
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(barO) : "memory");
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     *abort_flag = 0u;
   }
-  // the query tile (zero rows past the end)
+  // the two query halves (zero rows past the end): thread j loads row j
   {
     const int64_t q = q0 + tid;
+    unsigned char* Qh = Qs + (tid >> 7) * TILE_BYTES;
 #pragma unroll
     for (int c = 0; c < 16; ++c) {
       uint4 v = make_uint4(0u, 0u, 0u, 0u);
       if (q < a.Lq) v = __ldg(reinterpret_cast<const uint4*>(a.q + (q * H + h) * AD) + c);
-      *reinterpret_cast<uint4*>(Qs + swz(tid, c)) = v;
+      *reinterpret_cast<uint4*>(Qh + swz(tid & 127, c)) = v;
     }
   }
+  // this thread's dequantization job: key row kr of K (tid < 128) or V
+  const int kr = tid & 127;
+  const bool is_v = tid >= 128;
+  uint4 codes[8];
+  float scale = 0.0f;
+  bool have = false;  // the registers hold the codes of the next job
+  // the descriptor of the job after that, fetched a job ahead so the code
+  // loads never wait for it
+  AttnKeyTile nextT{};
+  bool next_ok = false;
+  auto fetch_desc = [&](int tile) {
+    next_ok = tile < n;
+    if (next_ok) nextT = a.tiles[tile];
+  };
+  auto load_job = [&]() {  // the codes of the job whose descriptor is prefetched
+    have = next_ok && kr < nextT.ntok;
+    if (!have) return;
+    const int64_t r = int64_t(kr) * H + h;
+    const uint4* src = reinterpret_cast<const uint4*>((is_v ? nextT.v_codes : nextT.k_codes) + r * AD);
+#pragma unroll
+    for (int c = 0; c < 8; ++c) codes[c] = __ldg(src + c);
+    scale = __ldg((is_v ? nextT.v_scales : nextT.k_scales) + r);
+  };
+  auto store_job = [&](unsigned char* tile_base) {
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      uint4 lo = make_uint4(0u, 0u, 0u, 0u), hi = lo;
+      if (have) {
+        lo = dequant8(make_uint2(codes[c].x, codes[c].y), scale);
+        hi = dequant8(make_uint2(codes[c].z, codes[c].w), scale);
+      }
+      *reinterpret_cast<uint4*>(tile_base + swz(kr, 2 * c)) = lo;
+      *reinterpret_cast<uint4*>(tile_base + swz(kr, 2 * c + 1)) = hi;
+    }
+  };
+  // prologue: K_0 into buffer 0; next jobs: K_1 (rows < 128) and V_0
+  fetch_desc(0);
+  load_job();
+  if (!is_v) {
+    store_job(Kb);
+    fetch_desc(1);
+    load_job();
+    fetch_desc(2);
+  } else {
+    fetch_desc(1);
+  }
+  fence_async_smem();
   tc_before();
   __syncthreads();
   tc_after();
   const uint32_t tmem = *tslot;
-  const uint32_t lane_base = tmem + (uint32_t(warp * 32) << 16);
+  const uint32_t lane_q = uint32_t((warp & 3) * 32) << 16;
+  const uint32_t s_cols = tmem + lane_q + uint32_t(hf * 128);        // S_hf
+  const uint32_t o_cols = tmem + lane_q + uint32_t(256 + hf * 128);  // O_hf
 
-  // O accumulates in TMEM columns [128, 256) across the tiles.  Each row
-  // keeps the base-2 maximum m its exponentials are taken against and moves
-  // it only when a tile's maximum exceeds it by more than 8 (the unscaled
-  // terms then stay below 2^8); a warp with such a row rescales its O rows.
   float m = -INFINITY, l = 0.0f;
-  uint32_t phase = 0;
   bool ok = true;
-
-  for (int t = 0; t < a.n_tiles; ++t) {
-    const AttnKeyTile T = a.tiles[t];
-    // ---- K and V rows of the tile, dequantized as the rebuild does
-    {
-      const bool valid = tid < T.ntok;
-      const int64_t row = int64_t(tid) * H + h;
-      const float sk = valid ? __ldg(T.k_scales + row) : 0.0f;
-      const float sv = valid ? __ldg(T.v_scales + row) : 0.0f;
-      const uint2* kc = reinterpret_cast<const uint2*>(T.k_codes + row * AD);
-      const uint2* vc = reinterpret_cast<const uint2*>(T.v_codes + row * AD);
-#pragma unroll 4
-      for (int c = 0; c < 16; ++c) {
-        uint4 kb = make_uint4(0u, 0u, 0u, 0u), vb = kb;
-        if (valid) {
-          kb = dequant8(__ldg(kc + c), sk);
-          vb = dequant8(__ldg(vc + c), sv);
+  for (int t = 0; t < n; ++t) {
+    const int ntok = a.tiles[t].ntok;
+    // 1. S_h = Q_h K_t^T
+    if (tid == 0) {
+      const uint32_t kaddr = smem_addr(Kb + (t & 1) * TILE_BYTES);
+#pragma unroll
+      for (int hh = 0; hh < kHalves; ++hh)
+#pragma unroll
+        for (int kk = 0; kk < AD / 16; ++kk) {
+          const uint32_t off = uint32_t((kk >> 2) * HALF_BYTES + (kk & 3) * 32);
+          mma_f16(tmem + uint32_t(hh * 128), desc_k(smem_addr(Qs + hh * TILE_BYTES) + off), desc_k(kaddr + off),
+                  kIdescS, kk > 0 ? 1u : 0u);
         }
-        *reinterpret_cast<uint4*>(Ks + swz(tid, c)) = kb;
-        *reinterpret_cast<uint4*>(Vs + swz(tid, c)) = vb;
-      }
+      mma_commit(barS);
+    }
+    // 2. P V of the previous tile has read V and P
+    if (t > 0 && !bar_wait(barO, uint32_t(t - 1) & 1u)) *abort_flag = 1u;
+    tc_after();
+    // 3. dequantize K_{t+1} / V_t, load the codes of K_{t+2} / V_{t+1}
+    if (is_v) {
+      store_job(Vs);
+      load_job();  // V_{t+1}
+      fetch_desc(t + 2);
+    } else if (t + 1 < n) {
+      store_job(Kb + ((t + 1) & 1) * TILE_BYTES);
+      load_job();  // K_{t+2}
+      fetch_desc(t + 3);
     }
     fence_async_smem();
-    tc_before();
-    __syncthreads();
+    // 4. softmax of this thread's row of half hf (base-2 logits)
+    if (!bar_wait(barS, uint32_t(t) & 1u)) *abort_flag = 1u;
     tc_after();
-    // ---- S = Q K^T into TMEM columns [0, 128)
-    if (tid == 0) {
-#pragma unroll
-      for (int kk = 0; kk < AD / 16; ++kk) {
-        const uint32_t off = uint32_t((kk >> 2) * HALF_BYTES + (kk & 3) * 32);
-        mma_f16(tmem, desc_k(smem_addr(Qs) + off), desc_k(smem_addr(Ks) + off), kIdescS, kk > 0 ? 1u : 0u);
-      }
-      mma_commit(bar_a);
-    }
-    if (!bar_wait(bar_a, phase)) *abort_flag = 1u;
-    phase ^= 1u;
-    tc_after();
-    __syncthreads();
-    if (*abort_flag) {
-      ok = false;
-      break;
-    }
-    // ---- online softmax of this thread's row (base-2 logits)
     float mt = -INFINITY;
 #pragma unroll
     for (int ch = 0; ch < 4; ++ch) {
-      float s[32];
-      tmem_load32(lane_base + ch * 32, s);
+      float sv[32];
+      tmem_load32(s_cols + ch * 32, sv);
 #pragma unroll
       for (int j = 0; j < 32; ++j)
-        if (ch * 32 + j < T.ntok) mt = fmaxf(mt, s[j] * a.scale_log2);
+        if (ch * 32 + j < ntok) mt = fmaxf(mt, sv[j] * a.scale_log2);
     }
     const bool move = mt > m + 8.0f;
     const float mn = move ? mt : m;
@@ -279,29 +342,30 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attend_int8(const AttnArgs 
 #pragma unroll 1
       for (int ch = 0; ch < 4; ++ch) {
         float ov[32];
-        tmem_load32(lane_base + 128 + ch * 32, ov);
+        tmem_load32(o_cols + ch * 32, ov);
 #pragma unroll
         for (int j = 0; j < 32; ++j) ov[j] *= alpha;
-        tmem_store32(lane_base + 128 + ch * 32, ov);
+        tmem_store32(o_cols + ch * 32, ov);
       }
     }
     float lsum = 0.0f;
+    unsigned char* Ph = Ps + hf * TILE_BYTES;
 #pragma unroll
     for (int ch = 0; ch < 4; ++ch) {
-      float s[32];
-      tmem_load32(lane_base + ch * 32, s);
+      float sv[32];
+      tmem_load32(s_cols + ch * 32, sv);
       uint32_t w[16];
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const int k0 = ch * 32 + 2 * j;
-        const float p0 = k0 < T.ntok ? exp2f(s[2 * j] * a.scale_log2 - mn) : 0.0f;
-        const float p1 = k0 + 1 < T.ntok ? exp2f(s[2 * j + 1] * a.scale_log2 - mn) : 0.0f;
+        const float p0 = k0 < ntok ? fast_exp2(__fmaf_rn(sv[2 * j], a.scale_log2, -mn)) : 0.0f;
+        const float p1 = k0 + 1 < ntok ? fast_exp2(__fmaf_rn(sv[2 * j + 1], a.scale_log2, -mn)) : 0.0f;
         lsum += p0 + p1;
         w[j] = dev::bf16x2_bits_nonnan(p0, p1);
       }
 #pragma unroll
       for (int q = 0; q < 4; ++q)
-        *reinterpret_cast<uint4*>(Ps + swz(tid, ch * 4 + q)) =
+        *reinterpret_cast<uint4*>(Ph + swz(row, ch * 4 + q)) =
             make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
     }
     l = l * alpha + lsum;
@@ -310,33 +374,36 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attend_int8(const AttnArgs 
     tc_before();
     __syncthreads();
     tc_after();
-    // ---- O += P V into TMEM columns [128, 256)
-    if (tid == 0) {
-#pragma unroll
-      for (int kk = 0; kk < AK / 16; ++kk) {
-        const uint32_t aoff = uint32_t((kk >> 2) * HALF_BYTES + (kk & 3) * 32);
-        mma_f16(tmem + 128, desc_k(smem_addr(Ps) + aoff), desc_mn(smem_addr(Vs) + uint32_t(kk * 2 * 1024)),
-                kIdescO, (t > 0 || kk > 0) ? 1u : 0u);
-      }
-      mma_commit(bar_a);
-    }
-    if (!bar_wait(bar_a, phase)) *abort_flag = 1u;
-    phase ^= 1u;
-    tc_after();
-    __syncthreads();
     if (*abort_flag) {
       ok = false;
       break;
     }
+    // 5. O_h += P_h V_t
+    if (tid == 0) {
+      const uint32_t vaddr = smem_addr(Vs);
+#pragma unroll
+      for (int hh = 0; hh < kHalves; ++hh)
+#pragma unroll
+        for (int kk = 0; kk < AK / 16; ++kk) {
+          const uint32_t aoff = uint32_t((kk >> 2) * HALF_BYTES + (kk & 3) * 32);
+          mma_f16(tmem + uint32_t(256 + hh * 128), desc_k(smem_addr(Ps + hh * TILE_BYTES) + aoff),
+                  desc_mn(vaddr + uint32_t(kk * 2 * 1024)), kIdescO, (t > 0 || kk > 0) ? 1u : 0u);
+        }
+      mma_commit(barO);
+    }
   }
 
-  if (ok) {
-    const int64_t q = q0 + tid;
+  if (ok && n > 0) {
+    if (!bar_wait(barO, uint32_t(n - 1) & 1u)) ok = false;
+    tc_after();
+  }
+  if (ok && n > 0) {
+    const int64_t q = q0 + hf * AQ + row;
     const float inv = 1.0f / l;
 #pragma unroll 1
     for (int ch = 0; ch < 4; ++ch) {
       float ov[32];
-      tmem_load32(lane_base + 128 + ch * 32, ov);
+      tmem_load32(o_cols + ch * 32, ov);
       if (q < a.Lq) {
         float4* out = reinterpret_cast<float4*>(a.out + (q * H + h) * AD + ch * 32);
 #pragma unroll
@@ -345,20 +412,20 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attend_int8(const AttnArgs 
       }
     }
     if (q < a.Lq) a.lse[int64_t(h) * a.Lq + q] = (m + log2f(l)) * 0.69314718055994531f;
-  } else if (tid == 0) {
+  } else if (!ok && tid == 0) {
     atomicOr(a.status, 1u);
   }
   tc_before();
   __syncthreads();
   tc_after();
-  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;" ::"r"(tmem) : "memory");
+  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
 }
 
 cudaError_t launch_attend_int8(const AttnArgs& a, cudaStream_t s) {
   if (a.Lq <= 0 || a.H <= 0 || a.n_tiles <= 0) return cudaSuccess;
   cudaError_t e = cudaFuncSetAttribute(k_attend_int8, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem);
   if (e != cudaSuccess) return e;
-  dim3 grid(unsigned((a.Lq + AQ - 1) / AQ), unsigned(a.H));
+  dim3 grid(unsigned((a.Lq + kHalves * AQ - 1) / (kHalves * AQ)), unsigned(a.H));
   k_attend_int8<<<grid, kAttnThreads, kAttnSmem, s>>>(a);
   return cudaGetLastError();
 }
