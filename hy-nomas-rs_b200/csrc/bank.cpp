@@ -1122,6 +1122,7 @@ void Bank::decode_segment(uint64_t pos, void* const* k_out, void* const* v_out) 
 void Bank::attend_history(int layer, const void* q, uint64_t q_len, float scale, float* out, float* lse) {
   if (layer < 0 || layer >= n_layers_) fail(NKV_ERR_ARGUMENT, "layer out of range");
   if (!q || !out || !lse) fail(NKV_ERR_ARGUMENT, "null q / out / lse pointer");
+  if (!(scale > 0.0f) || !std::isfinite(scale)) fail(NKV_ERR_ARGUMENT, "scale must be finite and positive");
   if (cfg_.storage != NKV_STORAGE_INT8) fail(NKV_ERR_INVALID_CONFIG, "history attention reads INT8 archives");
   if (D_ != 128 || B_ != 1 || dtype_ != NKV_BF16)
     fail(NKV_ERR_GEOMETRY, "history attention needs head_dim 128, batch 1 and a bf16 model");

@@ -41,11 +41,14 @@ constexpr int AQ = 128;                    // queries per half (TMEM lanes)
 constexpr int kHalves = 2;                 // query halves per CTA, sharing every K / V tile
 constexpr int AK = 128;                    // keys per tile
 constexpr int AD = 128;                    // head_dim
-constexpr int kAttnThreads = 256;
+// warps 0-7 softmax (half = warp / 4), 8-11 dequantization, 12 MMA issue
+constexpr int kSoftmaxWarps = 8, kDequantWarps = 4;
+constexpr int kMmaWarp = kSoftmaxWarps + kDequantWarps;
+constexpr int kAttnThreads = 32 * (kMmaWarp + 1);
 constexpr int HALF_BYTES = 128 * 128;      // 128 rows x 64 bf16
 constexpr int TILE_BYTES = 2 * HALF_BYTES; // 32 KB
-// Q (two halves), K (two buffers), V, P (two halves); barriers; alignment.
-constexpr int kAttnSmem = 7 * TILE_BYTES + 128 + 1024;
+// Q (two halves), K and V (two buffers each); barriers; alignment.
+constexpr int kAttnSmem = 6 * TILE_BYTES + 256 + 1024;
 constexpr uint64_t kAttnWaitNs = 1000000000ull;
 
 // S: f32 accumulate, bf16 A and B, both K-major, N = 128, M = 128.
@@ -153,6 +156,32 @@ __device__ __forceinline__ void tmem_store32(uint32_t taddr, const float* v) {
       : "memory");
 }
 
+// Store 16 32-bit columns (32 packed bf16) to this thread's TMEM lane.
+__device__ __forceinline__ void tmem_store16(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_store_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// D (TMEM) += A (TMEM) x B (shared memory descriptor).
+__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc,
+                                           uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc));
+}
+
+__device__ __forceinline__ void bar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
 // The rebuild's dequantization (int8.rs:139-155) of 8 codes into 4 bf16
 // pairs: RN((code - 128) * s) rounded to bf16.  code - 128 is exact as
 // (2^23 + code) - (2^23 + 128), with 2^23 + code assembled by one byte
@@ -186,48 +215,59 @@ __device__ __forceinline__ float fast_exp2(float x) {
 }  // namespace
 
 // One CTA per (256-query tile, head): two halves of 128 queries share each
-// dequantized K / V tile.  Warp w runs the softmax of half w / 4, rows
-// 32 (w % 4) + lane (its TMEM lane quadrant); thread j dequantizes key row
-// j % 128 of the next K tile (j < 128) or of the current V tile (j >= 128),
-// from codes loaded one iteration ahead.  Per tile t:
-//   1. thread 0 issues S_h = Q_h K_t^T for both halves (after P V of t - 1 in
-//      the tensor pipe);
-//   2. wait for P V of t - 1 (it read V and P);
-//   3. dequantize K_{t+1} (second K buffer) and V_t; load the next codes;
-//   4. wait for S; softmax, lazy rescale of O_h, P_h to shared memory;
-//   5. thread 0 issues O_h += P_h V_t.
+// dequantized K / V tile.  Warp roles:
+//  * warps 0-7 (softmax): half w / 4, row 32 (w % 4) + lane of that half (its
+//    TMEM lane quadrant).  Per tile: wait for S_h, take the row maximum, move
+//    the row's reference maximum (and rescale its O_h row in TMEM) only when
+//    the tile exceeds it by more than 8 (base 2), write the bf16 P_h row into
+//    the first 64 columns of S_h (a packed pair per column), arrive on P_h;
+//  * warps 8-11 (dequantization): thread j dequantizes key row j of K_t and of
+//    V_t into the tile's buffer (two buffers each), codes loaded a tile ahead;
+//  * warp 12, lane 0 (MMA issue), in the order
+//      S_0(t) S_1(t) | PV_0(t) S_0(t+1) | PV_1(t) S_1(t+1) | ...
+//    so one half's softmax runs while the tensor pipe serves the other half.
+// TMEM: S_0 / P_0 columns [0, 128), S_1 / P_1 [128, 256), O_0 [256, 384),
+// O_1 [384, 512).  An MMA reads P_h from TMEM (the A operand) and V from
+// shared memory; MMAs run in issue order, so S_h(t+1) overwrites P_h(t) only
+// after PV_h(t) read it, and S_h(t+1) completing implies PV_h(t) completed.
 __global__ void __launch_bounds__(kAttnThreads, 1) k_attend_int8(const AttnArgs a) {
   extern __shared__ unsigned char attn_raw[];
   unsigned char* base =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(attn_raw) + 1023) & ~uintptr_t(1023));
   unsigned char* Qs = base;                   // halves at 0 / TILE_BYTES
   unsigned char* Kb = base + 2 * TILE_BYTES;  // buffers at 0 / TILE_BYTES
-  unsigned char* Vs = base + 4 * TILE_BYTES;
-  unsigned char* Ps = base + 5 * TILE_BYTES;  // halves at 0 / TILE_BYTES
-  uint64_t* bars = reinterpret_cast<uint64_t*>(base + 7 * TILE_BYTES);  // [0] S done, [1] P V done
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 2);
+  unsigned char* Vb = base + 4 * TILE_BYTES;  // buffers at 0 / TILE_BYTES
+  // barriers: 0-1 S full (half), 2-3 P full (half), 4-5 K full (buffer),
+  // 6-7 V full, 8-9 K empty, 10-11 V empty, 12 O done
+  uint64_t* bars = reinterpret_cast<uint64_t*>(base + 6 * TILE_BYTES);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 16);
   volatile uint32_t* abort_flag = tslot + 1;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int hf = warp >> 2;                   // the softmax half of this warp
-  const int row = (warp & 3) * 32 + lane;     // its query row in the half
   const int h = blockIdx.y, H = a.H;
   const int64_t q0 = int64_t(blockIdx.x) * (kHalves * AQ);
-  const uint32_t barS = smem_addr(&bars[0]), barO = smem_addr(&bars[1]);
   const int n = a.n_tiles;
+  auto B = [&](int i) { return smem_addr(&bars[i]); };
 
-  if (warp == 0) {
+  if (warp == kMmaWarp) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_addr(tslot))
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
   if (tid == 0) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(barS) : "memory");
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(barO) : "memory");
+    for (int i = 0; i < 2; ++i) {
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(B(0 + i)) : "memory");
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(B(2 + i)), "r"(32 * kSoftmaxWarps / 2) : "memory");
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(B(4 + i)), "r"(32 * kDequantWarps) : "memory");
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(B(6 + i)), "r"(32 * kDequantWarps) : "memory");
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(B(8 + i)) : "memory");
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(B(10 + i)) : "memory");
+    }
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(B(12)) : "memory");
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     *abort_flag = 0u;
   }
-  // the two query halves (zero rows past the end): thread j loads row j
-  {
+  // the two query halves (zero rows past the end): softmax thread j loads row j
+  if (warp < kSoftmaxWarps) {
     const int64_t q = q0 + tid;
     unsigned char* Qh = Qs + (tid >> 7) * TILE_BYTES;
 #pragma unroll
@@ -236,189 +276,244 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attend_int8(const AttnArgs 
       if (q < a.Lq) v = __ldg(reinterpret_cast<const uint4*>(a.q + (q * H + h) * AD) + c);
       *reinterpret_cast<uint4*>(Qh + swz(tid & 127, c)) = v;
     }
+    fence_async_smem();
   }
-  // this thread's dequantization job: key row kr of K (tid < 128) or V
-  const int kr = tid & 127;
-  const bool is_v = tid >= 128;
-  uint4 codes[8];
-  float scale = 0.0f;
-  bool have = false;  // the registers hold the codes of the next job
-  // the descriptor of the job after that, fetched a job ahead so the code
-  // loads never wait for it
-  AttnKeyTile nextT{};
-  bool next_ok = false;
-  auto fetch_desc = [&](int tile) {
-    next_ok = tile < n;
-    if (next_ok) nextT = a.tiles[tile];
-  };
-  auto load_job = [&]() {  // the codes of the job whose descriptor is prefetched
-    have = next_ok && kr < nextT.ntok;
-    if (!have) return;
-    const int64_t r = int64_t(kr) * H + h;
-    const uint4* src = reinterpret_cast<const uint4*>((is_v ? nextT.v_codes : nextT.k_codes) + r * AD);
-#pragma unroll
-    for (int c = 0; c < 8; ++c) codes[c] = __ldg(src + c);
-    scale = __ldg((is_v ? nextT.v_scales : nextT.k_scales) + r);
-  };
-  auto store_job = [&](unsigned char* tile_base) {
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      uint4 lo = make_uint4(0u, 0u, 0u, 0u), hi = lo;
-      if (have) {
-        lo = dequant8(make_uint2(codes[c].x, codes[c].y), scale);
-        hi = dequant8(make_uint2(codes[c].z, codes[c].w), scale);
-      }
-      *reinterpret_cast<uint4*>(tile_base + swz(kr, 2 * c)) = lo;
-      *reinterpret_cast<uint4*>(tile_base + swz(kr, 2 * c + 1)) = hi;
-    }
-  };
-  // prologue: K_0 into buffer 0; next jobs: K_1 (rows < 128) and V_0
-  fetch_desc(0);
-  load_job();
-  if (!is_v) {
-    store_job(Kb);
-    fetch_desc(1);
-    load_job();
-    fetch_desc(2);
-  } else {
-    fetch_desc(1);
-  }
-  fence_async_smem();
   tc_before();
   __syncthreads();
   tc_after();
   const uint32_t tmem = *tslot;
-  const uint32_t lane_q = uint32_t((warp & 3) * 32) << 16;
-  const uint32_t s_cols = tmem + lane_q + uint32_t(hf * 128);        // S_hf
-  const uint32_t o_cols = tmem + lane_q + uint32_t(256 + hf * 128);  // O_hf
-
-  float m = -INFINITY, l = 0.0f;
   bool ok = true;
-  for (int t = 0; t < n; ++t) {
-    const int ntok = a.tiles[t].ntok;
-    // 1. S_h = Q_h K_t^T
-    if (tid == 0) {
-      const uint32_t kaddr = smem_addr(Kb + (t & 1) * TILE_BYTES);
-#pragma unroll
-      for (int hh = 0; hh < kHalves; ++hh)
+  auto fail = [&]() {
+    *abort_flag = 1u;
+    ok = false;
+  };
+
+  if (warp == kMmaWarp) {
+    // ------------------------------------------------------------ MMA issue
+    if (lane == 0 && n > 0) {
+      auto issue_s = [&](int t, int hh) {
+        const uint32_t kaddr = smem_addr(Kb + (t & 1) * TILE_BYTES);
+        const uint32_t qaddr = smem_addr(Qs + hh * TILE_BYTES);
 #pragma unroll
         for (int kk = 0; kk < AD / 16; ++kk) {
           const uint32_t off = uint32_t((kk >> 2) * HALF_BYTES + (kk & 3) * 32);
-          mma_f16(tmem + uint32_t(hh * 128), desc_k(smem_addr(Qs + hh * TILE_BYTES) + off), desc_k(kaddr + off),
-                  kIdescS, kk > 0 ? 1u : 0u);
+          mma_f16(tmem + uint32_t(hh * 128), desc_k(qaddr + off), desc_k(kaddr + off), kIdescS, kk > 0 ? 1u : 0u);
         }
-      mma_commit(barS);
-    }
-    // 2. P V of the previous tile has read V and P
-    if (t > 0 && !bar_wait(barO, uint32_t(t - 1) & 1u)) *abort_flag = 1u;
-    tc_after();
-    // 3. dequantize K_{t+1} / V_t, load the codes of K_{t+2} / V_{t+1}
-    if (is_v) {
-      store_job(Vs);
-      load_job();  // V_{t+1}
-      fetch_desc(t + 2);
-    } else if (t + 1 < n) {
-      store_job(Kb + ((t + 1) & 1) * TILE_BYTES);
-      load_job();  // K_{t+2}
-      fetch_desc(t + 3);
-    }
-    fence_async_smem();
-    // 4. softmax of this thread's row of half hf (base-2 logits)
-    if (!bar_wait(barS, uint32_t(t) & 1u)) *abort_flag = 1u;
-    tc_after();
-    float mt = -INFINITY;
+      };
+      auto issue_pv = [&](int t, int hh) {
+        const uint32_t vaddr = smem_addr(Vb + (t & 1) * TILE_BYTES);
 #pragma unroll
-    for (int ch = 0; ch < 4; ++ch) {
-      float sv[32];
-      tmem_load32(s_cols + ch * 32, sv);
-#pragma unroll
-      for (int j = 0; j < 32; ++j)
-        if (ch * 32 + j < ntok) mt = fmaxf(mt, sv[j] * a.scale_log2);
+        for (int kk = 0; kk < AK / 16; ++kk)
+          mma_f16_ts(tmem + uint32_t(256 + hh * 128), tmem + uint32_t(hh * 128 + kk * 8),
+                     desc_mn(vaddr + uint32_t(kk * 2 * 1024)), kIdescO, (t > 0 || kk > 0) ? 1u : 0u);
+      };
+      if (!bar_wait(B(4), 0)) fail();
+      tc_after();
+      if (ok) {
+        issue_s(0, 0);
+        mma_commit(B(0));
+        issue_s(0, 1);
+        mma_commit(B(1));
+        mma_commit(B(8));
+      }
+      for (int t = 0; t < n && ok && !*abort_flag; ++t) {
+        const uint32_t bt = uint32_t(t >> 1) & 1u;
+        if (!bar_wait(B(6 + (t & 1)), bt) || !bar_wait(B(2), uint32_t(t) & 1u)) {
+          fail();
+          break;
+        }
+        tc_after();
+        issue_pv(t, 0);
+        if (t + 1 < n) {
+          if (!bar_wait(B(4 + ((t + 1) & 1)), uint32_t((t + 1) >> 1) & 1u)) {
+            fail();
+            break;
+          }
+          tc_after();
+          issue_s(t + 1, 0);
+          mma_commit(B(0));
+        }
+        if (!bar_wait(B(3), uint32_t(t) & 1u)) {
+          fail();
+          break;
+        }
+        tc_after();
+        issue_pv(t, 1);
+        mma_commit(B(10 + (t & 1)));
+        if (t + 1 < n) {
+          issue_s(t + 1, 1);
+          mma_commit(B(1));
+          mma_commit(B(8 + ((t + 1) & 1)));
+        }
+      }
+      mma_commit(B(12));
     }
-    const bool move = mt > m + 8.0f;
-    const float mn = move ? mt : m;
-    const float alpha = move ? exp2f(m - mn) : 1.0f;  // 0 on the first tile
-    if (t > 0 && __any_sync(0xFFFFFFFFu, move)) {
-#pragma unroll 1
+  } else if (warp >= kSoftmaxWarps) {
+    // ---------------------------------------------------- dequantization
+    const int kr = tid - 32 * kSoftmaxWarps;  // key row 0..127
+    uint4 kc[8], vc[8];
+    float ks = 0.0f, vs = 0.0f;
+    bool have = false;
+    auto load = [&](int t) {
+      have = false;
+      if (t >= n) return;
+      const AttnKeyTile T = a.tiles[t];
+      if (kr >= T.ntok) return;
+      const int64_t r = int64_t(kr) * H + h;
+      const uint4* k4 = reinterpret_cast<const uint4*>(T.k_codes + r * AD);
+      const uint4* v4 = reinterpret_cast<const uint4*>(T.v_codes + r * AD);
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        kc[c] = __ldg(k4 + c);
+        vc[c] = __ldg(v4 + c);
+      }
+      ks = __ldg(T.k_scales + r);
+      vs = __ldg(T.v_scales + r);
+      have = true;
+    };
+    load(0);
+    for (int t = 0; t < n; ++t) {
+      const int b = t & 1;
+      const uint32_t pe = uint32_t((t >> 1) - 1) & 1u;  // the buffer's previous use, tile t - 2
+      if (t >= 2 && !bar_wait(B(8 + b), pe)) {
+        fail();
+        break;
+      }
+      {
+        unsigned char* tile = Kb + b * TILE_BYTES;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          uint4 lo = make_uint4(0u, 0u, 0u, 0u), hi = lo;
+          if (have) {
+            lo = dequant8(make_uint2(kc[c].x, kc[c].y), ks);
+            hi = dequant8(make_uint2(kc[c].z, kc[c].w), ks);
+          }
+          *reinterpret_cast<uint4*>(tile + swz(kr, 2 * c)) = lo;
+          *reinterpret_cast<uint4*>(tile + swz(kr, 2 * c + 1)) = hi;
+        }
+        fence_async_smem();
+      }
+      bar_arrive(B(4 + b));
+      if (t >= 2 && !bar_wait(B(10 + b), pe)) {
+        fail();
+        break;
+      }
+      {
+        unsigned char* tile = Vb + b * TILE_BYTES;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          uint4 lo = make_uint4(0u, 0u, 0u, 0u), hi = lo;
+          if (have) {
+            lo = dequant8(make_uint2(vc[c].x, vc[c].y), vs);
+            hi = dequant8(make_uint2(vc[c].z, vc[c].w), vs);
+          }
+          *reinterpret_cast<uint4*>(tile + swz(kr, 2 * c)) = lo;
+          *reinterpret_cast<uint4*>(tile + swz(kr, 2 * c + 1)) = hi;
+        }
+        fence_async_smem();
+      }
+      bar_arrive(B(6 + b));
+      load(t + 1);
+      if (*abort_flag) break;
+    }
+  } else {
+    // ------------------------------------------------------------ softmax
+    const int hf = warp >> 2;
+    const int row = (warp & 3) * 32 + lane;
+    const uint32_t lane_q = uint32_t((warp & 3) * 32) << 16;
+    const uint32_t s_cols = tmem + lane_q + uint32_t(hf * 128);
+    const uint32_t o_cols = tmem + lane_q + uint32_t(256 + hf * 128);
+    float m = -INFINITY, l = 0.0f;
+    for (int t = 0; t < n; ++t) {
+      const int ntok = a.tiles[t].ntok;
+      if (!bar_wait(B(hf), uint32_t(t) & 1u)) {
+        fail();
+        break;
+      }
+      tc_after();
+      // row maximum of the raw scores (the scale is positive), four chains
+      const bool full = ntok == AK;
+      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
       for (int ch = 0; ch < 4; ++ch) {
-        float ov[32];
-        tmem_load32(o_cols + ch * 32, ov);
+        float sv[32];
+        tmem_load32(s_cols + ch * 32, sv);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) ov[j] *= alpha;
-        tmem_store32(o_cols + ch * 32, ov);
+        for (int j = 0; j < 32; ++j)
+          if (full || ch * 32 + j < ntok) mx[j & 3] = fmaxf(mx[j & 3], sv[j]);
       }
-    }
-    float lsum = 0.0f;
-    unsigned char* Ph = Ps + hf * TILE_BYTES;
-#pragma unroll
-    for (int ch = 0; ch < 4; ++ch) {
-      float sv[32];
-      tmem_load32(s_cols + ch * 32, sv);
-      uint32_t w[16];
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int k0 = ch * 32 + 2 * j;
-        const float p0 = k0 < ntok ? fast_exp2(__fmaf_rn(sv[2 * j], a.scale_log2, -mn)) : 0.0f;
-        const float p1 = k0 + 1 < ntok ? fast_exp2(__fmaf_rn(sv[2 * j + 1], a.scale_log2, -mn)) : 0.0f;
-        lsum += p0 + p1;
-        w[j] = dev::bf16x2_bits_nonnan(p0, p1);
-      }
-#pragma unroll
-      for (int q = 0; q < 4; ++q)
-        *reinterpret_cast<uint4*>(Ph + swz(row, ch * 4 + q)) =
-            make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
-    }
-    l = l * alpha + lsum;
-    m = mn;
-    fence_async_smem();
-    tc_before();
-    __syncthreads();
-    tc_after();
-    if (*abort_flag) {
-      ok = false;
-      break;
-    }
-    // 5. O_h += P_h V_t
-    if (tid == 0) {
-      const uint32_t vaddr = smem_addr(Vs);
-#pragma unroll
-      for (int hh = 0; hh < kHalves; ++hh)
-#pragma unroll
-        for (int kk = 0; kk < AK / 16; ++kk) {
-          const uint32_t aoff = uint32_t((kk >> 2) * HALF_BYTES + (kk & 3) * 32);
-          mma_f16(tmem + uint32_t(256 + hh * 128), desc_k(smem_addr(Ps + hh * TILE_BYTES) + aoff),
-                  desc_mn(vaddr + uint32_t(kk * 2 * 1024)), kIdescO, (t > 0 || kk > 0) ? 1u : 0u);
-        }
-      mma_commit(barO);
-    }
-  }
-
-  if (ok && n > 0) {
-    if (!bar_wait(barO, uint32_t(n - 1) & 1u)) ok = false;
-    tc_after();
-  }
-  if (ok && n > 0) {
-    const int64_t q = q0 + hf * AQ + row;
-    const float inv = 1.0f / l;
+      const float mt = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * a.scale_log2;
+      const bool move = mt > m + 8.0f;
+      const float mn = move ? mt : m;
+      const float alpha = move ? exp2f(m - mn) : 1.0f;  // 0 on the first tile
+      if (t > 0 && __any_sync(0xFFFFFFFFu, move)) {
+        // PV_h(t - 1) completed before S_h(t) did
 #pragma unroll 1
-    for (int ch = 0; ch < 4; ++ch) {
-      float ov[32];
-      tmem_load32(o_cols + ch * 32, ov);
-      if (q < a.Lq) {
-        float4* out = reinterpret_cast<float4*>(a.out + (q * H + h) * AD + ch * 32);
+        for (int ch = 0; ch < 4; ++ch) {
+          float ov[32];
+          tmem_load32(o_cols + ch * 32, ov);
 #pragma unroll
-        for (int d = 0; d < 8; ++d)
-          out[d] = make_float4(ov[4 * d] * inv, ov[4 * d + 1] * inv, ov[4 * d + 2] * inv, ov[4 * d + 3] * inv);
+          for (int j = 0; j < 32; ++j) ov[j] *= alpha;
+          tmem_store32(o_cols + ch * 32, ov);
+        }
+      }
+      float ls[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      const float nm = -mn;
+#pragma unroll
+      for (int ch = 0; ch < 4; ++ch) {
+        float sv[32];
+        tmem_load32(s_cols + ch * 32, sv);
+        uint32_t w[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int k0 = ch * 32 + 2 * j;
+          float p0 = fast_exp2(__fmaf_rn(sv[2 * j], a.scale_log2, nm));
+          float p1 = fast_exp2(__fmaf_rn(sv[2 * j + 1], a.scale_log2, nm));
+          if (!full) {
+            p0 = k0 < ntok ? p0 : 0.0f;
+            p1 = k0 + 1 < ntok ? p1 : 0.0f;
+          }
+          ls[j & 3] += p0 + p1;
+          w[j] = dev::bf16x2_bits_nonnan(p0, p1);
+        }
+        // P columns [16 ch, 16 ch + 16) lie below the S columns read so far
+        tmem_store16(s_cols + ch * 16, w);
+      }
+      const float lsum = (ls[0] + ls[1]) + (ls[2] + ls[3]);
+      tmem_store_wait();
+      l = l * alpha + lsum;
+      m = mn;
+      tc_before();
+      bar_arrive(B(2 + hf));
+      if (*abort_flag) break;
+    }
+    if (!*abort_flag && n > 0) {
+      if (!bar_wait(B(12), 0)) fail();
+      tc_after();
+      if (ok) {
+        const int64_t q = q0 + hf * AQ + row;
+        const float inv = 1.0f / l;
+#pragma unroll 1
+        for (int ch = 0; ch < 4; ++ch) {
+          float ov[32];
+          tmem_load32(o_cols + ch * 32, ov);
+          if (q < a.Lq) {
+            float4* out = reinterpret_cast<float4*>(a.out + (q * H + h) * AD + ch * 32);
+#pragma unroll
+            for (int d = 0; d < 8; ++d)
+              out[d] =
+                  make_float4(ov[4 * d] * inv, ov[4 * d + 1] * inv, ov[4 * d + 2] * inv, ov[4 * d + 3] * inv);
+          }
+        }
+        if (q < a.Lq) a.lse[int64_t(h) * a.Lq + q] = (m + log2f(l)) * 0.69314718055994531f;
       }
     }
-    if (q < a.Lq) a.lse[int64_t(h) * a.Lq + q] = (m + log2f(l)) * 0.69314718055994531f;
-  } else if (!ok && tid == 0) {
-    atomicOr(a.status, 1u);
   }
   tc_before();
   __syncthreads();
   tc_after();
-  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
+  if (*abort_flag && tid == 0) atomicOr(a.status, 1u);
+  if (warp == kMmaWarp) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
 }
 
 cudaError_t launch_attend_int8(const AttnArgs& a, cudaStream_t s) {

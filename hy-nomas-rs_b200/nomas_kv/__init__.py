@@ -346,6 +346,9 @@ class LayerCache:
             out = torch.empty((n, b.heads, b.head_dim), dtype=torch.float32, device=q.device)
         if lse is None:
             lse = torch.empty((b.heads, n), dtype=torch.float32, device=q.device)
+        for t, shape in ((out, (n, b.heads, b.head_dim)), (lse, (b.heads, n))):
+            if tuple(t.shape) != shape or t.dtype != torch.float32 or not t.is_contiguous() or t.device != q.device:
+                raise GeometryError(f"out / lse must be contiguous f32 tensors of shape {shape} on {q.device}")
         s = float(scale) if scale is not None else 1.0 / math.sqrt(b.head_dim)
         _check(lib().nkv_bank_attend_history(b._h, self._layer, C.c_void_p(q.data_ptr()), n, s,
                                              C.c_void_p(out.data_ptr()), C.c_void_p(lse.data_ptr())))

@@ -224,8 +224,9 @@ int nkv_bank_decode_segment(nkv_bank* bank, uint64_t archive_pos, void* const* k
  * 128) bf16 device; out: (q_len, H, 128) f32, normalised; lse: (H, q_len) f32,
  * the natural-log log-sum-exp of each row's scaled scores, for merging with
  * the current segment's (masked) part.  INT8 storage, head_dim 128, batch 1,
- * bf16 model dtype; CacheState while parked, with an empty history or a
- * working set that is not the archive's rebuild.  Runs on the bank's stream
+ * bf16 model dtype, a finite positive scale; CacheState while parked, with
+ * an empty history or a working set that is not the archive's rebuild.  Runs
+ * on the bank's stream
  * and returns after the kernel.  No reference counterpart as a separate
  * call. */
 int nkv_bank_attend_history(nkv_bank* bank, int32_t layer, const void* q, uint64_t q_len, float scale, float* out,

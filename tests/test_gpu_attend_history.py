@@ -106,6 +106,12 @@ def test_attend_history_rejects_other_storage_and_empty_history(H):
     try:
         with pytest.raises(nk.CacheStateError, match="no history"):
             p.p.layer(0).attend_history(q)
+        assert p.commit() is None
+        for bad in (0.0, -0.1, float("inf"), float("nan")):
+            with pytest.raises(nk.ArgumentError, match="scale"):
+                p.p.layer(0).attend_history(q, bad)
+        with pytest.raises(nk.GeometryError, match="out / lse"):
+            p.p.layer(0).attend_history(q, out=torch.empty((7, 4, 128), device="cuda"))
     finally:
         p.close()
     spec = H.Spec(storage=nk.NKV_STORAGE_QVG, sampling=nk.NKV_SAMPLING_UNIFORM, past_frames=5)
