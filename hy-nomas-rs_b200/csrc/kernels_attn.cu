@@ -41,14 +41,22 @@ constexpr int AQ = 128;                    // queries per half (TMEM lanes)
 constexpr int kHalves = 2;                 // query halves per CTA, sharing every K / V tile
 constexpr int AK = 128;                    // keys per tile
 constexpr int AD = 128;                    // head_dim
-// warps 0-7 softmax (half = warp / 4), 8-11 dequantization, 12 MMA issue
+// warps 0-7 softmax (half = warp / 4), 8-11 dequantization, 12 MMA issue,
+// 13-15 idle (they complete the fourth warpgroup for the register split)
 constexpr int kSoftmaxWarps = 8, kDequantWarps = 4;
 constexpr int kMmaWarp = kSoftmaxWarps + kDequantWarps;
-constexpr int kAttnThreads = 32 * (kMmaWarp + 1);
+constexpr int kAttnThreads = 512;
+// Registers per thread after the split (setmaxnreg, per warpgroup): the
+// launch gives 512 x 128; softmax 2 x 128 x 168 + dequantization 128 x 128
+// + MMA / idle 128 x 48 = 65,536, exactly the launch's total.
+constexpr int kRegsLaunch = 128, kRegsSoftmax = 168, kRegsDequant = 128, kRegsOther = 48;
+static_assert(kRegsSoftmax * 256 + kRegsDequant * 128 + kRegsOther * 128 <= kRegsLaunch * kAttnThreads,
+              "register split exceeds the launch's registers");
 constexpr int HALF_BYTES = 128 * 128;      // 128 rows x 64 bf16
 constexpr int TILE_BYTES = 2 * HALF_BYTES; // 32 KB
 // Q (two halves), K and V (two buffers each); barriers; alignment.
 constexpr int kAttnSmem = 6 * TILE_BYTES + 256 + 1024;
+static_assert(kAttnSmem <= 232448, "shared memory");
 constexpr uint64_t kAttnWaitNs = 1000000000ull;
 
 // S: f32 accumulate, bf16 A and B, both K-major, N = 128, M = 128.
@@ -94,27 +102,6 @@ __device__ __forceinline__ bool bar_wait(uint32_t bar, uint32_t parity) {
 // `r` in a swizzled 128 x 128 bf16 tile.
 __device__ __forceinline__ uint32_t swz(int r, int c) {
   return uint32_t((c >> 3) * HALF_BYTES + (r >> 3) * 1024 + (r & 7) * 128 + (((c & 7) ^ (r & 7)) << 4));
-}
-
-// K-major SW128 descriptor (rows of 128 bytes, 8-row groups 1024 bytes apart).
-__device__ __forceinline__ uint64_t desc_k(uint32_t addr) {
-  return uint64_t((addr & 0x3FFFFu) >> 4) | (uint64_t(1) << 16) | (uint64_t(1024 >> 4) << 32) | (uint64_t(1) << 46) |
-         (uint64_t(2) << 61);
-}
-
-// MN-major SW128 descriptor: 64-element MN blocks LBO = 16 KB apart, 8-row K
-// groups SBO = 1024 bytes apart.
-__device__ __forceinline__ uint64_t desc_mn(uint32_t addr) {
-  return uint64_t((addr & 0x3FFFFu) >> 4) | (uint64_t(HALF_BYTES >> 4) << 16) | (uint64_t(1024 >> 4) << 32) |
-         (uint64_t(1) << 46) | (uint64_t(2) << 61);
-}
-
-__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a), "l"(b), "r"(idesc), "r"(acc));
 }
 
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
@@ -168,16 +155,6 @@ __device__ __forceinline__ void tmem_store16(uint32_t taddr, const uint32_t* r) 
 
 __device__ __forceinline__ void tmem_store_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-// D (TMEM) += A (TMEM) x B (shared memory descriptor).
-__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc,
-                                           uint32_t acc) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc));
-}
-
 __device__ __forceinline__ void bar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
@@ -204,6 +181,77 @@ __device__ __forceinline__ uint4 dequant8(uint2 codes, float s) {
     w[j] = dev::bf16x2_bits_nonnan(v.x, v.y);
   }
   return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// 32 consecutive f32 columns of this thread's TMEM lane, not waited for.
+__device__ __forceinline__ void tmem_load32_async(uint32_t taddr, float* v) {
+  uint32_t* r = reinterpret_cast<uint32_t*>(v);
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+}
+
+// The constant upper word of both descriptor forms: SBO 1024 bytes (bits
+// 32-45), descriptor version 1 (bit 46), 128-byte swizzle (bits 61-63).
+constexpr uint32_t kDescHi = (1024u >> 4) | (1u << 14) | (2u << 29);
+// Lower words: start address >> 4 (bits 0-13) and LBO (bits 16-29).  K-major
+// form (Q, K, P): rows of 128 bytes, 8-row groups SBO = 1024 bytes apart, LBO
+// unused (16 bytes).  MN-major form (V in P V): 64-element MN blocks LBO =
+// 16 KB apart, 8-row K groups SBO = 1024 bytes apart.  Adding (byte offset >>
+// 4) to a lower word moves the start address.
+__device__ __forceinline__ uint32_t desc_k_lo(uint32_t addr) { return ((addr & 0x3FFFFu) >> 4) | (1u << 16); }
+__device__ __forceinline__ uint32_t desc_mn_lo(uint32_t addr) {
+  return ((addr & 0x3FFFFu) >> 4) | (uint32_t(HALF_BYTES >> 4) << 16);
+}
+
+// SS MMA from descriptor lower words plus a start-address offset (16-byte units).
+__device__ __forceinline__ void mma_ss_lo(uint32_t d_tmem, uint32_t a_lo, uint32_t b_lo, uint32_t off, uint32_t idesc,
+                                          uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b32 al, bl;\n\t.reg .b64 da, db;\n\t"
+      "add.u32 al, %1, %5;\n\tadd.u32 bl, %2, %5;\n\t"
+      "mov.b64 da, {al, %6};\n\tmov.b64 db, {bl, %6};\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_lo), "r"(b_lo), "r"(idesc), "r"(acc), "r"(off), "n"(kDescHi));
+}
+
+// TS MMA (A from TMEM) with B from a descriptor lower word plus an offset.
+__device__ __forceinline__ void mma_ts_lo(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_lo, uint32_t off,
+                                          uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b32 bl;\n\t.reg .b64 db;\n\t"
+      "add.u32 bl, %2, %5;\n\tmov.b64 db, {bl, %6};\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], db, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "r"(b_lo), "r"(idesc), "r"(acc), "r"(off), "n"(kDescHi));
+}
+
+// One lane of the (converged) warp.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "elect.sync _|p, 0xFFFFFFFF;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(r));
+  return r != 0;
+}
+
+__device__ __forceinline__ void tmem_load_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
 }
 
 __device__ __forceinline__ float fast_exp2(float x) {
@@ -288,136 +336,146 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attend_int8(const AttnArgs 
     ok = false;
   };
 
-  if (warp == kMmaWarp) {
+  if (warp >= kMmaWarp) {
     // ------------------------------------------------------------ MMA issue
-    if (lane == 0 && n > 0) {
-      auto issue_s = [&](int t, int hh) {
-        const uint32_t kaddr = smem_addr(Kb + (t & 1) * TILE_BYTES);
-        const uint32_t qaddr = smem_addr(Qs + hh * TILE_BYTES);
-#pragma unroll
-        for (int kk = 0; kk < AD / 16; ++kk) {
-          const uint32_t off = uint32_t((kk >> 2) * HALF_BYTES + (kk & 3) * 32);
-          mma_f16(tmem + uint32_t(hh * 128), desc_k(qaddr + off), desc_k(kaddr + off), kIdescS, kk > 0 ? 1u : 0u);
-        }
-      };
-      auto issue_pv = [&](int t, int hh) {
-        const uint32_t vaddr = smem_addr(Vb + (t & 1) * TILE_BYTES);
-#pragma unroll
-        for (int kk = 0; kk < AK / 16; ++kk)
-          mma_f16_ts(tmem + uint32_t(256 + hh * 128), tmem + uint32_t(hh * 128 + kk * 8),
-                     desc_mn(vaddr + uint32_t(kk * 2 * 1024)), kIdescO, (t > 0 || kk > 0) ? 1u : 0u);
-      };
-      if (!bar_wait(B(4), 0)) fail();
-      tc_after();
-      if (ok) {
-        issue_s(0, 0);
-        mma_commit(B(0));
-        issue_s(0, 1);
-        mma_commit(B(1));
-        mma_commit(B(8));
-      }
-      for (int t = 0; t < n && ok && !*abort_flag; ++t) {
-        const uint32_t bt = uint32_t(t >> 1) & 1u;
-        if (!bar_wait(B(6 + (t & 1)), bt) || !bar_wait(B(2), uint32_t(t) & 1u)) {
-          fail();
-          break;
-        }
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsOther));
+    if (warp == kMmaWarp && n > 0) {
+      // The whole warp runs the schedule, so the descriptors are warp-uniform;
+      // one elected lane issues each batch of MMAs and its commits.  Lane 0
+      // waits and its outcome is the warp's.
+      const uint32_t dq0 = desc_k_lo(smem_addr(Qs)), dk0 = desc_k_lo(smem_addr(Kb)), dv0 = desc_mn_lo(smem_addr(Vb));
+      constexpr uint32_t kTileLo = TILE_BYTES >> 4;  // the second half / buffer
+      auto wait = [&](int i, uint32_t parity) {
+        int r = 1;
+        if (lane == 0) r = bar_wait(B(i), parity) ? 1 : 0;
+        r = __shfl_sync(0xFFFFFFFFu, r, 0);
+        if (!r) fail();
         tc_after();
-        issue_pv(t, 0);
-        if (t + 1 < n) {
-          if (!bar_wait(B(4 + ((t + 1) & 1)), uint32_t((t + 1) >> 1) & 1u)) {
-            fail();
-            break;
+        return r != 0;
+      };
+      // S_hh = Q_hh K_t^T, then the commits of `c0` / `c1` (-1: none)
+      auto issue_s = [&](int t, int hh, int c0, int c1) {
+        if (elect_one()) {
+#pragma unroll
+          for (int kk = 0; kk < AD / 16; ++kk) {
+            const uint32_t off = uint32_t(((kk >> 2) * HALF_BYTES + (kk & 3) * 32) >> 4);
+            mma_ss_lo(tmem + uint32_t(hh * 128), dq0 + uint32_t(hh) * kTileLo, dk0 + uint32_t(t & 1) * kTileLo, off,
+                      kIdescS, kk > 0 ? 1u : 0u);
           }
-          tc_after();
-          issue_s(t + 1, 0);
-          mma_commit(B(0));
+          if (c0 >= 0) mma_commit(B(c0));
+          if (c1 >= 0) mma_commit(B(c1));
         }
-        if (!bar_wait(B(3), uint32_t(t) & 1u)) {
-          fail();
-          break;
+        __syncwarp();
+      };
+      // O_hh += P_hh V_t (P_hh from TMEM), then the commit of `c0`
+      auto issue_pv = [&](int t, int hh, int c0) {
+        if (elect_one()) {
+#pragma unroll
+          for (int kk = 0; kk < AK / 16; ++kk)
+            mma_ts_lo(tmem + uint32_t(256 + hh * 128), tmem + uint32_t(hh * 128 + kk * 8),
+                      dv0 + uint32_t(t & 1) * kTileLo, uint32_t(kk * 2 * 1024 >> 4), kIdescO,
+                      (t > 0 || kk > 0) ? 1u : 0u);
+          if (c0 >= 0) mma_commit(B(c0));
         }
-        tc_after();
-        issue_pv(t, 1);
-        mma_commit(B(10 + (t & 1)));
-        if (t + 1 < n) {
-          issue_s(t + 1, 1);
-          mma_commit(B(1));
-          mma_commit(B(8 + ((t + 1) & 1)));
-        }
+        __syncwarp();
+      };
+      if (wait(4, 0)) {
+        issue_s(0, 0, 0, -1);
+        issue_s(0, 1, 1, 8);
       }
-      mma_commit(B(12));
+      for (int t = 0; t < n && ok; ++t) {
+        if (__shfl_sync(0xFFFFFFFFu, int(*abort_flag), 0)) break;
+        if (!wait(6 + (t & 1), uint32_t(t >> 1) & 1u) || !wait(2, uint32_t(t) & 1u)) break;
+        issue_pv(t, 0, -1);
+        if (t + 1 < n) {
+          if (!wait(4 + ((t + 1) & 1), uint32_t((t + 1) >> 1) & 1u)) break;
+          issue_s(t + 1, 0, 0, -1);
+        }
+        if (!wait(3, uint32_t(t) & 1u)) break;
+        issue_pv(t, 1, 10 + (t & 1));
+        if (t + 1 < n) issue_s(t + 1, 1, 1, 8 + ((t + 1) & 1));
+      }
+      if (elect_one()) mma_commit(B(12));
+      __syncwarp();
     }
   } else if (warp >= kSoftmaxWarps) {
     // ---------------------------------------------------- dequantization
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsDequant));
+    // Thread j owns key row j of every tile.  The K codes of tile t + 1 are
+    // requested right after K_t is written and the V codes right after V_t,
+    // so each load has the wait for the next buffer (about one tile of MMA
+    // work) to land; tile descriptors are read two tiles ahead.
     const int kr = tid - 32 * kSoftmaxWarps;  // key row 0..127
     uint4 kc[8], vc[8];
     float ks = 0.0f, vs = 0.0f;
-    bool have = false;
-    auto load = [&](int t) {
-      have = false;
-      if (t >= n) return;
-      const AttnKeyTile T = a.tiles[t];
-      if (kr >= T.ntok) return;
+    bool khave = false, vhave = false;
+    auto load_k = [&](const AttnKeyTile& T) {
+      khave = kr < T.ntok;
+      if (!khave) return;
       const int64_t r = int64_t(kr) * H + h;
       const uint4* k4 = reinterpret_cast<const uint4*>(T.k_codes + r * AD);
+#pragma unroll
+      for (int c = 0; c < 8; ++c) kc[c] = __ldg(k4 + c);
+      ks = __ldg(T.k_scales + r);
+    };
+    auto load_v = [&](const AttnKeyTile& T) {
+      vhave = kr < T.ntok;
+      if (!vhave) return;
+      const int64_t r = int64_t(kr) * H + h;
       const uint4* v4 = reinterpret_cast<const uint4*>(T.v_codes + r * AD);
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        kc[c] = __ldg(k4 + c);
-        vc[c] = __ldg(v4 + c);
-      }
-      ks = __ldg(T.k_scales + r);
+      for (int c = 0; c < 8; ++c) vc[c] = __ldg(v4 + c);
       vs = __ldg(T.v_scales + r);
-      have = true;
     };
-    load(0);
+    // the rebuild's dequantization (int8.rs:139-155) of row kr into a
+    // swizzled bf16 tile, zeros for rows past the tile's end
+    auto store = [&](unsigned char* tile, const uint4* w, float sc, bool hv) {
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        uint4 lo = make_uint4(0u, 0u, 0u, 0u), hi = lo;
+        if (hv) {
+          lo = dequant8(make_uint2(w[c].x, w[c].y), sc);
+          hi = dequant8(make_uint2(w[c].z, w[c].w), sc);
+        }
+        *reinterpret_cast<uint4*>(tile + swz(kr, 2 * c)) = lo;
+        *reinterpret_cast<uint4*>(tile + swz(kr, 2 * c + 1)) = hi;
+      }
+      fence_async_smem();
+    };
+    AttnKeyTile d1{};  // descriptor of tile t + 1
+    if (n > 0) {
+      const AttnKeyTile d0 = a.tiles[0];
+      load_k(d0);
+      load_v(d0);
+    }
+    if (n > 1) d1 = a.tiles[1];
     for (int t = 0; t < n; ++t) {
       const int b = t & 1;
       const uint32_t pe = uint32_t((t >> 1) - 1) & 1u;  // the buffer's previous use, tile t - 2
+      AttnKeyTile d2{};
+      if (t + 2 < n) d2 = a.tiles[t + 2];
+      // K_t into buffer b once S of tile t - 2 completed
       if (t >= 2 && !bar_wait(B(8 + b), pe)) {
         fail();
         break;
       }
-      {
-        unsigned char* tile = Kb + b * TILE_BYTES;
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          uint4 lo = make_uint4(0u, 0u, 0u, 0u), hi = lo;
-          if (have) {
-            lo = dequant8(make_uint2(kc[c].x, kc[c].y), ks);
-            hi = dequant8(make_uint2(kc[c].z, kc[c].w), ks);
-          }
-          *reinterpret_cast<uint4*>(tile + swz(kr, 2 * c)) = lo;
-          *reinterpret_cast<uint4*>(tile + swz(kr, 2 * c + 1)) = hi;
-        }
-        fence_async_smem();
-      }
+      store(Kb + b * TILE_BYTES, kc, ks, khave);
       bar_arrive(B(4 + b));
+      if (t + 1 < n) load_k(d1);
+      // V_t into buffer b once P V of tile t - 2 completed
       if (t >= 2 && !bar_wait(B(10 + b), pe)) {
         fail();
         break;
       }
-      {
-        unsigned char* tile = Vb + b * TILE_BYTES;
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          uint4 lo = make_uint4(0u, 0u, 0u, 0u), hi = lo;
-          if (have) {
-            lo = dequant8(make_uint2(vc[c].x, vc[c].y), vs);
-            hi = dequant8(make_uint2(vc[c].z, vc[c].w), vs);
-          }
-          *reinterpret_cast<uint4*>(tile + swz(kr, 2 * c)) = lo;
-          *reinterpret_cast<uint4*>(tile + swz(kr, 2 * c + 1)) = hi;
-        }
-        fence_async_smem();
-      }
+      store(Vb + b * TILE_BYTES, vc, vs, vhave);
       bar_arrive(B(6 + b));
-      load(t + 1);
+      if (t + 1 < n) load_v(d1);
+      d1 = d2;
       if (*abort_flag) break;
     }
   } else {
     // ------------------------------------------------------------ softmax
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsSoftmax));
     const int hf = warp >> 2;
     const int row = (warp & 3) * 32 + lane;
     const uint32_t lane_q = uint32_t((warp & 3) * 32) << 16;
@@ -431,23 +489,52 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attend_int8(const AttnArgs 
         break;
       }
       tc_after();
-      // row maximum of the raw scores (the scale is positive), four chains
-      const bool full = ntok == AK;
-      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      // the row's 128 scores in registers; keys past the tile's end at -inf
+      float sv[AK];
 #pragma unroll
-      for (int ch = 0; ch < 4; ++ch) {
-        float sv[32];
-        tmem_load32(s_cols + ch * 32, sv);
+      for (int ch = 0; ch < 4; ++ch) tmem_load32_async(s_cols + ch * 32, sv + ch * 32);
+      tmem_load_wait();
+      if (ntok < AK) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j)
-          if (full || ch * 32 + j < ntok) mx[j & 3] = fmaxf(mx[j & 3], sv[j]);
+        for (int j = 0; j < AK; ++j)
+          if (j >= ntok) sv[j] = -INFINITY;
       }
-      const float mt = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * a.scale_log2;
+      // row maximum of the raw scores (the scale is positive): eight chains
+      // of three-input maxima
+      float mx[8];
+#pragma unroll
+      for (int c = 0; c < 8; ++c) mx[c] = fmaxf(sv[c], sv[8 + c]);
+#pragma unroll
+      for (int j = 16; j < AK; j += 16)
+#pragma unroll
+        for (int c = 0; c < 8; ++c) mx[c] = max3(mx[c], sv[j + c], sv[j + 8 + c]);
+      const float mt =
+          max3(max3(mx[0], mx[1], mx[2]), max3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7])) * a.scale_log2;
       const bool move = mt > m + 8.0f;
       const float mn = move ? mt : m;
       const float alpha = move ? exp2f(m - mn) : 1.0f;  // 0 on the first tile
+      // P = 2^(s scale_log2 - mn) (masked keys give 0), packed bf16 pairs into
+      // the first 64 columns of S_h; the row sum in eight f32 partials
+      const float2 sc2 = make_float2(a.scale_log2, a.scale_log2), nm2 = make_float2(-mn, -mn);
+      float2 ls[4] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f),
+                      make_float2(0.0f, 0.0f)};
+#pragma unroll
+      for (int ch = 0; ch < 4; ++ch) {
+        uint32_t w[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int k0 = ch * 32 + 2 * j;
+          const float2 x = __ffma2_rn(make_float2(sv[k0], sv[k0 + 1]), sc2, nm2);
+          const float2 p = make_float2(fast_exp2(x.x), fast_exp2(x.y));
+          ls[j & 3] = __fadd2_rn(ls[j & 3], p);
+          w[j] = dev::bf16x2_bits_nonnan(p.x, p.y);
+        }
+        tmem_store16(s_cols + ch * 16, w);
+      }
+      const float2 l01 = __fadd2_rn(ls[0], ls[1]), l23 = __fadd2_rn(ls[2], ls[3]);
+      const float lsum = (l01.x + l01.y) + (l23.x + l23.y);
       if (t > 0 && __any_sync(0xFFFFFFFFu, move)) {
-        // PV_h(t - 1) completed before S_h(t) did
+        // O_h's row rescaled; PV_h(t - 1) completed before S_h(t) did
 #pragma unroll 1
         for (int ch = 0; ch < 4; ++ch) {
           float ov[32];
@@ -457,29 +544,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attend_int8(const AttnArgs 
           tmem_store32(o_cols + ch * 32, ov);
         }
       }
-      float ls[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-      const float nm = -mn;
-#pragma unroll
-      for (int ch = 0; ch < 4; ++ch) {
-        float sv[32];
-        tmem_load32(s_cols + ch * 32, sv);
-        uint32_t w[16];
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int k0 = ch * 32 + 2 * j;
-          float p0 = fast_exp2(__fmaf_rn(sv[2 * j], a.scale_log2, nm));
-          float p1 = fast_exp2(__fmaf_rn(sv[2 * j + 1], a.scale_log2, nm));
-          if (!full) {
-            p0 = k0 < ntok ? p0 : 0.0f;
-            p1 = k0 + 1 < ntok ? p1 : 0.0f;
-          }
-          ls[j & 3] += p0 + p1;
-          w[j] = dev::bf16x2_bits_nonnan(p0, p1);
-        }
-        // P columns [16 ch, 16 ch + 16) lie below the S columns read so far
-        tmem_store16(s_cols + ch * 16, w);
-      }
-      const float lsum = (ls[0] + ls[1]) + (ls[2] + ls[3]);
       tmem_store_wait();
       l = l * alpha + lsum;
       m = mn;
