@@ -247,6 +247,21 @@ __device__ __forceinline__ bool elect_one() {
 
 __device__ __forceinline__ void tmem_load_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// Threads 32 registers of an earlier unwaited TMEM load through an empty
+// volatile statement placed after tmem_load_wait(), so no use of them is
+// scheduled ahead of the wait.
+__device__ __forceinline__ void tmem_regs_after_wait(float* v) {
+  uint32_t* r = reinterpret_cast<uint32_t*>(v);
+  asm volatile(""
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
+                 "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]),
+                 "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+               :
+               : "memory");
+}
+
 
 __device__ __forceinline__ float max3(float a, float b, float c) {
   float d;
@@ -494,6 +509,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attend_int8(const AttnArgs 
 #pragma unroll
       for (int ch = 0; ch < 4; ++ch) tmem_load32_async(s_cols + ch * 32, sv + ch * 32);
       tmem_load_wait();
+#pragma unroll
+      for (int ch = 0; ch < 4; ++ch) tmem_regs_after_wait(sv + ch * 32);
       if (ntok < AK) {
 #pragma unroll
         for (int j = 0; j < AK; ++j)
@@ -584,6 +601,12 @@ cudaError_t launch_attend_int8(const AttnArgs& a, cudaStream_t s) {
   if (a.Lq <= 0 || a.H <= 0 || a.n_tiles <= 0) return cudaSuccess;
   cudaError_t e = cudaFuncSetAttribute(k_attend_int8, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem);
   if (e != cudaSuccess) return e;
+  // the register split's increase waits for registers the launch must hold:
+  // refuse a build whose launch count differs from the split's
+  cudaFuncAttributes fa{};
+  e = cudaFuncGetAttributes(&fa, k_attend_int8);
+  if (e != cudaSuccess) return e;
+  if (fa.numRegs != kRegsLaunch) return cudaErrorInvalidConfiguration;
   dim3 grid(unsigned((a.Lq + kHalves * AQ - 1) / (kHalves * AQ)), unsigned(a.H));
   k_attend_int8<<<grid, kAttnThreads, kAttnSmem, s>>>(a);
   return cudaGetLastError();

@@ -59,8 +59,17 @@ constexpr int A_BYTES = BM * BK * 2;      // 16 KB
 constexpr int B_BYTES = B_ROWS * BK * 2;  // 16 KB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int TMEM_COLS = 2 * BN;
-constexpr int kEpiWarps = 8;  // two per SM sub-partition: warps 2-5 head 0, 6-9 head 1 of a tile
-constexpr int kThreads = 32 * (2 + kEpiWarps);
+// Warp 0 TMA, warp 1 MMA, warps 2-3 idle (they complete the first warpgroup
+// for the register split), warps 4-11 the epilogue: two per SM
+// sub-partition, warps 4-7 head 0 and 8-11 head 1 of a tile.
+constexpr int kEpiWarps = 8, kEpiFirst = 4;
+constexpr int kThreads = 32 * (kEpiFirst + kEpiWarps);
+// Registers per thread after the split (setmaxnreg, per warpgroup): the
+// launch gives 384 x 168; the first warpgroup 128 x 88 + the epilogue
+// 256 x 208 = 64,512, exactly the launch's total.
+constexpr int kRegsLaunch = 168, kRegsCtl = 88, kRegsEpi = 208;
+static_assert(kRegsCtl * 128 + kRegsEpi * 32 * kEpiWarps <= kRegsLaunch * kThreads,
+              "register split exceeds the launch's registers");
 // Epilogue constants staged in shared memory ahead of each tile (cp.async,
 // overlapping the tile's main loop): the tile's 128 token rows of the rotary
 // cos / sin tables (the head-0 warp of a lane quadrant copies cos, the head-1
@@ -195,6 +204,17 @@ __device__ __forceinline__ void umma_bf16_pair(uint32_t d_tmem, uint64_t a, uint
 // MMAs issued so far have completed.
 __device__ __forceinline__ void umma_commit_pair(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+// One lane of the (converged) warp.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "elect.sync _|p, 0xFFFFFFFF;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(r));
+  return r != 0;
 }
 
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
@@ -429,7 +449,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  if (warp == 0) {
+  if (warp < kEpiFirst) {
+   asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsCtl));
+   if (warp == 0) {
     // ---------------------------------------------------- TMA producer
     if (lane == 0) {
       int stage = 0;
@@ -452,45 +474,62 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     // ---------------------------------------------------- MMA issuer (leader)
-    if (lane == 0 && rank == 0) {
+    // The whole warp runs the schedule, so the descriptors are warp-uniform;
+    // lane 0 waits (its outcome is the warp's) and one elected lane issues
+    // each stage's MMAs and commits.
+    if (rank == 0) {
+      auto wait = [&](uint32_t bar, uint32_t parity) {
+        int r = 1;
+        if (lane == 0) r = mbar_wait(bar, parity, abort_flag, p.err) ? 1 : 0;
+        r = __shfl_sync(0xFFFFFFFFu, r, 0);
+        tc_fence_after();
+        return r != 0;
+      };
       int stage = 0;
       uint32_t phase = 0;
       int buf = 0;
       uint32_t acc_phase = 0;
-      for (int t = pair; t < n_tiles && !*abort_flag; t += n_pairs) {
-        if (!mbar_wait(tempty_bar(buf), acc_phase ^ 1u, abort_flag, p.err)) break;
-        tc_fence_after();
+      for (int t = pair; t < n_tiles; t += n_pairs) {
+        if (__shfl_sync(0xFFFFFFFFu, int(*abort_flag), 0)) break;
+        if (!wait(tempty_bar(buf), acc_phase ^ 1u)) break;
         const uint32_t d_tmem = tmem_base + uint32_t(buf * BN);
         bool ok = true;
         for (int kb = 0; kb < kb_count; ++kb) {
-          if (!mbar_wait(full_bar(stage), phase, abort_flag, p.err)) {
+          if (!wait(full_bar(stage), phase)) {
             ok = false;
             break;
           }
-          tc_fence_after();
           const uint32_t a_addr = smem_base + stage * STAGE_BYTES;
           const uint64_t adesc = smem_desc(a_addr), bdesc = smem_desc(a_addr + A_BYTES);
+          if (elect_one()) {
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k)  // +32 bytes per K step = +2 in the address field
-            umma_bf16_pair(d_tmem, adesc + uint64_t(2 * k), bdesc + uint64_t(2 * k), (kb | k) != 0 ? 1u : 0u);
-          umma_commit_pair(map_to_rank(empty_bar(stage), 0));
-          umma_commit_pair(map_to_rank(empty_bar(stage), 1));
+            for (int k = 0; k < BK / 16; ++k)  // +32 bytes per K step = +2 in the address field
+              umma_bf16_pair(d_tmem, adesc + uint64_t(2 * k), bdesc + uint64_t(2 * k), (kb | k) != 0 ? 1u : 0u);
+            umma_commit_pair(map_to_rank(empty_bar(stage), 0));
+            umma_commit_pair(map_to_rank(empty_bar(stage), 1));
+          }
+          __syncwarp();
           if (++stage == STAGES) stage = 0, phase ^= 1u;
         }
         if (!ok) break;
-        umma_commit_pair(map_to_rank(tfull_bar(buf), 0));
-        umma_commit_pair(map_to_rank(tfull_bar(buf), 1));
+        if (elect_one()) {
+          umma_commit_pair(map_to_rank(tfull_bar(buf), 0));
+          umma_commit_pair(map_to_rank(tfull_bar(buf), 1));
+        }
+        __syncwarp();
         if (++buf == 2) buf = 0, acc_phase ^= 1u;
       }
     }
+   }
   } else {
     // ---------------------------------------------------- epilogue
-    const int quad = warp & 3, hh = (warp - 2) >> 2;  // lane quadrant, head of the tile
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsEpi));
+    const int quad = warp & 3, hh = (warp - kEpiFirst) >> 2;  // lane quadrant, head of the tile
     const int rit = quad * 32 + lane;                 // row in the tile
     const float* my_cos = rope_cos_s + rit * ROPE_PITCH;
     const float* my_sin = rope_sin_s + rit * ROPE_PITCH;
     float* my_table = (hh == 0 ? rope_cos_s : rope_sin_s) + rit * ROPE_PITCH;
-    float* wc = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(warp_consts) + (warp - 2) * WARP_CONST_BYTES);
+    float* wc = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(warp_consts) + (warp - kEpiFirst) * WARP_CONST_BYTES);
     // wc: [bias 128][gain 128] f32
     const uint32_t pair_bar = 1 + quad;  // named barrier of the two warps of a quadrant
     int buf = 0;
@@ -683,6 +722,12 @@ cudaError_t launch_kv_project(const void* x, const void* wk, const void* wv, con
     if (it == pairs_of_device.end()) {
       e = cudaFuncSetAttribute(k_kv_project, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
       if (e != cudaSuccess) return e;
+      // the register split's increase waits for registers the launch must
+      // hold: refuse a build whose launch count differs from the split's
+      cudaFuncAttributes fa{};
+      e = cudaFuncGetAttributes(&fa, k_kv_project);
+      if (e != cudaSuccess) return e;
+      if (fa.numRegs != kRegsLaunch) return cudaErrorInvalidConfiguration;
       int sms = 0;
       e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
       if (e != cudaSuccess) return e;
