@@ -122,6 +122,13 @@ void ArchiveArena::reserve(size_t bytes) {
   chunks_.push_back({p, b, host});
 }
 
+bool ArchiveArena::is_host(const void* p) const {
+  const unsigned char* q = static_cast<const unsigned char*>(p);
+  for (const auto& c : chunks_)
+    if (q >= c.base && q < c.base + c.cap) return c.host;
+  return false;
+}
+
 void ArchiveArena::usage(size_t* device, size_t* host) const {
   *device = *host = 0;
   for (const auto& sl : stack_) (chunks_[sl.chunk].host ? *host : *device) += sl.size;
@@ -167,9 +174,9 @@ void Staging::begin(cudaStream_t main) {
   used_ = 0;
 }
 
-size_t Staging::add(const void* p, size_t bytes) {
+size_t Staging::add(const void* p, size_t bytes, size_t align) {
   Slot& sl = slot_[cur_];
-  size_t off = align_up(used_, 16);
+  size_t off = align_up(used_, align);
   if (off + bytes > sl.cap) {
     size_t cap = std::max<size_t>(align_up(off + bytes, 4096) * 2, 64 * 1024);
     unsigned char *h = nullptr, *d = nullptr;
@@ -1133,6 +1140,32 @@ void Bank::attend_history(int layer, const void* q, uint64_t q_len, float scale,
   if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(out)) & 15u)
     fail(NKV_ERR_ARGUMENT, "q and out must be 16-byte aligned");
   DeviceScope ds(device_);
+  // Codes come by TMA through one tensor map per (record, side) of this
+  // layer when every record of the working set is in device memory; a
+  // working set that reaches the pinned host tier is read with plain loads.
+  bool tma = true;
+  std::vector<size_t> recs;                // distinct records, in run order
+  std::vector<int> map_of(archive_.size(), -1);
+  for (const auto& rs : ws_runs_) {
+    if (map_of[rs.rec] >= 0) continue;
+    map_of[rs.rec] = int(recs.size());
+    recs.push_back(rs.rec);
+    if (arena_.is_host(archive_[rs.rec].slab)) tma = false;
+  }
+  std::vector<TmaDesc> maps;
+  if (tma) {
+    maps.resize(2 * recs.size());
+    for (size_t i = 0; i < recs.size() && tma; ++i) {
+      const Rec& r = archive_[recs[i]];
+      const unsigned char* lb = r.slab + size_t(layer) * r.layer_stride;
+      const uint64_t L = r.desc.image_tokens + r.desc.text_tokens;
+      tma = make_codes_map(&maps[2 * i], lb + r.off[0], L, int(H_)) &&
+            make_codes_map(&maps[2 * i + 1], lb + r.off[1], L, int(H_));
+    }
+  }
+  if (!d_attn_status_) NKV_CUDA(cudaMalloc(&d_attn_status_, sizeof(uint32_t)));
+  stg_.begin(stream_);
+  const size_t moff = tma ? stg_.add(maps.data(), maps.size() * sizeof(TmaDesc), 64) : 0;
   std::vector<AttnKeyTile> tiles;
   for (const auto& rs : ws_runs_) {
     const Rec& r = archive_[rs.rec];
@@ -1144,12 +1177,12 @@ void Bank::attend_history(int layer, const void* q, uint64_t q_len, float scale,
       t.v_codes = lb + r.off[1] + tok * H_ * D_;
       t.k_scales = reinterpret_cast<const float*>(lb + r.off[2]) + tok * H_;
       t.v_scales = reinterpret_cast<const float*>(lb + r.off[3]) + tok * H_;
+      t.map = map_of[rs.rec];
+      t.tok0 = int32_t(tok);
       t.ntok = int32_t(std::min<int64_t>(128, rs.ntok - t0));
       tiles.push_back(t);
     }
   }
-  if (!d_attn_status_) NKV_CUDA(cudaMalloc(&d_attn_status_, sizeof(uint32_t)));
-  stg_.begin(stream_);
   const size_t toff = stg_.add(tiles.data(), tiles.size() * sizeof(AttnKeyTile));
   stg_.upload(aux_, stream_);
   NKV_CUDA(cudaMemsetAsync(d_attn_status_, 0, sizeof(uint32_t), stream_));
@@ -1163,6 +1196,7 @@ void Bank::attend_history(int layer, const void* q, uint64_t q_len, float scale,
   a.out = out;
   a.lse = lse;
   a.status = d_attn_status_;
+  a.maps = tma ? static_cast<const TmaDesc*>(stg_.dev(moff)) : nullptr;
   tbegin(NKV_KERNEL_ATTEND);
   NKV_CUDA(launch_attend_int8(a, stream_));
   tend(NKV_KERNEL_ATTEND);

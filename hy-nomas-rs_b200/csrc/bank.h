@@ -59,6 +59,8 @@ class ArchiveArena {
   size_t device_limit() const { return device_limit_; }
   // bytes of the live slabs in device memory / in host memory
   void usage(size_t* device, size_t* host) const;
+  // whether `p` lies in a pinned host chunk
+  bool is_host(const void* p) const;
 
  private:
   struct Chunk {
@@ -90,7 +92,7 @@ class Staging {
   ~Staging();
   // next slot; `main` is the stream whose work consumes the tables
   void begin(cudaStream_t main);
-  size_t add(const void* p, size_t bytes);
+  size_t add(const void* p, size_t bytes, size_t align = 16);
   // the copy on `aux`, ordered before everything enqueued on `main` afterwards
   void upload(cudaStream_t aux, cudaStream_t main);
   const void* dev(size_t off) const { return slot_[cur_].dev + off; }

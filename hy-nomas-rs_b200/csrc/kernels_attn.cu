@@ -27,6 +27,8 @@
 //
 // Every wait on an mbarrier gives up after 1 s of %globaltimer: the CTA then
 // sets bit 0 of the caller's status word, frees its TMEM and returns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -47,15 +49,19 @@ constexpr int kSoftmaxWarps = 8, kDequantWarps = 4;
 constexpr int kMmaWarp = kSoftmaxWarps + kDequantWarps;
 constexpr int kAttnThreads = 512;
 // Registers per thread after the split (setmaxnreg, per warpgroup): the
-// launch gives 512 x 128; softmax 2 x 128 x 168 + dequantization 128 x 128
-// + MMA / idle 128 x 48 = 65,536, exactly the launch's total.
+// launch gives 512 x 128; softmax 256 x 168 + dequantization 128 x 128 + MMA /
+// idle 128 x 48 = 65,536, exactly the launch's total.
 constexpr int kRegsLaunch = 128, kRegsSoftmax = 168, kRegsDequant = 128, kRegsOther = 48;
-static_assert(kRegsSoftmax * 256 + kRegsDequant * 128 + kRegsOther * 128 <= kRegsLaunch * kAttnThreads,
+static_assert(kRegsSoftmax * 32 * kSoftmaxWarps + kRegsDequant * 32 * kDequantWarps + kRegsOther * 128 <=
+                  kRegsLaunch * kAttnThreads,
               "register split exceeds the launch's registers");
 constexpr int HALF_BYTES = 128 * 128;      // 128 rows x 64 bf16
 constexpr int TILE_BYTES = 2 * HALF_BYTES; // 32 KB
-// Q (two halves), K and V (two buffers each); barriers; alignment.
-constexpr int kAttnSmem = 6 * TILE_BYTES + 256 + 1024;
+// INT8 codes of one side of a key tile: 128 rows of 128 bytes.
+constexpr int CODE_BYTES = AK * AD;
+// Q (two halves), K and V (two buffers each), the K and V code stages of the
+// TMA path; barriers; alignment: 230,656 of the 232,448 bytes a CTA may have.
+constexpr int kAttnSmem = 6 * TILE_BYTES + 2 * CODE_BYTES + 256 + 1024;
 static_assert(kAttnSmem <= 232448, "shared memory");
 constexpr uint64_t kAttnWaitNs = 1000000000ull;
 
@@ -263,6 +269,20 @@ __device__ __forceinline__ void tmem_regs_after_wait(float* v) {
 }
 
 
+// One head's 128 consecutive tokens of a record's code plane (a 3-D tensor
+// map: bytes, head, token) into 16 KB of shared memory, 128-byte swizzled,
+// completing on `bar`.  The innermost coordinate is 0 (16-byte aligned).
+__device__ __forceinline__ void tma_codes(uint32_t dst, const TmaDesc* map, int h, int tok0, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(h), "r"(tok0), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void bar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
 __device__ __forceinline__ float max3(float a, float b, float c) {
   float d;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
@@ -293,6 +313,7 @@ __device__ __forceinline__ float fast_exp2(float x) {
 // O_1 [384, 512).  An MMA reads P_h from TMEM (the A operand) and V from
 // shared memory; MMAs run in issue order, so S_h(t+1) overwrites P_h(t) only
 // after PV_h(t) read it, and S_h(t+1) completing implies PV_h(t) completed.
+template <bool kTma>
 __global__ void __launch_bounds__(kAttnThreads, 1) k_attend_int8(const AttnArgs a) {
   extern __shared__ unsigned char attn_raw[];
   unsigned char* base =
@@ -300,10 +321,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attend_int8(const AttnArgs 
   unsigned char* Qs = base;                   // halves at 0 / TILE_BYTES
   unsigned char* Kb = base + 2 * TILE_BYTES;  // buffers at 0 / TILE_BYTES
   unsigned char* Vb = base + 4 * TILE_BYTES;  // buffers at 0 / TILE_BYTES
+  unsigned char* Cs = base + 6 * TILE_BYTES;  // TMA path: K codes, then V codes
   // barriers: 0-1 S full (half), 2-3 P full (half), 4-5 K full (buffer),
-  // 6-7 V full, 8-9 K empty, 10-11 V empty, 12 O done
-  uint64_t* bars = reinterpret_cast<uint64_t*>(base + 6 * TILE_BYTES);
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 16);
+  // 6-7 V full, 8-9 K empty, 10-11 V empty, 12 O done; TMA path: 13 / 14 K /
+  // V codes landed, 15 / 16 K / V codes read by every dequantization thread
+  uint64_t* bars = reinterpret_cast<uint64_t*>(Cs + 2 * CODE_BYTES);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 20);
   volatile uint32_t* abort_flag = tslot + 1;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int h = blockIdx.y, H = a.H;
@@ -326,6 +349,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attend_int8(const AttnArgs 
       asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(B(10 + i)) : "memory");
     }
     asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(B(12)) : "memory");
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(B(13)) : "memory");
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(B(14)) : "memory");
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(B(15)), "r"(32 * kDequantWarps) : "memory");
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(B(16)), "r"(32 * kDequantWarps) : "memory");
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     *abort_flag = 0u;
   }
@@ -416,6 +443,116 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attend_int8(const AttnArgs 
   } else if (warp >= kSoftmaxWarps) {
     // ---------------------------------------------------- dequantization
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsDequant));
+    if constexpr (kTma) {
+      // Thread j owns key row j of every tile.  One code stage per side:
+      // thread 0 brings the next tile's codes (one TMA box per side: one
+      // head's rows of 128 tokens) as soon as every thread has read the
+      // current ones; the next tile's scales are loaded a tile ahead, tile
+      // descriptors two tiles ahead.
+      const int kr = tid - 32 * kSoftmaxWarps;  // key row 0..127
+      const uint32_t kc_row = smem_addr(Cs) + uint32_t(kr) * 128u, vc_row = kc_row + uint32_t(CODE_BYTES);
+      const uint32_t rsw = uint32_t(kr & 7);
+      auto issue = [&](int side, const AttnKeyTile& T) {
+        bar_expect_tx(B(13 + side), uint32_t(CODE_BYTES));
+        tma_codes(smem_addr(Cs) + uint32_t(side * CODE_BYTES), a.maps + 2 * T.map + side, h, T.tok0, B(13 + side));
+      };
+      auto scales = [&](const AttnKeyTile& T, float& k, float& v) {
+        if (kr < T.ntok) {
+          k = __ldg(T.k_scales + int64_t(kr) * H + h);
+          v = __ldg(T.v_scales + int64_t(kr) * H + h);
+        }
+      };
+      // the rebuild's dequantization (int8.rs:139-155) of row kr of a code
+      // stage into a swizzled bf16 tile, zeros for rows past the tile's end
+      auto convert = [&](uint32_t src, float sc, bool hv, unsigned char* tile) {
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          uint4 lo = make_uint4(0u, 0u, 0u, 0u), hi = lo;
+          if (hv) {
+            uint4 w;
+            asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                         : "=r"(w.x), "=r"(w.y), "=r"(w.z), "=r"(w.w)
+                         : "r"(src + ((uint32_t(c) ^ rsw) << 4)));
+            lo = dequant8(make_uint2(w.x, w.y), sc);
+            hi = dequant8(make_uint2(w.z, w.w), sc);
+          }
+          *reinterpret_cast<uint4*>(tile + swz(kr, 2 * c)) = lo;
+          *reinterpret_cast<uint4*>(tile + swz(kr, 2 * c + 1)) = hi;
+        }
+        fence_async_smem();
+      };
+      int k_issued = 0, v_issued = 0;  // tiles whose K / V codes were requested (thread 0)
+      float ks = 0.0f, vs = 0.0f, ks1 = 0.0f, vs1 = 0.0f;
+      AttnKeyTile d1{};
+      int nt = 0;  // rows of tile t
+      if (n > 0) {
+        const AttnKeyTile d0 = a.tiles[0];
+        nt = d0.ntok;
+        if (tid == 32 * kSoftmaxWarps) {
+          issue(0, d0);
+          issue(1, d0);
+          k_issued = v_issued = 1;
+        }
+        scales(d0, ks, vs);
+      }
+      if (n > 1) {
+        d1 = a.tiles[1];
+        scales(d1, ks1, vs1);
+      }
+      int t = 0;
+      for (; t < n; ++t) {
+        const int b = t & 1;
+        const uint32_t ph = uint32_t(t) & 1u;
+        const uint32_t pe = uint32_t((t >> 1) - 1) & 1u;  // the buffer's previous use, tile t - 2
+        const bool hv = kr < nt;
+        AttnKeyTile d2{};
+        if (t + 2 < n) d2 = a.tiles[t + 2];
+        // K_t into buffer b once its codes landed and S of tile t - 2 completed
+        if (!bar_wait(B(13), ph) || (t >= 2 && !bar_wait(B(8 + b), pe))) {
+          fail();
+          break;
+        }
+        convert(kc_row, ks, hv, Kb + b * TILE_BYTES);
+        bar_arrive(B(4 + b));
+        bar_arrive(B(15));
+        if (tid == 32 * kSoftmaxWarps && t + 1 < n) {
+          if (!bar_wait(B(15), ph)) {
+            fail();
+            break;
+          }
+          issue(0, d1);
+          k_issued = t + 2;
+        }
+        // V_t once its codes landed and P V of tile t - 2 completed
+        if (!bar_wait(B(14), ph) || (t >= 2 && !bar_wait(B(10 + b), pe))) {
+          fail();
+          break;
+        }
+        convert(vc_row, vs, hv, Vb + b * TILE_BYTES);
+        bar_arrive(B(6 + b));
+        bar_arrive(B(16));
+        if (tid == 32 * kSoftmaxWarps && t + 1 < n) {
+          if (!bar_wait(B(16), ph)) {
+            fail();
+            break;
+          }
+          issue(1, d1);
+          v_issued = t + 2;
+        }
+        ks = ks1;
+        vs = vs1;
+        if (t + 2 < n) scales(d2, ks1, vs1);
+        nt = d1.ntok;
+        d1 = d2;
+        if (*abort_flag) break;
+      }
+      // no copy in flight when the CTA ends: on an early exit, wait (bounded)
+      // for the boxes requested but not consumed
+      if (tid == 32 * kSoftmaxWarps) {
+        for (int u = t; u < k_issued; ++u) bar_wait(B(13), uint32_t(u) & 1u);
+        for (int u = t; u < v_issued; ++u) bar_wait(B(14), uint32_t(u) & 1u);
+      }
+    } else {
     // Thread j owns key row j of every tile.  The K codes of tile t + 1 are
     // requested right after K_t is written and the V codes right after V_t,
     // so each load has the wait for the next buffer (about one tile of MMA
@@ -487,6 +624,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attend_int8(const AttnArgs 
       if (t + 1 < n) load_v(d1);
       d1 = d2;
       if (*abort_flag) break;
+    }
     }
   } else {
     // ------------------------------------------------------------ softmax
@@ -597,19 +735,46 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attend_int8(const AttnArgs 
   if (warp == kMmaWarp) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
 }
 
-cudaError_t launch_attend_int8(const AttnArgs& a, cudaStream_t s) {
-  if (a.Lq <= 0 || a.H <= 0 || a.n_tiles <= 0) return cudaSuccess;
-  cudaError_t e = cudaFuncSetAttribute(k_attend_int8, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem);
+static_assert(sizeof(CUtensorMap) == sizeof(TmaDesc) && alignof(CUtensorMap) <= alignof(TmaDesc), "TmaDesc");
+
+bool make_codes_map(TmaDesc* m, const void* base, uint64_t tokens, int H) {
+  static PFN_cuTensorMapEncodeTiled_v12000 enc = nullptr;
+  if (!enc) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return false;
+    enc = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  if (tokens == 0 || H <= 0 || (reinterpret_cast<uintptr_t>(base) & 15u)) return false;
+  const cuuint64_t dims[3] = {uint64_t(AD), uint64_t(H), tokens};
+  const cuuint64_t strides[2] = {uint64_t(AD), uint64_t(H) * AD};
+  const cuuint32_t box[3] = {uint32_t(AD), 1u, uint32_t(AK)};
+  const cuuint32_t estr[3] = {1u, 1u, 1u};
+  return enc(reinterpret_cast<CUtensorMap*>(m), CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims,
+             strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <bool kTma>
+static cudaError_t launch_attend(const AttnArgs& a, cudaStream_t s) {
+  cudaError_t e = cudaFuncSetAttribute(k_attend_int8<kTma>, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem);
   if (e != cudaSuccess) return e;
   // the register split's increase waits for registers the launch must hold:
   // refuse a build whose launch count differs from the split's
   cudaFuncAttributes fa{};
-  e = cudaFuncGetAttributes(&fa, k_attend_int8);
+  e = cudaFuncGetAttributes(&fa, k_attend_int8<kTma>);
   if (e != cudaSuccess) return e;
   if (fa.numRegs != kRegsLaunch) return cudaErrorInvalidConfiguration;
   dim3 grid(unsigned((a.Lq + kHalves * AQ - 1) / (kHalves * AQ)), unsigned(a.H));
-  k_attend_int8<<<grid, kAttnThreads, kAttnSmem, s>>>(a);
+  k_attend_int8<kTma><<<grid, kAttnThreads, kAttnSmem, s>>>(a);
   return cudaGetLastError();
+}
+
+cudaError_t launch_attend_int8(const AttnArgs& a, cudaStream_t s) {
+  if (a.Lq <= 0 || a.H <= 0 || a.n_tiles <= 0) return cudaSuccess;
+  return a.maps ? launch_attend<true>(a, s) : launch_attend<false>(a, s);
 }
 
 }  // namespace nkv

@@ -204,12 +204,25 @@ cudaError_t launch_flag_reduce(uint32_t* flags, int n, cudaStream_t s);
 // ------------------------------------------------- history attention ---
 // A tile of <= 128 consecutive history keys inside one archived INT8
 // segment: the addresses of its first token (head 0) in the archive.
+// An encoded TMA descriptor (a CUtensorMap), opaque here.
+struct alignas(64) TmaDesc {
+  unsigned char bytes[128];
+};
+// The INT8 code plane of one archived record and layer, (tokens, H, 128)
+// bytes at `base` (16-byte aligned, device memory), as a 3-D tensor map
+// whose box is one head's 128-byte rows of 128 consecutive tokens,
+// 128-byte swizzled; tokens past the end read as zeros.  False when the
+// driver's encoder is unavailable or refuses the shape.
+bool make_codes_map(TmaDesc* m, const void* base, uint64_t tokens, int H);
+
 struct AttnKeyTile {
-  const uint8_t* k_codes;
+  const uint8_t* k_codes;  // the tile's first row (register path)
   const uint8_t* v_codes;
-  const float* k_scales;
+  const float* k_scales;  // the tile's first row
   const float* v_scales;
+  int32_t tok0;  // the tile's first token in its record
   int32_t ntok;
+  int32_t map;  // TMA path: the record's K / V code planes are maps[2 map] / maps[2 map + 1]
   int32_t pad_;
 };
 // Attention of q (Lq, H, 128) bf16 over the history keys of `tiles`, head
@@ -225,6 +238,7 @@ struct AttnArgs {
   float* out;
   float* lse;
   uint32_t* status;
+  const TmaDesc* maps;  // non-null: codes by TMA through these maps (device-memory archives)
 };
 cudaError_t launch_attend_int8(const AttnArgs& a, cudaStream_t s);
 cudaError_t launch_kv_project(const void* x, const void* wk, const void* wv, const KvProjectParams& p,

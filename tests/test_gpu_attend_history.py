@@ -145,3 +145,23 @@ def test_attend_history_at_8b_geometry(H, orc):
     finally:
         p.close()
         orc.set_threads(1)
+
+
+def test_attend_history_with_host_tier_archive(H):
+    """Records in the pinned-host tier are read with plain loads, records in
+    device memory by TMA: the same result either way."""
+    import torch
+    import nomas_kv as nk
+    p = _pair(H)
+    try:
+        desc = nk._abi.nkv_segment_desc(0, 0, p.geo.frames, p.geo.frames * p.geo.tpf, p.geo.text, -1)
+        p.p.set_archive_device_limit(2 * p.p.segment_bytes(desc) * p.geo.n_layers)
+        for _ in range(6):
+            assert p.commit() is None
+        dev, host = p.p.archive_usage()
+        assert dev > 0 and host > 0, (dev, host)
+        q = torch.randn((200, 4, 128), device="cuda").to(torch.bfloat16)
+        for layer in range(2):
+            _check(H, p, layer, q)
+    finally:
+        p.close()
