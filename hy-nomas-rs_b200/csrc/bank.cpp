@@ -314,6 +314,7 @@ Bank::~Bank() {
   if (flag_ev_) cudaEventDestroy(flag_ev_);
   if (encoded_) cudaEventDestroy(encoded_);
   if (d_attn_status_) cudaFree(d_attn_status_);
+  if (d_attn_part_) cudaFree(d_attn_part_);
   for (auto p : p_host_)
     if (p) cudaFreeHost(p);
   stg_.release();
@@ -1196,6 +1197,17 @@ void Bank::attend_history(int layer, const void* q, uint64_t q_len, float scale,
   a.out = out;
   a.lse = lse;
   a.status = d_attn_status_;
+  if (!sms_) NKV_CUDA(cudaDeviceGetAttribute(&sms_, cudaDevAttrMultiProcessorCount, device_));
+  const int64_t part_rows = attend_plan(int64_t(q_len), int(H_), int(tiles.size()), sms_, &a);
+  if (part_rows > attn_part_rows_) {
+    if (d_attn_part_) NKV_CUDA(cudaFree(d_attn_part_));
+    d_attn_part_ = nullptr;
+    attn_part_rows_ = 0;
+    NKV_CUDA(cudaMalloc(&d_attn_part_, size_t(part_rows) * (128 + 2) * sizeof(float)));
+    attn_part_rows_ = part_rows;
+  }
+  a.part_o = d_attn_part_;
+  a.part_ml = d_attn_part_ ? d_attn_part_ + size_t(attn_part_rows_) * 128 : nullptr;
   a.maps = tma ? static_cast<const TmaDesc*>(stg_.dev(moff)) : nullptr;
   tbegin(NKV_KERNEL_ATTEND);
   NKV_CUDA(launch_attend_int8(a, stream_));

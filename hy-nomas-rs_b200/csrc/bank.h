@@ -235,6 +235,9 @@ class Bank {
   std::vector<RunSpec> ws_runs_;  // the runs the current working set was gathered from
   std::vector<RunSpec> p_runs_;   // ... of the parked one
   uint32_t* d_attn_status_ = nullptr;
+  float* d_attn_part_ = nullptr;  // split units' partial rows: 128 + 2 floats per row
+  int64_t attn_part_rows_ = 0;
+  int sms_ = 0;
   uint64_t valid_ = 0;
 
   bool parked_ = false;

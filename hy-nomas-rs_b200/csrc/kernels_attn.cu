@@ -31,6 +31,7 @@
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdint>
 
 #include "nkv_device.cuh"
@@ -329,9 +330,22 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attend_int8(const AttnArgs 
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 20);
   volatile uint32_t* abort_flag = tslot + 1;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int h = blockIdx.y, H = a.H;
-  const int64_t q0 = int64_t(blockIdx.x) * (kHalves * AQ);
-  const int n = a.n_tiles;
+  // The work item: units (256 queries, head), head-major, whole for the first
+  // a.full_units CTAs; the remaining units split into a.parts key ranges each
+  // (the last wave would otherwise hold only those units), whose partial
+  // results a combine kernel merges.
+  const int H = a.H;
+  int unit = int(blockIdx.x), part = -1, tb = 0, n = a.n_tiles;
+  if (unit >= a.full_units) {
+    const int j = unit - a.full_units;
+    unit = a.full_units + j / a.parts;
+    part = j % a.parts;
+    tb = int(int64_t(a.n_tiles) * part / a.parts);
+    n = int(int64_t(a.n_tiles) * (part + 1) / a.parts) - tb;
+  }
+  const int h = unit / a.q_tiles;
+  const int64_t q0 = int64_t(unit % a.q_tiles) * (kHalves * AQ);
+  const AttnKeyTile* tiles = a.tiles + tb;  // this CTA's key tiles
   auto B = [&](int i) { return smem_addr(&bars[i]); };
 
   if (warp == kMmaWarp) {
@@ -486,7 +500,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attend_int8(const AttnArgs 
       AttnKeyTile d1{};
       int nt = 0;  // rows of tile t
       if (n > 0) {
-        const AttnKeyTile d0 = a.tiles[0];
+        const AttnKeyTile d0 = tiles[0];
         nt = d0.ntok;
         if (tid == 32 * kSoftmaxWarps) {
           issue(0, d0);
@@ -496,7 +510,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attend_int8(const AttnArgs 
         scales(d0, ks, vs);
       }
       if (n > 1) {
-        d1 = a.tiles[1];
+        d1 = tiles[1];
         scales(d1, ks1, vs1);
       }
       int t = 0;
@@ -506,7 +520,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attend_int8(const AttnArgs 
         const uint32_t pe = uint32_t((t >> 1) - 1) & 1u;  // the buffer's previous use, tile t - 2
         const bool hv = kr < nt;
         AttnKeyTile d2{};
-        if (t + 2 < n) d2 = a.tiles[t + 2];
+        if (t + 2 < n) d2 = tiles[t + 2];
         // K_t into buffer b once its codes landed and S of tile t - 2 completed
         if (!bar_wait(B(13), ph) || (t >= 2 && !bar_wait(B(8 + b), pe))) {
           fail();
@@ -596,16 +610,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attend_int8(const AttnArgs 
     };
     AttnKeyTile d1{};  // descriptor of tile t + 1
     if (n > 0) {
-      const AttnKeyTile d0 = a.tiles[0];
+      const AttnKeyTile d0 = tiles[0];
       load_k(d0);
       load_v(d0);
     }
-    if (n > 1) d1 = a.tiles[1];
+    if (n > 1) d1 = tiles[1];
     for (int t = 0; t < n; ++t) {
       const int b = t & 1;
       const uint32_t pe = uint32_t((t >> 1) - 1) & 1u;  // the buffer's previous use, tile t - 2
       AttnKeyTile d2{};
-      if (t + 2 < n) d2 = a.tiles[t + 2];
+      if (t + 2 < n) d2 = tiles[t + 2];
       // K_t into buffer b once S of tile t - 2 completed
       if (t >= 2 && !bar_wait(B(8 + b), pe)) {
         fail();
@@ -636,7 +650,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attend_int8(const AttnArgs 
     const uint32_t o_cols = tmem + lane_q + uint32_t(256 + hf * 128);
     float m = -INFINITY, l = 0.0f;
     for (int t = 0; t < n; ++t) {
-      const int ntok = a.tiles[t].ntok;
+      const int ntok = tiles[t].ntok;
       if (!bar_wait(B(hf), uint32_t(t) & 1u)) {
         fail();
         break;
@@ -711,20 +725,28 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attend_int8(const AttnArgs 
       tc_after();
       if (ok) {
         const int64_t q = q0 + hf * AQ + row;
-        const float inv = 1.0f / l;
+        // a part writes its unnormalised rows, running maximum and sum (base 2)
+        const int64_t prow = int64_t((unit - a.full_units) * a.parts + part) * (kHalves * AQ) + hf * AQ + row;
+        const float inv = part < 0 ? 1.0f / l : 1.0f;
 #pragma unroll 1
         for (int ch = 0; ch < 4; ++ch) {
           float ov[32];
           tmem_load32(o_cols + ch * 32, ov);
           if (q < a.Lq) {
-            float4* out = reinterpret_cast<float4*>(a.out + (q * H + h) * AD + ch * 32);
+            float4* out = reinterpret_cast<float4*>((part < 0 ? a.out + (q * H + h) * AD : a.part_o + prow * AD) +
+                                                    ch * 32);
 #pragma unroll
             for (int d = 0; d < 8; ++d)
               out[d] =
                   make_float4(ov[4 * d] * inv, ov[4 * d + 1] * inv, ov[4 * d + 2] * inv, ov[4 * d + 3] * inv);
           }
         }
-        if (q < a.Lq) a.lse[int64_t(h) * a.Lq + q] = (m + log2f(l)) * 0.69314718055994531f;
+        if (q < a.Lq) {
+          if (part < 0)
+            a.lse[int64_t(h) * a.Lq + q] = (m + log2f(l)) * 0.69314718055994531f;
+          else
+            reinterpret_cast<float2*>(a.part_ml)[prow] = make_float2(m, l);
+        }
       }
     }
   }
@@ -757,6 +779,56 @@ bool make_codes_map(TmaDesc* m, const void* base, uint64_t tokens, int H) {
              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// The merge of a split unit's parts, one thread per query row: with M the
+// largest part maximum, O = sum_p 2^(m_p - M) O_p / sum_p 2^(m_p - M) l_p and
+// lse = (M + log2 of that sum) ln 2.
+__global__ void __launch_bounds__(kHalves * AQ) k_attend_combine(const AttnArgs a) {
+  const int unit = a.full_units + int(blockIdx.x), r = int(threadIdx.x);
+  const int h = unit / a.q_tiles;
+  const int64_t q = int64_t(unit % a.q_tiles) * (kHalves * AQ) + r;
+  if (q >= a.Lq) return;
+  const int64_t row0 = int64_t(blockIdx.x) * a.parts * (kHalves * AQ) + r;  // part p: + p * 256
+  const float2* ml = reinterpret_cast<const float2*>(a.part_ml);
+  float M = -INFINITY;
+  for (int p = 0; p < a.parts; ++p) M = fmaxf(M, ml[row0 + int64_t(p) * (kHalves * AQ)].x);
+  float L = 0.0f;
+  for (int p = 0; p < a.parts; ++p) {
+    const float2 v = ml[row0 + int64_t(p) * (kHalves * AQ)];
+    L += exp2f(v.x - M) * v.y;
+  }
+  const float inv = 1.0f / L;
+  float4* out = reinterpret_cast<float4*>(a.out + (q * a.H + h) * AD);
+  for (int d = 0; d < AD / 4; ++d) {
+    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    for (int p = 0; p < a.parts; ++p) {
+      const int64_t pr = row0 + int64_t(p) * (kHalves * AQ);
+      const float w = exp2f(ml[pr].x - M) * inv;
+      const float4 o = reinterpret_cast<const float4*>(a.part_o + pr * AD)[d];
+      acc.x += w * o.x;
+      acc.y += w * o.y;
+      acc.z += w * o.z;
+      acc.w += w * o.w;
+    }
+    out[d] = acc;
+  }
+  a.lse[int64_t(h) * a.Lq + q] = (M + log2f(L)) * 0.69314718055994531f;
+}
+
+int64_t attend_plan(int64_t q_len, int H, int n_tiles, int sms, AttnArgs* a) {
+  const int64_t q_tiles = (q_len + kHalves * AQ - 1) / (kHalves * AQ);
+  const int64_t units = q_tiles * H;
+  a->q_tiles = int32_t(q_tiles);
+  a->full_units = int32_t(units);
+  a->parts = 1;
+  const int64_t rem = sms > 0 ? units % sms : 0;
+  if (rem == 0) return 0;
+  const int64_t parts = std::min<int64_t>(sms / rem, n_tiles / 4);
+  if (parts < 2) return 0;
+  a->full_units = int32_t(units - rem);
+  a->parts = int32_t(parts);
+  return rem * parts * (kHalves * AQ);
+}
+
 template <bool kTma>
 static cudaError_t launch_attend(const AttnArgs& a, cudaStream_t s) {
   cudaError_t e = cudaFuncSetAttribute(k_attend_int8<kTma>, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem);
@@ -767,8 +839,12 @@ static cudaError_t launch_attend(const AttnArgs& a, cudaStream_t s) {
   e = cudaFuncGetAttributes(&fa, k_attend_int8<kTma>);
   if (e != cudaSuccess) return e;
   if (fa.numRegs != kRegsLaunch) return cudaErrorInvalidConfiguration;
-  dim3 grid(unsigned((a.Lq + kHalves * AQ - 1) / (kHalves * AQ)), unsigned(a.H));
-  k_attend_int8<kTma><<<grid, kAttnThreads, kAttnSmem, s>>>(a);
+  const int64_t units = int64_t(a.q_tiles) * a.H;
+  const int64_t split = units - a.full_units;
+  k_attend_int8<kTma><<<unsigned(a.full_units + split * a.parts), kAttnThreads, kAttnSmem, s>>>(a);
+  e = cudaGetLastError();
+  if (e != cudaSuccess || split == 0) return e;
+  k_attend_combine<<<unsigned(split), kHalves * AQ, 0, s>>>(a);
   return cudaGetLastError();
 }
 

@@ -239,7 +239,21 @@ struct AttnArgs {
   float* lse;
   uint32_t* status;
   const TmaDesc* maps;  // non-null: codes by TMA through these maps (device-memory archives)
+  // the schedule (attend_plan): units of (256 queries, head), head-major; the
+  // first full_units whole, the rest split into `parts` key ranges whose
+  // partial rows go to part_o (f32, 128 per row) and part_ml ((max, sum) per
+  // row, base 2), 256 rows per (unit, part)
+  int32_t q_tiles;
+  int32_t full_units;
+  int32_t parts;
+  float* part_o;
+  float* part_ml;
 };
+// The schedule for q_len queries x H heads over n_tiles key tiles on `sms`
+// SMs: units beyond the last whole wave are split into key ranges (at least
+// four tiles each) so that the last wave fills the GPU.  Returns the partial
+// rows the split needs (0: none).
+int64_t attend_plan(int64_t q_len, int H, int n_tiles, int sms, AttnArgs* a);
 cudaError_t launch_attend_int8(const AttnArgs& a, cudaStream_t s);
 cudaError_t launch_kv_project(const void* x, const void* wk, const void* wv, const KvProjectParams& p,
                               cudaStream_t stream);

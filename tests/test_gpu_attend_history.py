@@ -165,3 +165,18 @@ def test_attend_history_with_host_tier_archive(H):
             _check(H, p, layer, q)
     finally:
         p.close()
+
+
+def test_attend_history_whole_and_split_units(H):
+    """10,000 queries x 4 heads = 160 units of 256 queries: the first 148 run
+    whole, the last 12 are split into key ranges and merged."""
+    import torch
+    p = _pair(H)
+    try:
+        for _ in range(6):
+            assert p.commit() is None
+        gen = torch.Generator(device="cuda").manual_seed(5)
+        q = (2.0 * torch.randn((10000, 4, 128), generator=gen, device="cuda")).to(torch.bfloat16)
+        _check(H, p, 1, q)
+    finally:
+        p.close()
