@@ -16,8 +16,8 @@ semantics).  Layers are sharded contiguously across ranks (48/N each).
 Prints one JSON line (rank 0).  `value` is device-timed with inputs resident
 in HBM; `e2e` repeats the step with the K/V coming from pinned host memory
 inside the timed region.  The banks are ShardedKvBanks: every turn carries
-the per-turn NCCL broadcast of the 1 KB turn record and the status
-all-reduce.  After the INT8 headline the same run adds, in the same
+the per-turn NCCL broadcast of the 1 KB turn record, on a side stream
+while the commit runs.  After the INT8 headline the same run adds, in the same
 process, one park + unpark of the working set (phase swap, against the
 measured pinned copy bandwidth), a short QVG turn (config 3) and a short
 turn with the fused K/V producer against the unfused chain (`--no-extras`
@@ -115,10 +115,19 @@ class ClockSampler:
     BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
             "hw_power_brake_slowdown": 0x80}
 
-    def __init__(self, local_index: int):
+    def __init__(self, local_indices, interval: float = 0.2):
+        """Samples the GPUs of `local_indices` (device indices of this
+        process) from one thread every `interval` seconds, the first sample
+        when start() returns.  Each rank samples only its own GPU: NVML
+        queries of GPUs that other processes drive stalled those processes
+        (8 ranks: 1.16 ms per turn became 8.7 ms with rank 0 polling all eight
+        every 10 ms)."""
         vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
         ids = [x for x in vis.split(",") if x.strip().isdigit()]
-        self.gpu = int(ids[local_index]) if local_index < len(ids) else local_index
+        if isinstance(local_indices, int):
+            local_indices = [local_indices]
+        self.gpus = [int(ids[i]) if i < len(ids) else i for i in local_indices]
+        self.interval = interval
         self.samples: list[tuple[float, float, int]] = []
         self._stop = threading.Event()
         self._ready = threading.Event()  # first sample taken (or sampling failed)
@@ -129,15 +138,16 @@ class ClockSampler:
         try:
             import pynvml
             pynvml.nvmlInit()
-            h = pynvml.nvmlDeviceGetHandleByIndex(self.gpu)
-            smax = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+            hs = [pynvml.nvmlDeviceGetHandleByIndex(g) for g in self.gpus]
+            smax = [float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)) for h in hs]
             get_reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
                 pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
             while not self._stop.is_set():
-                sm = float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
-                self.samples.append((sm, smax, int(get_reasons(h))))
+                for h, mx in zip(hs, smax):
+                    sm = float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
+                    self.samples.append((sm, mx, int(get_reasons(h))))
                 self._ready.set()
-                time.sleep(0.005)
+                self._stop.wait(self.interval)
             pynvml.nvmlShutdown()
         except Exception as e:  # noqa: BLE001
             self.err = repr(e)
@@ -152,16 +162,20 @@ class ClockSampler:
         while not self._stop.is_set():
             try:
                 out = subprocess.run(["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits",
-                                      "-i", str(self.gpu)], capture_output=True, text=True, timeout=5).stdout
-                sm, smax, reasons = [x.strip() for x in out.strip().split(",")]
-                self.samples.append((float(sm), float(smax), int(reasons, 16)))
+                                      "-i", ",".join(str(g) for g in self.gpus)], capture_output=True, text=True,
+                                     timeout=5).stdout
+                for line in out.strip().splitlines():
+                    sm, smax, reasons = [x.strip() for x in line.split(",")]
+                    self.samples.append((float(sm), float(smax), int(reasons, 16)))
             except Exception as e:  # noqa: BLE001
                 self.err = f"{self.err}; nvidia-smi: {e!r}"
                 return
             self._ready.set()
-            time.sleep(0.02)
+            self._stop.wait(self.interval)
 
     def start(self):
+        if not self.gpus:
+            return
         self._t = threading.Thread(target=self._loop, daemon=True)
         self._t.start()
         self._ready.wait(timeout=5.0)  # so a short timed region still gets samples
@@ -170,11 +184,15 @@ class ClockSampler:
         self._stop.set()
         if self._t is not None:
             self._t.join(timeout=5)
+        if not self.gpus:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0, "gpus": 0,
+                    "what": "sampled by local rank 0"}
         if not self.samples:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [f"no samples: {self.err}"], "samples": 0}
         reasons = sorted({n for _, _, r in self.samples for n, b in self.BITS.items() if r & b})
         return {"sm_mhz": statistics.median(s for s, _, _ in self.samples),
-                "sm_max_mhz": max(m for _, m, _ in self.samples), "reasons": reasons, "samples": len(self.samples)}
+                "sm_max_mhz": max(m for _, m, _ in self.samples), "reasons": reasons, "samples": len(self.samples),
+                "gpus": len(self.gpus)}
 
 
 # ------------------------------------------------------------- CPU side
@@ -337,6 +355,23 @@ def _max_over_ranks(world: int, dev, values: list[float]) -> list[float]:
     return [float(x) for x in t.tolist()]
 
 
+def _gather_clocks(world: int, mine: dict) -> dict:
+    """Every rank's clock summary merged for rank 0's line (after the timed
+    region): the median of the ranks' medians, the largest maximum, the union
+    of the reasons."""
+    if world == 1:
+        return mine
+    import torch.distributed as dist
+    allc = [None] * world
+    dist.all_gather_object(allc, mine)
+    sm = [c["sm_mhz"] for c in allc if c.get("sm_mhz") is not None]
+    mx = [c["sm_max_mhz"] for c in allc if c.get("sm_max_mhz") is not None]
+    return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+            "reasons": sorted({r for c in allc for r in c.get("reasons", [])}),
+            "samples": sum(c.get("samples", 0) for c in allc), "gpus": world,
+            "per_rank_sm_mhz": [c.get("sm_mhz") for c in allc]}
+
+
 def _barrier(world: int) -> None:
     import torch
     import torch.distributed as dist
@@ -393,7 +428,8 @@ class Turns:
         storage = nk.CacheStorage.qvg_() if workload == "qvg" else nk.CacheStorage.int8()
         cfg = nk.CacheConfig(storage=storage, sampling=nk.HistorySampling.uniform(), past_frames=PAST,
                              phase_swap=phase_swap)
-        self.sb = ShardedKvBank(cfg, args.layers, 1, HEADS, HEAD_DIM, torch.bfloat16, device=dev, verify=True)
+        self.sb = ShardedKvBank(cfg, args.layers, 1, HEADS, HEAD_DIM, torch.bfloat16, device=dev,
+                                verify=getattr(args, "verify", "broadcast"))
         self.bank = self.sb.local
         self.begin, self.n_layers = self.sb.begin, self.sb.count
         self.stream = torch.cuda.current_stream(dev)
@@ -536,7 +572,9 @@ def run_gpu(args) -> None:
     torch.cuda.synchronize()
 
     # ---------------------------------------------------- timed: resident
-    clocks = ClockSampler(local)
+    # one GPU: 20 ms polling costs nothing measurable; several ranks: the
+    # recipe's 200 ms, each rank its own GPU
+    clocks = ClockSampler(local, 0.02 if world == 1 else 0.2)
     T.bank.kernel_stats(reset=True)
     T.bank.set_timing(True)
     _barrier(world)
@@ -550,7 +588,7 @@ def run_gpu(args) -> None:
     t1.record(stream)
     torch.cuda.synchronize()
     _barrier(world)
-    clk = clocks.stop()
+    clk = _gather_clocks(world, clocks.stop())
     T.bank.set_timing(False)
     kst = T.bank.kernel_stats(reset=True)
     ms_max = _max_over_ranks(world, dev, [t0.elapsed_time(t1)])[0]
@@ -695,7 +733,7 @@ def run_gpu(args) -> None:
                        "phase_swap": swap,
                        "working_set_tokens": rebuild_tokens(), "bytes_per_step": step_bytes(model_layers, wl, swap)["total"],
                        "parallelism": f"layer-sharded x{world} (ShardedKvBank: per-turn NCCL broadcast of the "
-                                      f"1 KB turn record + status all-reduce, no data-path collective)",
+                                      f"1 KB turn record on a side stream, no data-path collective)",
                        "l2": "inputs 3.8 GB per step > 126 MB L2"},
             "tokens_per_s": tok,
             "host_policy_latency": host_policy_latency(),
@@ -1048,6 +1086,8 @@ def main():
                     help="box-run configuration: phase-swapped cache, park + unpark every turn, 64-segment archive")
     ap.add_argument("--archive-device-gb", type=float, default=0.0,
                     help="tiered archive: keep at most this many GB of archive slabs in device memory (0: no limit)")
+    ap.add_argument("--verify", default="broadcast", choices=["broadcast", "strict", "off"],
+                    help="ShardedKvBank turn-record verification across ranks (N > 1)")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="model layers (48 = the 8B geometry; fewer only for small profiling cases)")
     args = ap.parse_args()

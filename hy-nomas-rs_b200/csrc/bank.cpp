@@ -274,7 +274,10 @@ Bank::Bank(const nkv_cache_config& cfg, int n_layers, int layer_begin, int64_t b
   }
   d_flag_ = d_flags_[0];
   NKV_CUDA(cudaHostAlloc(&h_flag_, sizeof(uint32_t) * (n_layers_ + 1), cudaHostAllocDefault));
-  NKV_CUDA(cudaEventCreateWithFlags(&flag_ev_, cudaEventDisableTiming));
+  // the commit's one host wait (its non-finite flags): the thread sleeps
+  // instead of spinning, which leaves the host cores to the other ranks'
+  // processes; the wake-up is hidden behind the gather queued before the wait
+  NKV_CUDA(cudaEventCreateWithFlags(&flag_ev_, cudaEventDisableTiming | cudaEventBlockingSync));
   NKV_CUDA(cudaEventCreateWithFlags(&encoded_, cudaEventDisableTiming));
   std::memset(h_flag_, 0, sizeof(uint32_t) * (n_layers_ + 1));
   if (cfg.storage == NKV_STORAGE_QVG) {

@@ -5,19 +5,29 @@ independent cache per DiT layer (cache/mod.rs:257-297).  Sharding therefore
 needs no data exchange: rank r owns the contiguous layer block
 ``partition_layers(n_layers, world, r)`` and every archive, working set and
 codebook of those layers stays in that GPU's HBM.  The only cross-rank
-traffic is host metadata, at most 1 KB per turn:
+traffic is host metadata, at most 1 KB per turn.  The turn record of a
+commit or rollback is rank 0's operation, segment descriptor, timeline
+length after the turn, and the frames the history sampler picks then, or the
+Recent-mode trim plan (cache/uniform_history.rs:76-125, cache/swa.rs:52-95);
+every rank evaluates the same samplers on its own state and compares.
 
-* the turn record (``verify=True``): before a commit or rollback, rank 0
-  broadcasts its record of the turn (operation, segment descriptor, the
-  timeline length after the turn, and the frames the history sampler picks
-  then, or the Recent-mode trim plan; cache/uniform_history.rs:76-125,
-  cache/swa.rs:52-95).  Every rank evaluates the same samplers on its own
-  state and compares, and one all-reduce of the comparisons lets every rank
-  take the same decision: when any rank disagrees no bank is touched and
-  every rank raises CacheState;
-* the status: every rank's outcome is all-reduced (MAX of the status code),
-  so when one rank fails every rank raises and no rank silently diverges in
-  what it reports;
+* ``verify="broadcast"`` (default): rank 0's record is broadcast on the
+  communication stream while the local commit runs, and compared in the
+  rank's next call (the next turn, park, unpark, metrics, ``check()`` or
+  close): one collective per turn, off the cache's stream, never waited for
+  inside the turn that posted it, so the ranks keep a turn of slack instead
+  of meeting at every turn's end.  A rank whose record of a turn differs
+  raises CacheState in its next call (its bank applied the turn); a rank
+  whose own operation fails raises its own error at once, and the
+  divergence stops it at the next turn (its own timeline check, or the
+  record comparison);
+* ``verify="strict"``: the records are compared before anything is touched,
+  one all-reduce of the comparisons lets every rank take the same decision
+  (when any rank disagrees no bank is touched and every rank raises
+  CacheState), and every rank's outcome is all-reduced (MAX of the status
+  code), so when one rank fails every rank raises.  Three collectives per
+  turn, each waited for on the host;
+* ``verify="off"``: no collectives.
 * ``metrics()`` reproduces KvBank::metrics (cache/mod.rs:305-319) over all
   layers of the model: MAX of archived_segments / rebuilds / evicted_tokens /
   rollbacks, SUM of the byte and encode counters.
@@ -59,7 +69,7 @@ def _fnv1a(values) -> int:
 
 class ShardedKvBank:
     def __init__(self, cfg: CacheConfig, n_layers: int, batch: int, heads: int, head_dim: int, dtype,
-                 group=None, bank_factory: Optional[Callable[[int, int], object]] = None, verify: bool = True,
+                 group=None, bank_factory: Optional[Callable[[int, int], object]] = None, verify="broadcast",
                  device: Optional[torch.device] = None):
         self.cfg = cfg
         self.group = group
@@ -68,14 +78,32 @@ class ShardedKvBank:
         self.world = dist.get_world_size(group) if self.distributed else 1
         self.n_layers = n_layers
         self.begin, self.count = partition_layers(n_layers, self.world, self.rank)
+        if verify is True:
+            verify = "strict"
+        elif verify is False or verify is None:
+            verify = "off"
+        if verify not in ("broadcast", "strict", "off"):
+            raise ValueError(f"verify must be 'broadcast', 'strict' or 'off', not {verify!r}")
         self.verify = verify
         nccl = self.distributed and dist.get_backend(group) == "nccl"
         self.comm_device = torch.device("cuda", torch.cuda.current_device()) if nccl else torch.device("cpu")
-        # high priority: the collectives' kernels are scheduled ahead of the
-        # rebuild gather's pending CTAs instead of after the whole grid
-        self.comm_stream = torch.cuda.Stream(self.comm_device, priority=-1) if nccl else None
+        # strict mode waits for its collectives inside the turn: high priority
+        # schedules their kernels ahead of the rebuild gather's pending CTAs.
+        # Broadcast mode checks a turn later, so its kernel runs at normal
+        # priority in the gaps of the cache's stream and never holds back the
+        # gather's CTAs while it waits for the other ranks
+        self.comm_stream = torch.cuda.Stream(self.comm_device, priority=-1 if verify == "strict" else 0) \
+            if nccl else None
         pin = nccl
         self._rec_host = torch.zeros(RECORD_WORDS, dtype=torch.int64, pin_memory=pin)
+        # broadcast mode: two slots, so turn t + 1 posts while turn t's
+        # broadcast is still unchecked
+        self._bc_in = [torch.zeros(RECORD_WORDS, dtype=torch.int64, pin_memory=pin) for _ in range(2)]
+        self._bc_out = [torch.zeros(RECORD_WORDS, dtype=torch.int64, pin_memory=pin) for _ in range(2)]
+        self._bc_dev = [torch.zeros(RECORD_WORDS, dtype=torch.int64, device=self.comm_device) for _ in range(2)]
+        self._bc_ev = [torch.cuda.Event(blocking=True) for _ in range(2)] if nccl else [None, None]
+        self._bc_slot = 0
+        self._bc_pending: Optional[tuple[int, list[int]]] = None  # (slot, this rank's record)
         self._rec_dev = torch.zeros(RECORD_WORDS, dtype=torch.int64, device=self.comm_device)
         self._st_host = torch.zeros(1, dtype=torch.int64, pin_memory=pin)
         self._st_dev = torch.zeros(1, dtype=torch.int64, device=self.comm_device)
@@ -153,6 +181,44 @@ class ShardedKvBank:
             return self._rec_host.tolist() == mine
         return self._collective(run)
 
+    def _post_record(self, mine: list[int]) -> None:
+        """Enqueue the broadcast of rank 0's turn record into the next slot (no
+        host wait on NCCL); the comparison is left pending."""
+        k = self._bc_slot
+        self._bc_slot ^= 1
+
+        def run():
+            self._bc_in[k].copy_(torch.tensor(mine, dtype=torch.int64))
+            buf = self._bc_in[k]
+            if self.comm_stream is not None:
+                self._bc_dev[k].copy_(self._bc_in[k], non_blocking=True)
+                buf = self._bc_dev[k]
+            dist.broadcast(buf, src=dist.get_global_rank(self.group, 0) if self.group else 0, group=self.group)
+            if self.comm_stream is not None:
+                self._bc_out[k].copy_(self._bc_dev[k], non_blocking=True)
+                self._bc_ev[k].record(self.comm_stream)
+            else:
+                self._bc_out[k].copy_(self._bc_in[k])
+        self._collective(run)
+        self._bc_pending = (k, mine)
+
+    def check(self) -> None:
+        """Compare the pending turn record with rank 0's (broadcast mode);
+        raises CacheState when they differ.  Every call of the bank does this
+        first; call it after the last turn to check that one."""
+        pending, self._bc_pending = self._bc_pending, None
+        self._check_one(pending)
+
+    def _check_one(self, pending) -> None:
+        if pending is None:
+            return
+        k, mine = pending
+        if self._bc_ev[k] is not None:
+            self._bc_ev[k].synchronize()
+        if self._bc_out[k].tolist() != mine:
+            raise CacheStateError("this rank's record of the last turn (segment descriptor or sampled history) "
+                                  "differs from rank 0's")
+
     def _any(self, flag: int) -> int:
         return self._status(flag)
 
@@ -171,7 +237,18 @@ class ShardedKvBank:
         """Check the turn record, run fn locally, make every rank raise if any
         rank failed."""
         err: Optional[NomasError] = None
-        if self.world > 1 and self.verify and op in (OP_COMMIT, OP_ROLLBACK):
+        if self.world > 1 and self.verify == "broadcast":
+            if op in (OP_COMMIT, OP_ROLLBACK):
+                # post this turn's broadcast first, so every rank's sequence of
+                # collectives stays the same even when the check below raises
+                prev, self._bc_pending = self._bc_pending, None
+                self._post_record(self._record(op, desc))
+                self._check_one(prev)  # the previous turn's record
+            else:
+                self.check()
+            fn()
+            return
+        if self.world > 1 and self.verify == "strict" and op in (OP_COMMIT, OP_ROLLBACK):
             same = self._check_record(self._record(op, desc))
             if self._any(0 if same else 1) != 0:
                 raise CacheStateError("ranks disagree on the turn record (segment descriptor or sampled history)")
@@ -181,7 +258,7 @@ class ShardedKvBank:
             except NomasError as e:
                 err = e
         code = err.code if err is not None else 0
-        c = self._status(code) if self.world > 1 else code
+        c = self._status(code) if self.world > 1 and self.verify == "strict" else code
         if err is None and c == 0:
             return
         if err is not None:
@@ -228,6 +305,8 @@ class ShardedKvBank:
         self._turn(0, self.local.unpark_all)
 
     def metrics(self) -> CacheMetrics:
+        if self.world > 1 and self.verify == "broadcast":
+            self.check()
         m = self.local.metrics()
         d = m.as_dict() if isinstance(m, CacheMetrics) else dict(m)
         if self.world == 1:
@@ -241,5 +320,9 @@ class ShardedKvBank:
         return CacheMetrics(**out)
 
     def close(self) -> None:
+        pending = self._bc_pending
+        self._bc_pending = None
+        if pending is not None and self._bc_ev[pending[0]] is not None:
+            self._bc_ev[pending[0]].synchronize()  # the broadcast's buffers outlive it
         if hasattr(self.local, "close"):
             self.local.close()

@@ -70,7 +70,7 @@ def _worker(rank, world, port, q):
         L = frames * tpf + text
         ocfg = orc.Config(storage=orc.INT8, sampling=orc.UNIFORM, past_frames=3)
         sb = ShardedKvBank(nk.CacheConfig(), n_layers, 1, H, D, 0,
-                           bank_factory=lambda b, c: OracleShard(orc, ocfg, b, c, H, D))
+                           bank_factory=lambda b, c: OracleShard(orc, ocfg, b, c, H, D), verify="strict")
         assert (sb.begin, sb.count) == nk.partition_layers(n_layers, world, rank)
         for s in range(3):
             desc = nk._abi.nkv_segment_desc(s, s * frames, frames, frames * tpf, text, -1)
@@ -124,6 +124,102 @@ def _worker(rank, world, port, q):
     except BaseException as e:  # noqa: BLE001
         import traceback
         q.put((rank, f"fail: {e!r}\n{traceback.format_exc()}"))
+
+
+def _worker_broadcast(rank, world, port, q):
+    """The default verification: one broadcast of rank 0's turn record per
+    commit / rollback, compared after the local turn; a disagreeing rank
+    raises by itself."""
+    try:
+        for p in (ROOT, os.path.join(ROOT, "oracle"), os.path.join(ROOT, "hy-nomas-rs_b200")):
+            sys.path.insert(0, p)
+        import torch.distributed as dist
+        from datetime import timedelta
+        import nomas_kv as nk
+        import oracle as orc
+        from nomas_kv.sharded import ShardedKvBank
+
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+        n_layers, H, D, tpf, frames, text = 4, 2, 16, 8, 2, 3
+        L = frames * tpf + text
+        ocfg = orc.Config(storage=orc.INT8, sampling=orc.UNIFORM, past_frames=3)
+        sb = ShardedKvBank(nk.CacheConfig(), n_layers, 1, H, D, 0,
+                           bank_factory=lambda b, c: OracleShard(orc, ocfg, b, c, H, D))
+        assert sb.verify == "broadcast"
+
+        def kv_of(s):
+            kv = [_inputs(0, sb.begin + i, s, L, H, D) for i in range(sb.count)]
+            return [k for k, _ in kv], [v for _, v in kv]
+
+        for s in range(3):
+            sb.commit(nk._abi.nkv_segment_desc(s, s * frames, frames, frames * tpf, text, -1), *kv_of(s))
+        full = orc.Bank(ocfg, n_layers, 1, H, D, orc.F32)
+        for s in range(3):
+            kv = [_inputs(0, l, s, L, H, D) for l in range(n_layers)]
+            full.commit(dict(segment_index=s, frame_start=s * frames, frame_count=frames, image_tokens=frames * tpf,
+                             text_tokens=text, action_start=-1), orc.F32, [k for k, _ in kv], [v for _, v in kv])
+        assert sb.metrics().as_dict() == full.metrics()
+        full.close()
+        # a descriptor that differs on rank 1: the turn is applied everywhere,
+        # and rank 1 (only) raises CacheState in its next call
+        bad = nk._abi.nkv_segment_desc(3, 6, frames, frames * tpf, text, -1 if rank == 0 else 0)
+        sb.commit(bad, *kv_of(3))
+        try:
+            sb.check()
+            assert rank == 0, "disagreement not detected"
+        except nk.CacheStateError:
+            assert rank == 1
+        sb.rollback()
+        sb.check()  # the rollback's records agree again
+        # a non-finite input on rank 1 only: rank 1 raises its own error at
+        # once, and the divergence (rank 1 archived nothing) stops rank 1 at
+        # the next turn (its own timeline check or the record comparison)
+        ks, vs = kv_of(3)
+        if rank == 1:
+            ks[0][0, 1, 0, 0] = np.nan
+        try:
+            sb.commit(nk._abi.nkv_segment_desc(3, 6, frames, frames * tpf, text, -1), ks, vs)
+            assert rank == 0, "failure not raised"
+        except nk.NomasError as e:
+            assert rank == 1 and e.code == nk.MsgError.code
+        try:
+            sb.commit(nk._abi.nkv_segment_desc(4, 8, frames, frames * tpf, text, -1), *kv_of(4))
+            sb.check()
+            assert rank == 0, "divergence not detected"
+        except nk.NomasError:
+            assert rank == 1
+        sb.close()
+        dist.destroy_process_group()
+        q.put((rank, "ok"))
+    except BaseException as e:  # noqa: BLE001
+        import traceback
+        q.put((rank, f"fail: {e!r}\n{traceback.format_exc()}"))
+
+
+def _run_two(target):
+    import socket
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=target, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = {}
+    for _ in procs:
+        r, msg = q.get(timeout=240)
+        results[r] = msg
+    for p in procs:
+        p.join(timeout=60)
+    return results
+
+
+def test_sharded_bank_broadcast_verification_two_gloo_ranks():
+    results = _run_two(_worker_broadcast)
+    assert results == {0: "ok", 1: "ok"}, results
 
 
 def test_sharded_bank_two_gloo_ranks():
