@@ -266,3 +266,27 @@ def test_sharded_bank_without_a_process_group_is_one_rank():
     assert sb._record(2)[7] == 4  # a rollback would leave 4 frames
     sb.close()
     full.close()
+
+
+def test_sharded_bank_verify_modes():
+    """verify accepts "broadcast" (the default), "strict" and "off", with True
+    / False as "strict" / "off"; anything else is refused."""
+    import pytest
+    import nomas_kv as nk
+    import oracle as orc
+    from nomas_kv.sharded import ShardedKvBank
+
+    ocfg = orc.Config(storage=orc.INT8, sampling=orc.UNIFORM, past_frames=3)
+
+    def make(**kw):
+        return ShardedKvBank(nk.CacheConfig(), 2, 1, 2, 16, 0,
+                             bank_factory=lambda b, c: OracleShard(orc, ocfg, b, c, 2, 16), **kw)
+
+    for kw, want in (({}, "broadcast"), ({"verify": True}, "strict"), ({"verify": False}, "off"),
+                     ({"verify": "strict"}, "strict"), ({"verify": "off"}, "off")):
+        sb = make(**kw)
+        assert sb.verify == want
+        sb.check()  # nothing pending: a no-op
+        sb.close()
+    with pytest.raises(ValueError, match="verify"):
+        make(verify="sometimes")
