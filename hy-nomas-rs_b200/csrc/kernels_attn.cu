@@ -20,10 +20,17 @@
 //
 // Shared-memory tiles are 128-byte-swizzled: a 128 x 128 bf16 tile is two
 // halves of 64 columns, each 16 rows-groups of 8 rows x 128 bytes (1024-byte
-// atoms) with the 16-byte chunk index XORed with the row in the atom.  Q, K
-// and P are K-major operands of that layout; V, stored the same way (key
-// rows, dims contiguous), is the MN-major operand of P V (its two halves are
-// the 64-dim blocks, LBO 16 KB apart; key groups of 8 rows, SBO 1024 bytes).
+// atoms) with the 16-byte chunk index XORed with the row in the atom.  Q and K
+// are K-major operands of that layout; V, stored the same way (key rows, dims
+// contiguous), is the MN-major operand of P V (its two halves are the 64-dim
+// blocks, LBO 16 KB apart; key groups of 8 rows, SBO 1024 bytes); P is read
+// from TMEM as the A operand of P V.
+//
+// The codes of a key tile come by TMA (one 3-D box per side from the
+// archived record's tensor map) when the archive is in device memory, and by
+// plain loads when it reaches the pinned host tier.  Units of (256 queries,
+// head) beyond the last whole wave are split into key ranges whose partial
+// rows k_attend_combine merges.
 //
 // Every wait on an mbarrier gives up after 1 s of %globaltimer: the CTA then
 // sets bit 0 of the caller's status word, frees its TMEM and returns.
