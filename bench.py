@@ -338,10 +338,16 @@ def _dist_setup(args):
     dev = torch.device("cuda", local)
     if world > 1:
         from datetime import timedelta
-        # high-priority NCCL streams: the per-turn collectives of the sharded
-        # bank must not queue behind the rebuild gather's CTAs
+        # The group carries only host metadata (the 1 KB turn record, timings,
+        # counters): one channel and no NVLS, so its kernels hold one SM while
+        # they wait for the other ranks.  High-priority NCCL streams only for
+        # the strict protocol, which waits for its collectives inside the
+        # turn; the default broadcast is checked a turn later and must not be
+        # dispatched ahead of the rebuild gather's CTAs.
+        os.environ.setdefault("NCCL_MAX_NCHANNELS", "1")
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
         opts = dist.ProcessGroupNCCL.Options()
-        opts.is_high_priority_stream = True
+        opts.is_high_priority_stream = getattr(args, "verify", "broadcast") == "strict"
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev, pg_options=opts)
     return world, rank, local, dev
 
